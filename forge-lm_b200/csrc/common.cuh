@@ -1,0 +1,61 @@
+// common.cuh — shared device helpers for libforge_b200 (sm_100a).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define FB2_DEV __device__ __forceinline__
+
+namespace fb2 {
+
+constexpr int kWarp = 32;
+constexpr float kLnEps = 1e-5f;  // LayerNorm eps (src/LLM.Core/Model/Layers.cs:106)
+
+FB2_DEV float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+FB2_DEV float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// tanh-approximation GELU with the reference constants
+// (src/LLM.Core/Tensor/CpuBackend.cs:25-26, 510-514).
+FB2_DEV float gelu_tanh(float v) {
+    // MathF.Sqrt(2f / MathF.PI) evaluated in float is 0x3f4c4229 (one ulp below
+    // the float nearest sqrt(2/pi), which the ILGPU kernel uses).
+    const float c = __uint_as_float(0x3f4c4229u);
+    const float coeff = 0.044715f;
+    float u = c * (v + coeff * v * v * v);
+    return 0.5f * v * (1.0f + tanhf(u));
+}
+
+// Order-preserving map float -> uint32 (larger float -> larger key).  NaN maps
+// to 0, the smallest key, the position Array.Sort<float> gives NaN.
+FB2_DEV uint32_t float_key(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return 0u;  // NaN
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+FB2_DEV float key_float(uint32_t k) {
+    uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+    return __uint_as_float(u);
+}
+
+// Loads that must observe data written earlier in the same kernel by other
+// CTAs: bypass L1 (which is not coherent across SMs).
+FB2_DEV float ld_cg(const float* p) { return __ldcg(p); }
+FB2_DEV float4 ld_cg4(const float4* p) { return __ldcg(p); }
+
+// Streaming read-only weight load: do not keep in L1.
+FB2_DEV float4 ld_stream4(const float4* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+}  // namespace fb2

@@ -1,0 +1,30 @@
+// expf_libm.cuh — device exponential that returns the host C runtime's expf
+// bit for bit.
+//
+// The reference sampler computes MathF.Exp (src/LLM.Core/Inference/Sampler.cs:57),
+// i.e. the C runtime's expf.  Here: the correctly rounded value
+// (float)exp((double)x), then a binary search in a build-time table of the
+// inputs where the host expf is not correctly rounded (gen_expf_fixups.c).
+#pragma once
+#include <stdint.h>
+
+#define FB2_EXPF_FIXUP_STORAGE __device__ const
+#include "generated/expf_fixups.inc"
+
+namespace fb2 {
+
+__device__ __forceinline__ float expf_libm(float x) {
+    float r = (float)exp((double)x);
+    uint32_t b = __float_as_uint(x);
+    uint32_t lo = 0, hi = FB2_EXPF_FIXUP_COUNT;
+    while (lo < hi) {
+        uint32_t mid = (lo + hi) >> 1;
+        uint32_t k = kExpfFixupData[2 * mid];
+        if (k < b) lo = mid + 1;
+        else hi = mid;
+    }
+    if (lo < FB2_EXPF_FIXUP_COUNT && kExpfFixupData[2 * lo] == b) r = __uint_as_float(kExpfFixupData[2 * lo + 1]);
+    return r;
+}
+
+}  // namespace fb2

@@ -1,0 +1,1472 @@
+// forge_b200.cu — runtime and C ABI of libforge_b200.so (sm_100a).
+//
+// Host-side structure:
+//   fb2_model   : per-device fp32 weight copies (one contiguous allocation).
+//   fb2_session : per-device DeviceSession (stream, KV cache, histories,
+//                 activation buffers, captured decode-step graph).
+// The token loop (Sampler.Generate, src/LLM.Core/Inference/Sampler.cs:78-109)
+// runs as: one prefill of every prompt window, then per step a CUDA-graph
+// replay of the KV-cached decode step for the slots whose window still fits
+// the context, a full re-prefill for the slots whose window slides
+// (Sampler.cs:93-94), and the on-device sampler for all slots.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/forge_b200.h"
+#include "dotnet_random.hpp"
+#include "kernels.cuh"
+#include "sampler.cuh"
+
+using namespace fb2;
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+namespace {
+thread_local std::string g_last_error;
+
+struct Fb2Error {
+    int status;
+    std::string msg;
+};
+
+[[noreturn]] void fail(int status, const std::string& msg) { throw Fb2Error{status, msg}; }
+
+void ck(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return;
+    if (e == cudaErrorMemoryAllocation) {
+        cudaGetLastError();
+        fail(FB2_OUT_OF_MEMORY, std::string(what) + ": " + cudaGetErrorString(e));
+    }
+    fail(FB2_CUDA_ERROR, std::string(what) + ": " + cudaGetErrorString(e));
+}
+#define CK(x) ck((x), #x)
+
+template <class F>
+int32_t guarded(F&& f) {
+    try {
+        f();
+        return FB2_OK;
+    } catch (const Fb2Error& e) {
+        g_last_error = e.msg;
+        return e.status;
+    } catch (const std::bad_alloc&) {
+        g_last_error = "host out of memory";
+        return FB2_OUT_OF_MEMORY;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return FB2_CUDA_ERROR;
+    }
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        CK(cudaSetDevice(dev));
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+template <class T>
+T* dalloc(size_t n) {
+    void* p = nullptr;
+    if (n == 0) n = 1;
+    CK(cudaMalloc(&p, n * sizeof(T)));
+    return static_cast<T*>(p);
+}
+template <class T>
+void dfree(T*& p) {
+    if (p) cudaFree(p);
+    p = nullptr;
+}
+
+inline int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
+
+constexpr int kMaxGemvRows = 16;
+constexpr int kMaxChunkSlots = 64;  // sequences per prefill chunk (head scratch rows)
+constexpr int kGemvMaxKChunk = 256;
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// model
+// ---------------------------------------------------------------------------
+struct LayerW {
+    const float *ln1_w, *ln1_b, *qkv_w, *qkv_b, *proj_w, *proj_b, *ln2_w, *ln2_b, *fc_w, *fc_b, *mproj_w, *mproj_b;
+};
+
+struct DeviceModel {
+    int device = 0;
+    int sm_count = 148;
+    float* blob = nullptr;
+    std::vector<const float*> p;
+    std::vector<LayerW> layers;
+    const float *tok_emb = nullptr, *pos_emb = nullptr, *lnf_w = nullptr, *lnf_b = nullptr;
+};
+
+struct fb2_model {
+    fb2_model_desc desc{};
+    int V = 0, ctx = 0, D = 0, L = 0, H = 0, hd = 0, F = 0;
+    std::vector<DeviceModel> devs;
+};
+
+static std::vector<long long> param_numels(const fb2_model_desc& d) {
+    long long D = d.d_model, F = 4LL * d.d_model;
+    std::vector<long long> n;
+    n.push_back((long long)d.vocab_size * D);
+    n.push_back((long long)d.context_length * D);
+    for (int l = 0; l < d.n_layers; l++) {
+        long long b[12] = {D, D, D * 3 * D, 3 * D, D * D, D, D, D, D * F, F, F * D, D};
+        n.insert(n.end(), b, b + 12);
+    }
+    n.push_back(D);
+    n.push_back(D);
+    return n;
+}
+
+// ---------------------------------------------------------------------------
+// kernel launch configuration (per device, set once)
+// ---------------------------------------------------------------------------
+static void configure_kernels() {
+    auto setmax = [](const void* f, int bytes) {
+        CK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    };
+    setmax((const void*)k_gemv<1>, 227 * 1024);
+    setmax((const void*)k_gemv<2>, 227 * 1024);
+    setmax((const void*)k_gemv<4>, 227 * 1024);
+    setmax((const void*)k_gemv<8>, 227 * 1024);
+    setmax((const void*)k_gemv<16>, 227 * 1024);
+    setmax((const void*)k_attn_prefill<4>, 227 * 1024);
+    setmax((const void*)k_attn_prefill<8>, 227 * 1024);
+    setmax((const void*)k_attn_prefill<16>, 227 * 1024);
+    setmax((const void*)k_attn_prefill<32>, 227 * 1024);
+    setmax((const void*)k_attn_prefill<64>, 227 * 1024);
+    setmax((const void*)k_attn_prefill<128>, 227 * 1024);
+    setmax((const void*)k_head<1>, 227 * 1024);
+    setmax((const void*)k_head<2>, 227 * 1024);
+    setmax((const void*)k_head<4>, 227 * 1024);
+    setmax((const void*)k_head<8>, 227 * 1024);
+    setmax((const void*)k_head<16>, 227 * 1024);
+    setmax((const void*)k_sample_step, 227 * 1024);
+    setmax((const void*)k_sample_rows, 227 * 1024);
+}
+
+// ---------------------------------------------------------------------------
+// session
+// ---------------------------------------------------------------------------
+struct ChunkPlan {
+    int row_off;      // first entry in the row table
+    int rows;         // rows in this chunk
+    int qblk_off, nqblk;
+    int slot_off, nslots;  // entries in last_row / out_slot tables
+};
+
+struct DeviceSession {
+    fb2_model* model = nullptr;
+    const DeviceModel* dm = nullptr;
+    int device = 0;
+    int slot0 = 0, nslots = 0;  // global slot range
+    cudaStream_t own_stream = nullptr, stream = nullptr;
+
+    // per-slot state
+    int *d_len = nullptr, *d_count = nullptr, *d_done = nullptr, *d_hist = nullptr;
+    int hist_cap = 0;
+    float* d_kv = nullptr;
+    long long kv_slot_stride = 0, kv_layer_stride = 0, v_offset = 0;
+
+    // rows
+    int row_cap = 0;
+    int *d_row_seq = nullptr, *d_row_pos = nullptr, *d_row_hidx = nullptr, *d_row_active = nullptr;
+    int* d_ones = nullptr;
+    float *d_x = nullptr, *d_x2 = nullptr, *d_ln = nullptr, *d_q = nullptr, *d_att = nullptr, *d_h = nullptr;
+    float *d_logits = nullptr, *d_lnf = nullptr;
+    float* d_attn_part = nullptr;
+    int attn_nsplit = 0;
+    float* d_gemv_part = nullptr;
+    size_t gemv_part_cap = 0;
+    unsigned int* d_tickets = nullptr;
+
+    // call tables (uploaded once per call)
+    int* d_tab = nullptr;
+    size_t tab_cap = 0;  // ints
+    int* h_tab = nullptr;  // pinned staging
+    size_t h_tab_cap = 0;
+    cudaEvent_t tab_event = nullptr;
+    bool tab_event_pending = false;
+    double* d_uni = nullptr;
+    size_t uni_cap = 0;
+    int* d_out = nullptr;
+    size_t out_cap = 0;
+
+    // decode graph
+    cudaGraphExec_t graph = nullptr;
+    int graph_n = -1;
+    long long graph_kernels = 0;  // kernel nodes in the captured step
+    cudaStream_t graph_stream = nullptr;
+
+    std::vector<DotNetRandom> rngs;  // FB2_RNG_SESSION streams of this device's slots
+
+    // stats
+    fb2_stats_t stats{};
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+};
+
+struct fb2_session {
+    fb2_model* model = nullptr;
+    int max_seqs = 0;
+    std::vector<DeviceSession*> ds;
+};
+
+static void session_free(DeviceSession* s) {
+    if (!s) return;
+    cudaSetDevice(s->device);
+    if (s->graph) cudaGraphExecDestroy(s->graph);
+    dfree(s->d_len); dfree(s->d_count); dfree(s->d_done); dfree(s->d_hist); dfree(s->d_kv);
+    dfree(s->d_row_seq); dfree(s->d_row_pos); dfree(s->d_row_hidx); dfree(s->d_row_active); dfree(s->d_ones);
+    dfree(s->d_x); dfree(s->d_x2); dfree(s->d_ln); dfree(s->d_q); dfree(s->d_att); dfree(s->d_h);
+    dfree(s->d_logits); dfree(s->d_lnf); dfree(s->d_attn_part); dfree(s->d_gemv_part); dfree(s->d_tickets);
+    dfree(s->d_tab); dfree(s->d_uni); dfree(s->d_out);
+    if (s->h_tab) cudaFreeHost(s->h_tab);
+    if (s->tab_event) cudaEventDestroy(s->tab_event);
+    if (s->ev0) cudaEventDestroy(s->ev0);
+    if (s->ev1) cudaEventDestroy(s->ev1);
+    if (s->own_stream) cudaStreamDestroy(s->own_stream);
+    delete s;
+}
+
+// ---------------------------------------------------------------------------
+// launch helpers
+// ---------------------------------------------------------------------------
+static void launch_layernorm(DeviceSession& s, int rows, const float* x, const float* w, const float* b, float* y,
+                             const int* row_map) {
+    int D = s.model->D;
+    int per = ceil_div(D, 32);
+    dim3 grid(ceil_div(rows, 8)), block(256);
+#define LN_CASE(P) \
+    if (per <= P) { s.stats.kernel_launches++; k_layernorm<P><<<grid, block, 0, s.stream>>>(rows, D, x, w, b, y, row_map); return; }
+    LN_CASE(1) LN_CASE(2) LN_CASE(4) LN_CASE(8) LN_CASE(16) LN_CASE(24) LN_CASE(32) LN_CASE(48) LN_CASE(64)
+#undef LN_CASE
+    fail(FB2_UNSUPPORTED, "d_model too large for the LayerNorm kernel");
+}
+
+template <int MR>
+static void launch_gemv_mr(DeviceSession& s, int M, int K, int N, const float* A, const float* W, const Epi& e) {
+    int nblk = ceil_div(N, 64);
+    int target = 2 * s.dm->sm_count;
+    int S = std::max(1, ceil_div(target, nblk));
+    S = std::min(S, std::max(1, K / 16));
+    int kchunk = ceil_div(ceil_div(K, S), 16) * 16;
+    if (kchunk > kGemvMaxKChunk) kchunk = kGemvMaxKChunk;
+    S = ceil_div(K, kchunk);
+    size_t need = (size_t)S * M * N;
+    if (S > 1 && need > s.gemv_part_cap) fail(FB2_UNSUPPORTED, "split-K scratch too small");
+    size_t smem = (size_t)MR * kchunk * 4 + (size_t)16 * MR * 64 * 4;
+    s.stats.kernel_launches++; k_gemv<MR><<<dim3(nblk, S), 256, smem, s.stream>>>(M, K, N, kchunk, A, W, s.d_gemv_part, s.d_tickets, e);
+}
+
+// y = A * W (+ epilogue) for M rows.
+static void launch_linear(DeviceSession& s, int M, int K, int N, const float* A, const float* W, Epi e) {
+    if (M <= kMaxGemvRows) {
+        if (M <= 1) launch_gemv_mr<1>(s, M, K, N, A, W, e);
+        else if (M <= 2) launch_gemv_mr<2>(s, M, K, N, A, W, e);
+        else if (M <= 4) launch_gemv_mr<4>(s, M, K, N, A, W, e);
+        else if (M <= 8) launch_gemv_mr<8>(s, M, K, N, A, W, e);
+        else launch_gemv_mr<16>(s, M, K, N, A, W, e);
+        return;
+    }
+    if (M <= 64) {
+        // decode batches of up to 64 rows: stream W once per 16 rows
+        for (int m0 = 0; m0 < M; m0 += kMaxGemvRows) {
+            int mm = std::min(kMaxGemvRows, M - m0);
+            Epi e2 = e;
+            const float* A2 = A + (size_t)m0 * K;
+            if (e.kind == EPI_QKV) {
+                e2.out = e.out + (size_t)m0 * e.D;
+                e2.R.seq = e.R.seq + m0; e2.R.pos = e.R.pos + m0; e2.R.active = e.R.active + m0;
+                if (e.R.hidx) e2.R.hidx = e.R.hidx + m0;
+            } else {
+                e2.out = e.out + (size_t)m0 * N;
+                if (e.resid) e2.resid = e.resid + (size_t)m0 * N;
+            }
+            if (mm <= 8) launch_gemv_mr<8>(s, mm, K, N, A2, W, e2);
+            else launch_gemv_mr<16>(s, mm, K, N, A2, W, e2);
+        }
+        return;
+    }
+    if (M <= 1024) {
+        dim3 grid(ceil_div(N, 128), ceil_div(M, 64));
+        s.stats.kernel_launches++; k_gemm_tiled<64><<<grid, 256, 0, s.stream>>>(M, K, N, A, W, e);
+    } else {
+        dim3 grid(ceil_div(N, 128), ceil_div(M, 128));
+        s.stats.kernel_launches++; k_gemm_tiled<128><<<grid, 256, 0, s.stream>>>(M, K, N, A, W, e);
+    }
+}
+
+static Epi make_epi(int kind, const float* bias, const float* resid, float* out) {
+    Epi e{};
+    e.kind = kind;
+    e.bias = bias;
+    e.resid = resid;
+    e.out = out;
+    return e;
+}
+
+template <int HD>
+static void launch_attn_decode_hd(DeviceSession& s, int M, int layer, Rows R) {
+    const fb2_model& m = *s.model;
+    float scale = 1.0f / sqrtf((float)m.hd);  // Layers.cs:174
+    const float* kvl = s.d_kv + (size_t)layer * s.kv_layer_stride;
+    s.stats.kernel_launches++; k_attn_decode_partial<HD><<<dim3(M, m.H, s.attn_nsplit), 128, 0, s.stream>>>(
+        s.d_q, kvl, s.kv_slot_stride, s.v_offset, m.H, m.ctx, scale, R, s.d_attn_part, s.attn_nsplit);
+    s.stats.kernel_launches++; k_attn_decode_combine<HD><<<dim3(M, m.H), 64, 0, s.stream>>>(s.d_attn_part, m.H, s.attn_nsplit, R, s.d_att);
+}
+
+static void launch_attn_decode(DeviceSession& s, int M, int layer, Rows R) {
+    switch (s.model->hd) {
+    case 4: launch_attn_decode_hd<4>(s, M, layer, R); break;
+    case 8: launch_attn_decode_hd<8>(s, M, layer, R); break;
+    case 16: launch_attn_decode_hd<16>(s, M, layer, R); break;
+    case 32: launch_attn_decode_hd<32>(s, M, layer, R); break;
+    case 64: launch_attn_decode_hd<64>(s, M, layer, R); break;
+    case 128: launch_attn_decode_hd<128>(s, M, layer, R); break;
+    default: fail(FB2_UNSUPPORTED, "head_dim must be a power of two in [4, 128]");
+    }
+}
+
+template <int HD>
+static void launch_attn_prefill_hd(DeviceSession& s, int nblk, const int4* qblk, int layer) {
+    const fb2_model& m = *s.model;
+    float scale = 1.0f / sqrtf((float)m.hd);
+    const float* kvl = s.d_kv + (size_t)layer * s.kv_layer_stride;
+    size_t smem = (size_t)(64 * (HD + 1) * 2 + 64 * HD + 64 * 65) * 4;
+    s.stats.kernel_launches++; k_attn_prefill<HD><<<dim3(nblk, m.H), 256, smem, s.stream>>>(s.d_q, kvl, s.kv_slot_stride, s.v_offset, m.H,
+                                                                 m.ctx, scale, qblk, s.d_att);
+}
+
+static void launch_attn_prefill(DeviceSession& s, int nblk, const int4* qblk, int layer) {
+    switch (s.model->hd) {
+    case 4: launch_attn_prefill_hd<4>(s, nblk, qblk, layer); break;
+    case 8: launch_attn_prefill_hd<8>(s, nblk, qblk, layer); break;
+    case 16: launch_attn_prefill_hd<16>(s, nblk, qblk, layer); break;
+    case 32: launch_attn_prefill_hd<32>(s, nblk, qblk, layer); break;
+    case 64: launch_attn_prefill_hd<64>(s, nblk, qblk, layer); break;
+    case 128: launch_attn_prefill_hd<128>(s, nblk, qblk, layer); break;
+    default: fail(FB2_UNSUPPORTED, "head_dim must be a power of two in [4, 128]");
+    }
+}
+
+static void launch_head(DeviceSession& s, int M, const float* xln, const int* out_slot_host_unused,
+                        float* logits_base) {
+    (void)out_slot_host_unused;
+    const fb2_model& m = *s.model;
+    int blocks = std::min(ceil_div(m.V, 8), 8 * s.dm->sm_count);
+    for (int m0 = 0; m0 < M; m0 += kMaxGemvRows) {
+        int mm = std::min(kMaxGemvRows, M - m0);
+        const float* x = xln + (size_t)m0 * m.D;
+        float* out = logits_base + (size_t)m0 * m.V;
+        size_t smem;
+#define HEAD_CASE(R)                                                                               \
+    if (mm <= R) {                                                                                 \
+        smem = (size_t)R * m.D * 4;                                                                \
+        s.stats.kernel_launches++; k_head<R><<<blocks, 256, smem, s.stream>>>(mm, m.D, m.V, x, s.dm->tok_emb, out, m.V);      \
+        continue;                                                                                  \
+    }
+        HEAD_CASE(1) HEAD_CASE(2) HEAD_CASE(4) HEAD_CASE(8) HEAD_CASE(16)
+#undef HEAD_CASE
+    }
+}
+
+// All transformer blocks (TransformerBlock.Forward, Layers.cs:384-392) over
+// rows 0..M-1 of d_x.  decode: single-row attention over the cache;
+// otherwise causal prefill attention over the query blocks.
+static void run_layers(DeviceSession& s, int M, Rows R, bool decode, int nqblk, const int4* qblk) {
+    const fb2_model& m = *s.model;
+    for (int l = 0; l < m.L; l++) {
+        const LayerW& w = s.dm->layers[l];
+        launch_layernorm(s, M, s.d_x, w.ln1_w, w.ln1_b, s.d_ln, nullptr);
+        Epi eq = make_epi(EPI_QKV, w.qkv_b, nullptr, s.d_q);
+        eq.kv_layer = s.d_kv + (size_t)l * s.kv_layer_stride;
+        eq.kv_slot_stride = s.kv_slot_stride;
+        eq.v_offset = s.v_offset;
+        eq.D = m.D;
+        eq.hd = m.hd;
+        eq.ctx = m.ctx;
+        eq.R = R;
+        launch_linear(s, M, m.D, 3 * m.D, s.d_ln, w.qkv_w, eq);
+        if (decode) launch_attn_decode(s, M, l, R);
+        else launch_attn_prefill(s, nqblk, qblk, l);
+        launch_linear(s, M, m.D, m.D, s.d_att, w.proj_w, make_epi(EPI_RESID, w.proj_b, s.d_x, s.d_x2));
+        launch_layernorm(s, M, s.d_x2, w.ln2_w, w.ln2_b, s.d_ln, nullptr);
+        launch_linear(s, M, m.D, m.F, s.d_ln, w.fc_w, make_epi(EPI_GELU, w.fc_b, nullptr, s.d_h));
+        launch_linear(s, M, m.F, m.D, s.d_h, w.mproj_w, make_epi(EPI_RESID, w.mproj_b, s.d_x2, s.d_x));
+    }
+}
+
+// One KV-cached decode step for slots 0..n-1 (graph-captured).
+static void enqueue_decode_step(DeviceSession& s, int n) {
+    const fb2_model& m = *s.model;
+    s.stats.kernel_launches++; k_step_prepare<<<ceil_div(n, 128), 128, 0, s.stream>>>(n, s.d_len, s.d_done, m.ctx, s.d_row_seq, s.d_row_pos,
+                                                          s.d_row_hidx, s.d_row_active);
+    Rows R{s.d_row_seq, s.d_row_pos, s.d_row_hidx, s.d_row_active};
+    s.stats.kernel_launches++; k_embed<<<n, 128, 0, s.stream>>>(n, R, s.d_hist, s.hist_cap, s.dm->tok_emb, s.dm->pos_emb, m.D, m.V, s.d_x);
+    run_layers(s, n, R, true, 0, nullptr);
+    launch_layernorm(s, n, s.d_x, s.dm->lnf_w, s.dm->lnf_b, s.d_lnf, nullptr);
+    launch_head(s, n, s.d_lnf, nullptr, s.d_logits);
+}
+
+static void run_decode_step(DeviceSession& s, int n) {
+    if (s.graph && (s.graph_n != n)) {
+        cudaGraphExecDestroy(s.graph);
+        s.graph = nullptr;
+    }
+    if (!s.graph) {
+        cudaGraph_t g = nullptr;
+        const long long before = s.stats.kernel_launches;
+        CK(cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeThreadLocal));
+        try {
+            enqueue_decode_step(s, n);
+            s.graph_kernels = s.stats.kernel_launches - before;
+            s.stats.kernel_launches = before;
+        } catch (...) {
+            cudaStreamEndCapture(s.stream, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+        }
+        CK(cudaStreamEndCapture(s.stream, &g));
+        cudaError_t e = cudaGraphInstantiate(&s.graph, g, 0);
+        cudaGraphDestroy(g);
+        CK(e);
+        s.graph_n = n;
+    }
+    CK(cudaGraphLaunch(s.graph, s.stream));
+    s.stats.kernel_launches += s.graph_kernels;
+    s.stats.decode_steps++;
+}
+
+// Prefill of one chunk: rows described by the uploaded tables.
+// tab layout per chunk: row_seq[rows], row_pos[rows], qblk (int4) [nqblk],
+// last_row[nslots], out_slot[nslots].
+struct PrefillTables {
+    const int* row_seq;
+    const int* row_pos;
+    const int4* qblk;
+    const int* last_row;
+    const int* out_slot;
+};
+
+__global__ void k_gather_logits_rows(int n, const int* out_slot, const float* src, float* dst, int V) {
+    // src rows are chunk-compact; dst rows are session slots
+    int r = blockIdx.y;
+    if (r >= n) return;
+    const float* a = src + (size_t)r * V;
+    float* b = dst + (size_t)out_slot[r] * V;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) b[i] = a[i];
+}
+
+__global__ void k_prefill_hidx(int rows, const int* row_seq, const int* row_pos, const int* len, int ctx, int* hidx) {
+    int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    int L = len[row_seq[r]];
+    int w = L < ctx ? L : ctx;
+    hidx[r] = L - w + row_pos[r];
+}
+
+static void run_prefill_chunk(DeviceSession& s, const ChunkPlan& c, const int* d_tab_base) {
+    const fb2_model& m = *s.model;
+    const int* row_seq = d_tab_base + c.row_off;
+    const int* row_pos = row_seq + c.rows;
+    const int4* qblk = reinterpret_cast<const int4*>(d_tab_base + c.qblk_off);
+    const int* last_row = d_tab_base + c.slot_off;
+    const int* out_slot = last_row + c.nslots;
+    s.stats.kernel_launches++; k_prefill_hidx<<<ceil_div(c.rows, 256), 256, 0, s.stream>>>(c.rows, row_seq, row_pos, s.d_len, m.ctx,
+                                                               s.d_row_hidx);
+    Rows R{row_seq, row_pos, s.d_row_hidx, s.d_ones};
+    s.stats.kernel_launches++; k_embed<<<c.rows, 128, 0, s.stream>>>(c.rows, R, s.d_hist, s.hist_cap, s.dm->tok_emb, s.dm->pos_emb, m.D, m.V,
+                                          s.d_x);
+    run_layers(s, c.rows, R, false, c.nqblk, qblk);
+    launch_layernorm(s, c.nslots, s.d_x, s.dm->lnf_w, s.dm->lnf_b, s.d_lnf, last_row);
+    // head into the chunk-compact area after the slots' logits, then scatter
+    float* tmp = s.d_logits + (size_t)s.nslots * m.V;
+    launch_head(s, c.nslots, s.d_lnf, nullptr, tmp);
+    s.stats.kernel_launches++; k_gather_logits_rows<<<dim3(std::min(ceil_div(m.V, 256), 64), c.nslots), 256, 0, s.stream>>>(c.nslots, out_slot,
+                                                                                              tmp, s.d_logits, m.V);
+    s.stats.prefill_rows += c.rows;
+}
+
+// Builds prefill chunk tables for slots `order` with window lengths `wl`
+// (slot-local indices), appending to `tab` and `plans`.
+static void plan_prefill(const DeviceSession& s, const std::vector<int>& order, const std::vector<int>& wl,
+                         std::vector<int>& tab, std::vector<ChunkPlan>& plans) {
+    size_t i = 0;
+    while (i < order.size()) {
+        size_t j = i;
+        int rows = 0;
+        while (j < order.size() && j - i < (size_t)kMaxChunkSlots && (rows + wl[order[j]] <= s.row_cap || j == i))
+            rows += wl[order[j++]];
+        if (rows > s.row_cap) fail(FB2_UNSUPPORTED, "window longer than the session's row capacity");
+        ChunkPlan c{};
+        c.rows = rows;
+        c.nslots = (int)(j - i);
+        c.row_off = (int)tab.size();
+        std::vector<int> seq, pos;
+        std::vector<int> q;
+        std::vector<int> last, slot;
+        int r = 0;
+        for (size_t k = i; k < j; k++) {
+            int sl = order[k], w = wl[sl];
+            for (int p = 0; p < w; p++) {
+                seq.push_back(sl);
+                pos.push_back(p);
+            }
+            for (int p0 = 0; p0 < w; p0 += 64) {
+                int cnt = std::min(64, w - p0);
+                q.push_back(r + p0);
+                q.push_back(cnt);
+                q.push_back(sl);
+                q.push_back(p0);
+            }
+            last.push_back(r + w - 1);
+            slot.push_back(sl);
+            r += w;
+        }
+        tab.insert(tab.end(), seq.begin(), seq.end());
+        tab.insert(tab.end(), pos.begin(), pos.end());
+        while (tab.size() % 4) tab.push_back(0);  // int4 alignment
+        c.qblk_off = (int)tab.size();
+        c.nqblk = (int)(q.size() / 4);
+        tab.insert(tab.end(), q.begin(), q.end());
+        c.slot_off = (int)tab.size();
+        tab.insert(tab.end(), last.begin(), last.end());
+        tab.insert(tab.end(), slot.begin(), slot.end());
+        while (tab.size() % 4) tab.push_back(0);
+        plans.push_back(c);
+        i = j;
+    }
+}
+
+static void ensure_capacity(DeviceSession& s, int hist_cap_needed, size_t uni_needed, size_t out_needed) {
+    DeviceGuard g(s.device);
+    if (hist_cap_needed > s.hist_cap) {
+        CK(cudaStreamSynchronize(s.stream));
+        dfree(s.d_hist);
+        s.hist_cap = std::max(hist_cap_needed, s.model->ctx + 64);
+        s.d_hist = dalloc<int>((size_t)s.nslots * s.hist_cap);
+        CK(cudaMemset(s.d_hist, 0, (size_t)s.nslots * s.hist_cap * sizeof(int)));
+        if (s.graph) {  // the captured step embeds the history pointer and stride
+            cudaGraphExecDestroy(s.graph);
+            s.graph = nullptr;
+        }
+    }
+    if (uni_needed > s.uni_cap) {
+        CK(cudaStreamSynchronize(s.stream));
+        dfree(s.d_uni);
+        s.uni_cap = uni_needed;
+        s.d_uni = dalloc<double>(s.uni_cap);
+    }
+    if (out_needed > s.out_cap) {
+        CK(cudaStreamSynchronize(s.stream));
+        dfree(s.d_out);
+        s.out_cap = out_needed;
+        s.d_out = dalloc<int>(s.out_cap);
+    }
+}
+
+// Uploads `tab` (ints) + optional doubles through the pinned staging buffer.
+static void upload_tables(DeviceSession& s, const std::vector<int>& tab, const std::vector<double>* uni) {
+    size_t nint = tab.size();
+    size_t nuni = uni ? uni->size() : 0;
+    size_t bytes = nint * 4 + 16 + nuni * 8;
+    if (s.tab_event_pending) {
+        CK(cudaEventSynchronize(s.tab_event));
+        s.tab_event_pending = false;
+    }
+    if (bytes > s.h_tab_cap) {
+        if (s.h_tab) cudaFreeHost(s.h_tab);
+        s.h_tab = nullptr;
+        s.h_tab_cap = std::max(bytes, (size_t)1 << 16);
+        CK(cudaMallocHost((void**)&s.h_tab, s.h_tab_cap));
+    }
+    if (nint > s.tab_cap) {
+        CK(cudaStreamSynchronize(s.stream));
+        dfree(s.d_tab);
+        s.tab_cap = std::max(nint, (size_t)1024);
+        s.d_tab = dalloc<int>(s.tab_cap);
+    }
+    if (nint) {
+        memcpy(s.h_tab, tab.data(), nint * 4);
+        CK(cudaMemcpyAsync(s.d_tab, s.h_tab, nint * 4, cudaMemcpyHostToDevice, s.stream));
+    }
+    if (nuni) {
+        char* hu = reinterpret_cast<char*>(s.h_tab) + ((nint * 4 + 15) / 16) * 16;
+        memcpy(hu, uni->data(), nuni * 8);
+        CK(cudaMemcpyAsync(s.d_uni, hu, nuni * 8, cudaMemcpyHostToDevice, s.stream));
+    }
+    CK(cudaEventRecord(s.tab_event, s.stream));
+    s.tab_event_pending = true;
+}
+
+__global__ void k_init_slots(int n, const int* __restrict__ plens_eff, const int* __restrict__ poff,
+                             const int* __restrict__ ptok, int* hist, int hist_stride, int* len, int* count, int* done,
+                             int max_new) {
+    int sidx = blockIdx.x;
+    if (sidx >= n) return;
+    int w = plens_eff[sidx];
+    const int* src = ptok + poff[sidx];
+    for (int i = threadIdx.x; i < w; i += blockDim.x) hist[(size_t)sidx * hist_stride + i] = src[i];
+    if (threadIdx.x == 0) {
+        len[sidx] = w;
+        count[sidx] = 0;
+        done[sidx] = max_new <= 0;
+    }
+}
+
+// Device-pointer variant of the slot init: prompt tokens and lengths already
+// on the device; keeps the last min(len, ctx) tokens of each prompt.
+__global__ void k_init_slots_device(int n, const int* __restrict__ plens, const int* __restrict__ ptok, int ctx,
+                                    int* hist, int hist_stride, int* len, int* count, int* done, int max_new) {
+    int sidx = blockIdx.x;
+    if (sidx >= n) return;
+    long long off = 0;
+    for (int i = 0; i < sidx; i++) off += plens[i];
+    int pl = plens[sidx];
+    int w = pl < ctx ? pl : ctx;
+    const int* src = ptok + off + (pl - w);
+    for (int i = threadIdx.x; i < w; i += blockDim.x) hist[(size_t)sidx * hist_stride + i] = src[i];
+    if (threadIdx.x == 0) {
+        len[sidx] = w;
+        count[sidx] = 0;
+        done[sidx] = max_new <= 0;
+    }
+}
+
+__global__ void k_copy_counts(int n, const int* count, int* out) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = count[i];
+}
+
+static SampleParams to_params(const fb2_sampling& sp) {
+    SampleParams p;
+    p.temperature = sp.temperature;
+    p.top_k = sp.top_k;
+    p.penalty = sp.repetition_penalty;
+    p.ngram = sp.no_repeat_ngram;
+    p.eos = sp.eos_id;
+    p.max_new = sp.max_new_tokens;
+    return p;
+}
+
+static void validate_sampling(const fb2_model& m, const fb2_sampling* sp) {
+    if (!sp) fail(FB2_INVALID_ARG, "sampling options are NULL");
+    if (!std::isfinite(sp->temperature)) fail(FB2_INVALID_ARG, "Temperature must be finite.");
+    if (sp->max_new_tokens < 0) fail(FB2_INVALID_ARG, "maxNewTokens must be >= 0.");
+    if (sp->eos_id >= m.V) fail(FB2_INVALID_ARG, "EOS token must be inside the model vocabulary.");
+    if (!std::isfinite(sp->repetition_penalty) || sp->repetition_penalty < 1.0f)
+        fail(FB2_INVALID_ARG, "Repetition penalty must be finite and >= 1.");
+    if (sp->no_repeat_ngram < 0) fail(FB2_INVALID_ARG, "No-repeat n-gram size must be >= 0.");
+}
+
+// ---------------------------------------------------------------------------
+// The token loop for one device's share of the sequences.
+// ---------------------------------------------------------------------------
+struct ShardJob {
+    int first;  // first global sequence index of this shard
+    int n;      // sequences on this device
+    const int* prompt_tokens;     // host, this shard's first prompt
+    const int* prompt_lens;       // host
+    const int* dev_prompt_tokens; // device variant
+    const int* dev_prompt_lens;
+    const fb2_sampling* sp;
+    int rng_mode;
+    const int32_t* seeds;
+    const double* uniforms;       // host [n_total * max_new] or device
+    bool device_io;
+    int* out_tokens;              // host [n * max_new] or device
+    int* out_counts;              // host [n] or device
+    fb2_token_cb cb;
+    void* user;
+    std::mutex* cb_mutex;
+    std::atomic<int>* stop;
+};
+
+static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
+    DeviceGuard guard(s.device);
+    const fb2_model& m = *s.model;
+    const fb2_sampling& sp = *job.sp;
+    const int n = job.n, ctx = m.ctx, max_new = sp.max_new_tokens;
+    if (n == 0) return;
+    ensure_capacity(s, ctx + max_new + 1, (size_t)n * std::max(max_new, 1), (size_t)n * std::max(max_new, 1));
+    const bool sampled = sp.temperature > 0.0f;
+
+    // host-side plan: effective window lengths and when each slot starts sliding
+    std::vector<int> wl0(n), plen(n);
+    std::vector<long long> poff(n);
+    long long off = 0;
+    for (int i = 0; i < n; i++) {
+        plen[i] = job.prompt_lens[i];
+        wl0[i] = std::min(plen[i], ctx);
+        poff[i] = off;
+        off += plen[i];
+    }
+    // slot i re-prefills at every step >= slide_at[i] (window before
+    // truncation = plen + step > ctx, Sampler.cs:93-94)
+    std::vector<int> slide_at(n);
+    for (int i = 0; i < n; i++) slide_at[i] = std::max(1, ctx - wl0[i] + 1);
+    std::vector<int> order(n);
+    for (int i = 0; i < n; i++) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return slide_at[a] < slide_at[b]; });
+
+    std::vector<int> tab;
+    std::vector<ChunkPlan> init_plans, slide_plans_all;
+    std::vector<int> all(n);
+    for (int i = 0; i < n; i++) all[i] = i;
+    plan_prefill(s, all, wl0, tab, init_plans);
+    // sliding re-prefill: every window is ctx rows; plan chunks over prefixes
+    // of `order` (the set that slides only grows with the step).
+    std::vector<int> wctx(n, ctx);
+    // plan per prefix length lazily: prefixes change at most n times
+    std::vector<int> prefix_sizes;
+    for (int k = 1; k <= n; k++)
+        if (k == n || slide_at[order[k]] != slide_at[order[k - 1]]) prefix_sizes.push_back(k);
+    std::vector<std::vector<ChunkPlan>> slide_plans(prefix_sizes.size());
+    int first_slide = slide_at[order[0]];
+    if (max_new > first_slide) {
+        for (size_t pi = 0; pi < prefix_sizes.size(); pi++) {
+            int k = prefix_sizes[pi];
+            if (slide_at[order[k - 1]] >= max_new) break;
+            std::vector<int> sub(order.begin(), order.begin() + k);
+            plan_prefill(s, sub, wctx, tab, slide_plans[pi]);
+        }
+    }
+    // prompts: device variant copies on device; host variant appends to tab
+    int ptok_off = 0, pl_off = 0, poff_off = 0;
+    if (!job.device_io) {
+        while (tab.size() % 4) tab.push_back(0);
+        ptok_off = (int)tab.size();
+        for (int i = 0; i < n; i++) {
+            const int* p = job.prompt_tokens + poff[i] + (plen[i] - wl0[i]);
+            tab.insert(tab.end(), p, p + wl0[i]);
+        }
+        pl_off = (int)tab.size();
+        tab.insert(tab.end(), wl0.begin(), wl0.end());
+        poff_off = (int)tab.size();
+        int acc = 0;
+        for (int i = 0; i < n; i++) {
+            tab.push_back(acc);
+            acc += wl0[i];
+        }
+    }
+    // uniforms
+    std::vector<double> uni;
+    const double* d_uni = nullptr;
+    if (sampled && max_new > 0) {
+        if (job.rng_mode == FB2_RNG_UNIFORMS) {
+            if (job.device_io) d_uni = job.uniforms;
+            else uni.assign(job.uniforms, job.uniforms + (size_t)n * max_new);
+        } else {
+            uni.resize((size_t)n * max_new);
+            for (int i = 0; i < n; i++) {
+                DotNetRandom r = (job.rng_mode == FB2_RNG_SEEDS) ? DotNetRandom(job.seeds[job.first + i])
+                                                                  : s.rngs[i];
+                for (int k = 0; k < max_new; k++) uni[(size_t)i * max_new + k] = r.next_double();
+            }
+        }
+        if (!d_uni) d_uni = s.d_uni;
+    }
+    upload_tables(s, tab, uni.empty() ? nullptr : &uni);
+    CK(cudaEventRecord(s.ev0, s.stream));
+
+    int* d_out = job.device_io ? job.out_tokens : s.d_out;
+    if (job.device_io) {
+        s.stats.kernel_launches++; k_init_slots_device<<<n, 256, 0, s.stream>>>(n, job.dev_prompt_lens, job.dev_prompt_tokens, ctx, s.d_hist,
+                                                     s.hist_cap, s.d_len, s.d_count, s.d_done, max_new);
+    } else {
+        s.stats.kernel_launches++; k_init_slots<<<n, 256, 0, s.stream>>>(n, s.d_tab + pl_off, s.d_tab + poff_off, s.d_tab + ptok_off, s.d_hist,
+                                              s.hist_cap, s.d_len, s.d_count, s.d_done, max_new);
+    }
+    CK(cudaGetLastError());
+    SampleParams P = to_params(sp);
+    size_t ssmem = sampler_smem_bytes(m.V);
+    auto sample_all = [&]() {
+        s.stats.kernel_launches++; k_sample_step<<<n, kSampleThreads, ssmem, s.stream>>>(n, s.d_logits, m.V, ctx, s.d_hist, s.hist_cap, s.d_len,
+                                                              s.d_count, s.d_done, d_uni, max_new, P, d_out, max_new);
+    };
+    std::vector<int> h_tok, h_cnt, prev_cnt(n, 0);
+    auto stream_callbacks = [&](int step) -> bool {
+        // returns true when generation should stop
+        CK(cudaStreamSynchronize(s.stream));
+        h_cnt.resize(n);
+        CK(cudaMemcpy(h_cnt.data(), s.d_count, n * sizeof(int), cudaMemcpyDeviceToHost));
+        h_tok.resize((size_t)n * max_new);
+        CK(cudaMemcpy(h_tok.data(), d_out, (size_t)n * max_new * sizeof(int), cudaMemcpyDeviceToHost));
+        bool any_active = false;
+        for (int i = 0; i < n; i++) {
+            for (int k = prev_cnt[i]; k < h_cnt[i]; k++) {
+                int rc;
+                {
+                    std::lock_guard<std::mutex> lk(*job.cb_mutex);
+                    rc = job.cb(job.user, job.first + i, step, h_tok[(size_t)i * max_new + k]);
+                }
+                if (rc != 0) job.stop->store(1);
+            }
+            prev_cnt[i] = h_cnt[i];
+            bool eos_hit = sp.eos_id >= 0 && h_cnt[i] > 0 && h_tok[(size_t)i * max_new + h_cnt[i] - 1] == sp.eos_id;
+            if (!eos_hit && h_cnt[i] < max_new) any_active = true;
+        }
+        return job.stop->load() != 0 || !any_active;
+    };
+
+    if (max_new > 0) {
+        for (const ChunkPlan& c : init_plans) run_prefill_chunk(s, c, s.d_tab);
+        sample_all();
+        CK(cudaGetLastError());
+        bool stop = job.cb ? stream_callbacks(0) : false;
+        for (int step = 1; step < max_new && !stop; step++) {
+            // slots with slide_at <= step re-prefill; the rest decode
+            int k = 0;
+            while (k < n && slide_at[order[k]] <= step) k++;
+            if (k < n) run_decode_step(s, n);
+            if (k > 0) {
+                size_t pi = 0;
+                while (prefix_sizes[pi] < k) pi++;
+                for (const ChunkPlan& c : slide_plans[pi]) run_prefill_chunk(s, c, s.d_tab);
+                s.stats.reprefills += k;
+            }
+            sample_all();
+            if (job.cb) stop = stream_callbacks(step);
+            else if (sp.eos_id >= 0 && (step % 64) == 0) {
+                // all slots finished? (cheap poll, keeps the pipeline mostly full)
+                std::vector<int> hd(n);
+                CK(cudaMemcpyAsync(hd.data(), s.d_done, n * sizeof(int), cudaMemcpyDeviceToHost, s.stream));
+                CK(cudaStreamSynchronize(s.stream));
+                bool all_done = true;
+                for (int i = 0; i < n; i++) all_done = all_done && hd[i];
+                if (all_done) break;
+            }
+        }
+    }
+    CK(cudaGetLastError());
+    CK(cudaEventRecord(s.ev1, s.stream));
+    if (job.device_io) {
+        s.stats.kernel_launches++; k_copy_counts<<<ceil_div(n, 128), 128, 0, s.stream>>>(n, s.d_count, job.out_counts);
+        CK(cudaGetLastError());
+        return;
+    }
+    // results back to the host
+    std::vector<int> counts(n);
+    CK(cudaMemcpyAsync(counts.data(), s.d_count, n * sizeof(int), cudaMemcpyDeviceToHost, s.stream));
+    if (max_new > 0)
+        CK(cudaMemcpyAsync(job.out_tokens, d_out, (size_t)n * max_new * sizeof(int), cudaMemcpyDeviceToHost, s.stream));
+    CK(cudaStreamSynchronize(s.stream));
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, s.ev0, s.ev1) == cudaSuccess) s.stats.decode_ms += ms;
+    for (int i = 0; i < n; i++) {
+        job.out_counts[i] = counts[i];
+        s.stats.tokens_generated += counts[i];
+        if (job.rng_mode == FB2_RNG_SESSION && sampled)
+            for (int k = 0; k < counts[i]; k++) s.rngs[i].next_double();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" {
+
+int32_t fb2_version(void) { return FB2_ABI_VERSION; }
+
+const char* fb2_last_error(void) { return g_last_error.c_str(); }
+
+int32_t fb2_device_count(int32_t* n) {
+    return guarded([&] {
+        if (!n) fail(FB2_INVALID_ARG, "n is NULL");
+        int c = 0;
+        cudaError_t e = cudaGetDeviceCount(&c);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            c = 0;
+        }
+        *n = c;
+    });
+}
+
+int32_t fb2_model_create(const fb2_model_desc* desc, const float* const* params, int32_t n_params,
+                         const int32_t* devices, int32_t n_devices, fb2_model** out) {
+    return guarded([&] {
+        if (!desc || !params || !out) fail(FB2_INVALID_ARG, "NULL argument");
+        *out = nullptr;
+        const fb2_model_desc& d = *desc;
+        if (d.vocab_size <= 0 || d.context_length <= 0 || d.d_model <= 0 || d.n_layers <= 0 || d.n_heads <= 0)
+            fail(FB2_INVALID_ARG, "model sizes must be positive");
+        if (d.d_model % d.n_heads != 0) fail(FB2_INVALID_ARG, "DModel must be divisible by NHeads.");
+        int hd = d.d_model / d.n_heads;
+        if (hd < 4 || hd > 128 || (hd & (hd - 1))) fail(FB2_UNSUPPORTED, "head_dim must be a power of two in [4, 128]");
+        if (d.d_model % 4 != 0 || d.d_model > 2048) fail(FB2_UNSUPPORTED, "d_model must be a multiple of 4, <= 2048");
+        if (sampler_smem_bytes(d.vocab_size) > 227 * 1024)
+            fail(FB2_UNSUPPORTED, "vocabulary too large for the on-chip sampler");
+        if (d.weight_dtype != FB2_WEIGHTS_FP32) fail(FB2_UNSUPPORTED, "only fp32 weights in this build");
+        if (n_params != 4 + 12 * d.n_layers) fail(FB2_INVALID_ARG, "n_params must be 4 + 12*n_layers");
+        for (int i = 0; i < n_params; i++)
+            if (!params[i]) fail(FB2_INVALID_ARG, "parameter pointer is NULL");
+        int ndev = 0;
+        if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+            cudaGetLastError();
+            fail(FB2_NO_DEVICE, "no CUDA device available");
+        }
+        std::vector<int> devs;
+        if (!devices || n_devices <= 0) devs.push_back(0);
+        else devs.assign(devices, devices + n_devices);
+        auto m = new fb2_model();
+        try {
+            m->desc = d;
+            m->V = d.vocab_size; m->ctx = d.context_length; m->D = d.d_model; m->L = d.n_layers;
+            m->H = d.n_heads; m->hd = hd; m->F = 4 * d.d_model;
+            std::vector<long long> numel = param_numels(d);
+            std::vector<size_t> offs;
+            size_t total = 0;
+            for (long long k : numel) {
+                offs.push_back(total);
+                total += ((size_t)k + 63) / 64 * 64;  // 256-byte aligned tensors
+            }
+            for (int dev : devs) {
+                if (dev < 0 || dev >= ndev) fail(FB2_INVALID_ARG, "device index out of range");
+                DeviceGuard g(dev);
+                cudaDeviceProp prop;
+                CK(cudaGetDeviceProperties(&prop, dev));
+                if (prop.major != 10) fail(FB2_UNSUPPORTED, "this build targets sm_100a (B200) only");
+                configure_kernels();
+                DeviceModel dm;
+                dm.device = dev;
+                dm.sm_count = prop.multiProcessorCount;
+                dm.blob = dalloc<float>(total);
+                m->devs.push_back(dm);
+                DeviceModel& D = m->devs.back();
+                for (int i = 0; i < n_params; i++) {
+                    CK(cudaMemcpy(D.blob + offs[i], params[i], (size_t)numel[i] * 4, cudaMemcpyHostToDevice));
+                    D.p.push_back(D.blob + offs[i]);
+                }
+                D.tok_emb = D.p[0];
+                D.pos_emb = D.p[1];
+                for (int l = 0; l < d.n_layers; l++) {
+                    const float* const* q = D.p.data() + 2 + 12 * l;
+                    D.layers.push_back(LayerW{q[0], q[1], q[2], q[3], q[4], q[5], q[6], q[7], q[8], q[9], q[10], q[11]});
+                }
+                D.lnf_w = D.p[2 + 12 * d.n_layers];
+                D.lnf_b = D.p[3 + 12 * d.n_layers];
+            }
+        } catch (...) {
+            for (auto& dm : m->devs) {
+                cudaSetDevice(dm.device);
+                dfree(dm.blob);
+            }
+            delete m;
+            throw;
+        }
+        *out = m;
+    });
+}
+
+void fb2_model_destroy(fb2_model* m) {
+    if (!m) return;
+    for (auto& dm : m->devs) {
+        cudaSetDevice(dm.device);
+        dfree(dm.blob);
+    }
+    delete m;
+}
+
+int32_t fb2_session_create(fb2_model* m, int32_t max_seqs, fb2_session** out) {
+    return guarded([&] {
+        if (!m || !out) fail(FB2_INVALID_ARG, "NULL argument");
+        if (max_seqs <= 0) fail(FB2_INVALID_ARG, "max_seqs must be positive");
+        *out = nullptr;
+        auto S = new fb2_session();
+        S->model = m;
+        S->max_seqs = max_seqs;
+        try {
+            int nd = (int)m->devs.size();
+            int per = ceil_div(max_seqs, nd);
+            for (int di = 0; di < nd; di++) {
+                int slot0 = di * per, cnt = std::max(0, std::min(per, max_seqs - slot0));
+                auto s = new DeviceSession();
+                S->ds.push_back(s);
+                s->model = m;
+                s->dm = &m->devs[di];
+                s->device = m->devs[di].device;
+                s->slot0 = slot0;
+                s->nslots = cnt;
+                if (cnt == 0) continue;
+                DeviceGuard g(s->device);
+                CK(cudaStreamCreateWithFlags(&s->own_stream, cudaStreamNonBlocking));
+                s->stream = s->own_stream;
+                CK(cudaEventCreate(&s->ev0));
+                CK(cudaEventCreate(&s->ev1));
+                CK(cudaEventCreateWithFlags(&s->tab_event, cudaEventDisableTiming));
+                const long long D = m->D, F = m->F;
+                s->kv_layer_stride = 2LL * m->H * m->ctx * m->hd;
+                s->v_offset = (long long)m->H * m->ctx * m->hd;
+                s->kv_slot_stride = s->kv_layer_stride * m->L;
+                s->d_kv = dalloc<float>((size_t)s->kv_slot_stride * cnt);
+                s->d_len = dalloc<int>(cnt);
+                s->d_count = dalloc<int>(cnt);
+                s->d_done = dalloc<int>(cnt);
+                CK(cudaMemset(s->d_len, 0, cnt * 4));
+                CK(cudaMemset(s->d_count, 0, cnt * 4));
+                CK(cudaMemset(s->d_done, 0, cnt * 4));
+                s->hist_cap = m->ctx + 64;
+                s->d_hist = dalloc<int>((size_t)cnt * s->hist_cap);
+                CK(cudaMemset(s->d_hist, 0, (size_t)cnt * s->hist_cap * 4));
+                // rows: enough for the largest prefill chunk
+                long long want = (long long)cnt * m->ctx;
+                s->row_cap = (int)std::max<long long>(m->ctx, std::min<long long>(want, 32768));
+                s->row_cap = std::max(s->row_cap, cnt);
+                size_t rc = s->row_cap;
+                s->d_row_seq = dalloc<int>(rc);
+                s->d_row_pos = dalloc<int>(rc);
+                s->d_row_hidx = dalloc<int>(rc);
+                s->d_row_active = dalloc<int>(rc);
+                s->d_ones = dalloc<int>(rc);
+                {
+                    std::vector<int> ones(rc, 1);
+                    CK(cudaMemcpy(s->d_ones, ones.data(), rc * 4, cudaMemcpyHostToDevice));
+                }
+                s->d_x = dalloc<float>(rc * D);
+                s->d_x2 = dalloc<float>(rc * D);
+                s->d_ln = dalloc<float>(rc * D);
+                s->d_q = dalloc<float>(rc * D);
+                s->d_att = dalloc<float>(rc * D);
+                s->d_h = dalloc<float>(rc * F);
+                s->d_logits = dalloc<float>((size_t)(cnt + kMaxChunkSlots) * m->V);
+                s->d_lnf = dalloc<float>((size_t)std::max(cnt, kMaxChunkSlots) * D);
+                s->attn_nsplit = ceil_div(m->ctx, kAttnChunk);
+                s->d_attn_part = dalloc<float>((size_t)cnt * m->H * s->attn_nsplit * (m->hd + 2));
+                s->gemv_part_cap = (size_t)64 * kMaxGemvRows * (size_t)std::max<long long>(4 * D, 1);
+                s->d_gemv_part = dalloc<float>(s->gemv_part_cap);
+                s->d_tickets = dalloc<unsigned int>(4096);
+                CK(cudaMemset(s->d_tickets, 0, 4096 * 4));
+                s->rngs.assign(cnt, DotNetRandom(0));
+                s->stats.device_count = nd;
+            }
+        } catch (...) {
+            for (auto s : S->ds) session_free(s);
+            delete S;
+            throw;
+        }
+        *out = S;
+    });
+}
+
+void fb2_session_destroy(fb2_session* S) {
+    if (!S) return;
+    for (auto s : S->ds) session_free(s);
+    delete S;
+}
+
+int32_t fb2_session_seed(fb2_session* S, int32_t seq, int32_t seed) {
+    return guarded([&] {
+        if (!S) fail(FB2_INVALID_ARG, "session is NULL");
+        if (seq < 0 || seq >= S->max_seqs) fail(FB2_INVALID_ARG, "slot out of range");
+        for (auto s : S->ds)
+            if (seq >= s->slot0 && seq < s->slot0 + s->nslots) s->rngs[seq - s->slot0].reseed(seed);
+    });
+}
+
+int32_t fb2_session_set_stream(fb2_session* S, int32_t device_slot, void* stream) {
+    return guarded([&] {
+        if (!S) fail(FB2_INVALID_ARG, "session is NULL");
+        if (device_slot < 0 || device_slot >= (int)S->ds.size()) fail(FB2_INVALID_ARG, "device slot out of range");
+        DeviceSession* s = S->ds[device_slot];
+        s->stream = stream ? static_cast<cudaStream_t>(stream) : s->own_stream;
+    });
+}
+
+static void check_generate_args(fb2_session* S, int32_t n_seqs, const int32_t* prompt_lens, const fb2_sampling* sp,
+                                int32_t rng_mode, const int32_t* seeds, const void* uniforms) {
+    if (!S) fail(FB2_INVALID_ARG, "session is NULL");
+    if (n_seqs <= 0 || n_seqs > S->max_seqs) fail(FB2_INVALID_ARG, "n_seqs out of range");
+    validate_sampling(*S->model, sp);
+    if (prompt_lens)
+        for (int i = 0; i < n_seqs; i++)
+            if (prompt_lens[i] <= 0) fail(FB2_INVALID_ARG, "Need at least one prompt token.");
+    if (rng_mode < FB2_RNG_SEEDS || rng_mode > FB2_RNG_UNIFORMS) fail(FB2_INVALID_ARG, "bad rng_mode");
+    if (sp->temperature > 0.0f && sp->max_new_tokens > 0) {
+        if (rng_mode == FB2_RNG_SEEDS && !seeds) fail(FB2_INVALID_ARG, "seeds is NULL");
+        if (rng_mode == FB2_RNG_UNIFORMS && !uniforms) fail(FB2_INVALID_ARG, "uniforms is NULL");
+    }
+}
+
+static void run_shards(fb2_session* S, std::vector<ShardJob>& jobs) {
+    std::vector<int> idx;
+    for (size_t i = 0; i < jobs.size(); i++)
+        if (jobs[i].n > 0) idx.push_back((int)i);
+    if (idx.size() <= 1) {
+        for (int i : idx) run_generate_shard(*S->ds[i], jobs[i]);
+        return;
+    }
+    std::vector<std::thread> th;
+    std::vector<int> st(jobs.size(), FB2_OK);
+    std::vector<std::string> msg(jobs.size());
+    for (int i : idx)
+        th.emplace_back([&, i] {
+            st[i] = guarded([&] { run_generate_shard(*S->ds[i], jobs[i]); });
+            if (st[i] != FB2_OK) msg[i] = g_last_error;
+        });
+    for (auto& t : th) t.join();
+    for (int i : idx)
+        if (st[i] != FB2_OK) fail(st[i], msg[i]);
+}
+
+int32_t fb2_generate(fb2_session* S, int32_t n_seqs, const int32_t* prompt_tokens, const int32_t* prompt_lens,
+                     const fb2_sampling* sp, int32_t rng_mode, const int32_t* seeds, const double* uniforms,
+                     int32_t* out_tokens, int32_t* out_counts, fb2_token_cb cb, void* user) {
+    return guarded([&] {
+        if (!prompt_tokens || !prompt_lens || !out_counts) fail(FB2_INVALID_ARG, "NULL argument");
+        check_generate_args(S, n_seqs, prompt_lens, sp, rng_mode, seeds, uniforms);
+        if (sp->max_new_tokens > 0 && !out_tokens) fail(FB2_INVALID_ARG, "out_tokens is NULL");
+        const fb2_model& m = *S->model;
+        long long total = 0;
+        for (int i = 0; i < n_seqs; i++) total += prompt_lens[i];
+        for (long long i = 0; i < total; i++)
+            if (prompt_tokens[i] < 0 || prompt_tokens[i] >= m.V)
+                fail(FB2_INVALID_ARG, "Token id out of range [0," + std::to_string(m.V) + ").");
+        const int max_new = sp->max_new_tokens;
+        std::mutex cbm;
+        std::atomic<int> stop{0};
+        std::vector<ShardJob> jobs;
+        long long toff = 0;
+        for (auto s : S->ds) {
+            ShardJob j{};
+            j.first = s->slot0;
+            j.n = std::max(0, std::min(s->nslots, n_seqs - s->slot0));
+            j.prompt_tokens = prompt_tokens + toff;
+            j.prompt_lens = prompt_lens + std::min(s->slot0, n_seqs);
+            for (int i = 0; i < j.n; i++) toff += prompt_lens[s->slot0 + i];
+            j.sp = sp;
+            j.rng_mode = rng_mode;
+            j.seeds = seeds;
+            j.uniforms = uniforms ? uniforms + (size_t)std::min(s->slot0, n_seqs) * max_new : nullptr;
+            j.device_io = false;
+            j.out_tokens = out_tokens ? out_tokens + (size_t)std::min(s->slot0, n_seqs) * max_new : nullptr;
+            j.out_counts = out_counts + std::min(s->slot0, n_seqs);
+            j.cb = cb;
+            j.user = user;
+            j.cb_mutex = &cbm;
+            j.stop = &stop;
+            jobs.push_back(j);
+        }
+        if (max_new == 0) {
+            for (int i = 0; i < n_seqs; i++) out_counts[i] = 0;
+            return;
+        }
+        run_shards(S, jobs);
+    });
+}
+
+int32_t fb2_generate_device(fb2_session* S, int32_t n_seqs, const int32_t* device_prompt_tokens,
+                            const int32_t* device_prompt_lens, const int32_t* host_prompt_lens, const fb2_sampling* sp,
+                            int32_t rng_mode, const int32_t* seeds, const double* device_uniforms,
+                            int32_t* device_out_tokens, int32_t* device_out_counts) {
+    return guarded([&] {
+        if (!device_prompt_tokens || !device_prompt_lens || !host_prompt_lens || !device_out_counts)
+            fail(FB2_INVALID_ARG, "NULL argument");
+        check_generate_args(S, n_seqs, host_prompt_lens, sp, rng_mode, seeds, device_uniforms);
+        if (S->ds.size() != 1) fail(FB2_UNSUPPORTED, "fb2_generate_device needs a single-device session");
+        if (sp->max_new_tokens > 0 && !device_out_tokens) fail(FB2_INVALID_ARG, "out_tokens is NULL");
+        std::mutex cbm;
+        std::atomic<int> stop{0};
+        ShardJob j{};
+        j.first = 0;
+        j.n = n_seqs;
+        j.prompt_lens = host_prompt_lens;
+        j.dev_prompt_tokens = device_prompt_tokens;
+        j.dev_prompt_lens = device_prompt_lens;
+        j.sp = sp;
+        j.rng_mode = rng_mode;
+        j.seeds = seeds;
+        j.uniforms = device_uniforms;
+        j.device_io = true;
+        j.out_tokens = device_out_tokens;
+        j.out_counts = device_out_counts;
+        j.cb = nullptr;
+        j.cb_mutex = &cbm;
+        j.stop = &stop;
+        if (sp->max_new_tokens == 0) {
+            DeviceGuard g(S->ds[0]->device);
+            CK(cudaMemsetAsync(device_out_counts, 0, n_seqs * 4, S->ds[0]->stream));
+            return;
+        }
+        run_generate_shard(*S->ds[0], j);
+    });
+}
+
+__global__ void k_bump_len(int n, int* len) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) len[i] += 1;
+}
+
+// Loads whole token sequences into the slots' histories with len = `len0`.
+static void load_histories(DeviceSession& s, int n, const int* tokens_host, int seq_len, int len0) {
+    std::vector<int> tab;
+    tab.assign(tokens_host, tokens_host + (size_t)n * seq_len);
+    int pl_off = (int)tab.size();
+    for (int i = 0; i < n; i++) tab.push_back(seq_len);
+    int poff_off = (int)tab.size();
+    for (int i = 0; i < n; i++) tab.push_back(i * seq_len);
+    upload_tables(s, tab, nullptr);
+    s.stats.kernel_launches++; k_init_slots<<<n, 256, 0, s.stream>>>(n, s.d_tab + pl_off, s.d_tab + poff_off, s.d_tab, s.d_hist, s.hist_cap,
+                                          s.d_len, s.d_count, s.d_done, 1);
+    std::vector<int> lens(n, len0);
+    CK(cudaMemcpyAsync(s.d_len, lens.data(), n * 4, cudaMemcpyHostToDevice, s.stream));
+    CK(cudaStreamSynchronize(s.stream));
+}
+
+int32_t fb2_forward_last_logits(fb2_session* S, int32_t n_seqs, const int32_t* tokens, const int32_t* lens,
+                                float* out_logits) {
+    return guarded([&] {
+        if (!S || !tokens || !lens || !out_logits) fail(FB2_INVALID_ARG, "NULL argument");
+        if (n_seqs <= 0 || n_seqs > S->max_seqs) fail(FB2_INVALID_ARG, "n_seqs out of range");
+        const fb2_model& m = *S->model;
+        long long total = 0;
+        for (int i = 0; i < n_seqs; i++) {
+            if (lens[i] <= 0) fail(FB2_INVALID_ARG, "Need at least one token.");
+            if (lens[i] > m.ctx) fail(FB2_INVALID_ARG, "Sequence length exceeds ContextLength.");
+            total += lens[i];
+        }
+        for (long long i = 0; i < total; i++)
+            if (tokens[i] < 0 || tokens[i] >= m.V) fail(FB2_INVALID_ARG, "Token id out of range.");
+        long long toff = 0;
+        for (auto sp : S->ds) {
+            DeviceSession& s = *sp;
+            int n = std::max(0, std::min(s.nslots, n_seqs - s.slot0));
+            if (n == 0) continue;
+            DeviceGuard g(s.device);
+            ensure_capacity(s, m.ctx + 1, 1, 1);
+            std::vector<int> wl(n), all(n), tab;
+            for (int i = 0; i < n; i++) { wl[i] = lens[s.slot0 + i]; all[i] = i; }
+            std::vector<ChunkPlan> plans;
+            plan_prefill(s, all, wl, tab, plans);
+            while (tab.size() % 4) tab.push_back(0);
+            int ptok_off = (int)tab.size();
+            long long cnt = 0;
+            for (int i = 0; i < n; i++) cnt += wl[i];
+            tab.insert(tab.end(), tokens + toff, tokens + toff + cnt);
+            int pl_off = (int)tab.size();
+            tab.insert(tab.end(), wl.begin(), wl.end());
+            int poff_off = (int)tab.size();
+            int acc = 0;
+            for (int i = 0; i < n; i++) { tab.push_back(acc); acc += wl[i]; }
+            toff += cnt;
+            upload_tables(s, tab, nullptr);
+            s.stats.kernel_launches++; k_init_slots<<<n, 256, 0, s.stream>>>(n, s.d_tab + pl_off, s.d_tab + poff_off, s.d_tab + ptok_off,
+                                                  s.d_hist, s.hist_cap, s.d_len, s.d_count, s.d_done, 1);
+            for (const ChunkPlan& c : plans) run_prefill_chunk(s, c, s.d_tab);
+            CK(cudaGetLastError());
+            CK(cudaMemcpyAsync(out_logits + (size_t)s.slot0 * m.V, s.d_logits, (size_t)n * m.V * 4,
+                               cudaMemcpyDeviceToHost, s.stream));
+            CK(cudaStreamSynchronize(s.stream));
+        }
+    });
+}
+
+int32_t fb2_teacher_forced_logits(fb2_session* S, int32_t n_seqs, const int32_t* tokens, int32_t len,
+                                  int32_t prompt_len, float* out_logits) {
+    return guarded([&] {
+        if (!S || !tokens || !out_logits) fail(FB2_INVALID_ARG, "NULL argument");
+        const fb2_model& m = *S->model;
+        if (n_seqs <= 0 || n_seqs > S->max_seqs) fail(FB2_INVALID_ARG, "n_seqs out of range");
+        if (prompt_len < 1 || len < prompt_len || len > m.ctx) fail(FB2_INVALID_ARG, "need 1 <= prompt_len <= len <= ctx");
+        for (long long i = 0; i < (long long)n_seqs * len; i++)
+            if (tokens[i] < 0 || tokens[i] >= m.V) fail(FB2_INVALID_ARG, "Token id out of range.");
+        const int steps = len - prompt_len + 1;
+        for (auto sp : S->ds) {
+            DeviceSession& s = *sp;
+            int n = std::max(0, std::min(s.nslots, n_seqs - s.slot0));
+            if (n == 0) continue;
+            DeviceGuard g(s.device);
+            ensure_capacity(s, m.ctx + 1, 1, 1);
+            load_histories(s, n, tokens + (size_t)s.slot0 * len, len, prompt_len);
+            std::vector<int> wl(n, prompt_len), all(n), tab;
+            for (int i = 0; i < n; i++) all[i] = i;
+            std::vector<ChunkPlan> plans;
+            plan_prefill(s, all, wl, tab, plans);
+            upload_tables(s, tab, nullptr);
+            for (const ChunkPlan& c : plans) run_prefill_chunk(s, c, s.d_tab);
+            for (int st = 0; st < steps; st++) {
+                if (st > 0) {
+                    s.stats.kernel_launches++; k_bump_len<<<ceil_div(n, 128), 128, 0, s.stream>>>(n, s.d_len);
+                    run_decode_step(s, n);
+                }
+                CK(cudaGetLastError());
+                for (int i = 0; i < n; i++)
+                    CK(cudaMemcpyAsync(out_logits + (((size_t)(s.slot0 + i)) * steps + st) * m.V,
+                                       s.d_logits + (size_t)i * m.V, (size_t)m.V * 4, cudaMemcpyDeviceToHost,
+                                       s.stream));
+            }
+            CK(cudaStreamSynchronize(s.stream));
+        }
+    });
+}
+
+int32_t fb2_sample_logits(fb2_session* S, int32_t n, const float* logits, const int32_t* windows,
+                          const int32_t* window_lens, const fb2_sampling* sp, const double* uniforms,
+                          int32_t* out_ids) {
+    return guarded([&] {
+        if (!S || !logits || !window_lens || !out_ids) fail(FB2_INVALID_ARG, "NULL argument");
+        if (n <= 0) fail(FB2_INVALID_ARG, "n must be positive");
+        const fb2_model& m = *S->model;
+        validate_sampling(m, sp);
+        if (sp->temperature > 0.0f && !uniforms) fail(FB2_INVALID_ARG, "uniforms is NULL");
+        long long wtot = 0;
+        for (int i = 0; i < n; i++) {
+            if (window_lens[i] < 0) fail(FB2_INVALID_ARG, "window length must be >= 0");
+            wtot += window_lens[i];
+        }
+        if (wtot > 0 && !windows) fail(FB2_INVALID_ARG, "windows is NULL");
+        DeviceSession& s = *S->ds[0];
+        DeviceGuard g(s.device);
+        std::vector<int> tab;
+        tab.assign(windows ? windows : nullptr, windows ? windows + wtot : nullptr);
+        int off_off = (int)tab.size();
+        long long acc = 0;
+        for (int i = 0; i < n; i++) { tab.push_back((int)acc); acc += window_lens[i]; }
+        int len_off = (int)tab.size();
+        tab.insert(tab.end(), window_lens, window_lens + n);
+        int ids_off = (int)tab.size();
+        for (int i = 0; i < n; i++) tab.push_back(0);
+        std::vector<double> uni(n, 0.0);
+        if (uniforms) uni.assign(uniforms, uniforms + n);
+        ensure_capacity(s, 1, (size_t)n, 1);
+        upload_tables(s, tab, &uni);
+        float* d_l = dalloc<float>((size_t)n * m.V);
+        try {
+            CK(cudaMemcpyAsync(d_l, logits, (size_t)n * m.V * 4, cudaMemcpyHostToDevice, s.stream));
+            s.stats.kernel_launches++; k_sample_rows<<<n, kSampleThreads, sampler_smem_bytes(m.V), s.stream>>>(
+                n, d_l, m.V, s.d_tab, s.d_tab + off_off, s.d_tab + len_off, s.d_uni, to_params(*sp), s.d_tab + ids_off);
+            CK(cudaGetLastError());
+            CK(cudaMemcpyAsync(out_ids, s.d_tab + ids_off, n * 4, cudaMemcpyDeviceToHost, s.stream));
+            CK(cudaStreamSynchronize(s.stream));
+        } catch (...) {
+            cudaFree(d_l);
+            throw;
+        }
+        cudaFree(d_l);
+    });
+}
+
+int32_t fb2_init_params(const fb2_model_desc* desc, int32_t seed, float* const* params, int32_t n_params) {
+    return guarded([&] {
+        if (!desc || !params) fail(FB2_INVALID_ARG, "NULL argument");
+        const fb2_model_desc& d = *desc;
+        if (d.vocab_size <= 0 || d.context_length <= 0 || d.d_model <= 0 || d.n_layers <= 0 || d.n_heads <= 0)
+            fail(FB2_INVALID_ARG, "model sizes must be positive");
+        if (n_params != 4 + 12 * d.n_layers) fail(FB2_INVALID_ARG, "n_params must be 4 + 12*n_layers");
+        std::vector<long long> numel = param_numels(d);
+        DotNetRandom rng(seed);
+        const float std_ = 0.02f;
+        const float resid = 0.02f / sqrtf(2.0f * (float)d.n_layers);  // GptModel.cs:50
+        auto normal = [&](float* p, long long n, float s) {  // Tensor.FillNormal, Tensor.cs:79-91
+            for (long long i = 0; i < n; i += 2) {
+                double u1 = 1.0 - rng.next_double();
+                double u2 = rng.next_double();
+                double r = std::sqrt(-2.0 * std::log(u1));
+                p[i] = (float)(r * std::cos(2 * M_PI * u2) * (double)s);
+                if (i + 1 < n) p[i + 1] = (float)(r * std::sin(2 * M_PI * u2) * (double)s);
+            }
+        };
+        for (int i = 0; i < n_params; i++) {
+            float* p = params[i];
+            if (!p) fail(FB2_INVALID_ARG, "parameter pointer is NULL");
+            long long n = numel[i];
+            int kind = (i < 2) ? -1 : (i >= n_params - 2 ? 100 + (i - (n_params - 2)) : (i - 2) % 12);
+            switch (kind) {
+            case -1: case 2: case 8: normal(p, n, std_); break;
+            case 4: case 10: normal(p, n, resid); break;
+            case 0: case 6: case 100: std::fill(p, p + n, 1.0f); break;  // LayerNorm weights
+            default: std::fill(p, p + n, 0.0f); break;                   // biases
+            }
+        }
+    });
+}
+
+int32_t fb2_stats(fb2_session* S, fb2_stats_t* out) {
+    return guarded([&] {
+        if (!S || !out) fail(FB2_INVALID_ARG, "NULL argument");
+        fb2_stats_t t{};
+        for (auto s : S->ds) {
+            t.tokens_generated += s->stats.tokens_generated;
+            t.decode_steps += s->stats.decode_steps;
+            t.prefill_rows += s->stats.prefill_rows;
+            t.reprefills += s->stats.reprefills;
+            t.prefill_ms += s->stats.prefill_ms;
+            t.decode_ms += s->stats.decode_ms;
+            t.sample_ms += s->stats.sample_ms;
+            t.kernel_launches += s->stats.kernel_launches;
+        }
+        t.device_count = (int)S->ds.size();
+        *out = t;
+    });
+}
+
+int32_t fb2_stats_reset(fb2_session* S) {
+    return guarded([&] {
+        if (!S) fail(FB2_INVALID_ARG, "NULL argument");
+        for (auto s : S->ds) {
+            int dc = s->stats.device_count;
+            s->stats = fb2_stats_t{};
+            s->stats.device_count = dc;
+        }
+    });
+}
+
+// ---- test hooks (not part of the reference surface) -------------------------
+// n successive NextDouble() values of `new Random(seed)` as the library
+// restates it (host code; needs no device).
+int32_t fb2_test_dotnet_random(int32_t seed, int32_t n, double* out) {
+    return guarded([&] {
+        if (!out || n < 0) fail(FB2_INVALID_ARG, "bad arguments");
+        DotNetRandom r(seed);
+        for (int i = 0; i < n; i++) out[i] = r.next_double();
+    });
+}
+
+// Device expf_libm over n inputs (host arrays).
+int32_t fb2_test_expf(const float* x, float* y, int64_t n) {
+    return guarded([&] {
+        if (!x || !y || n <= 0) fail(FB2_INVALID_ARG, "bad arguments");
+        float *dx = dalloc<float>(n), *dy = dalloc<float>(n);
+        CK(cudaMemcpy(dx, x, n * 4, cudaMemcpyHostToDevice));
+        k_expf_libm<<<ceil_div(n, 256), 256>>>(dx, dy, n);
+        cudaError_t e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaMemcpy(y, dy, n * 4, cudaMemcpyDeviceToHost);
+        cudaFree(dx);
+        cudaFree(dy);
+        CK(e);
+    });
+}
+
+// Per-chunk (2^20 inputs) hashes of expf_libm over [lo_bits, lo_bits + nchunks*2^20).
+int32_t fb2_test_expf_hash(uint32_t lo_bits, int32_t nchunks, uint64_t* hashes) {
+    return guarded([&] {
+        if (!hashes || nchunks <= 0) fail(FB2_INVALID_ARG, "bad arguments");
+        unsigned long long* d = dalloc<unsigned long long>(nchunks);
+        CK(cudaMemset(d, 0, nchunks * 8));
+        k_expf_libm_hash<<<nchunks, 1024>>>(lo_bits, nchunks, d);
+        cudaError_t e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaMemcpy(hashes, d, nchunks * 8, cudaMemcpyDeviceToHost);
+        cudaFree(d);
+        CK(e);
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,205 @@
+/*
+ * forge_b200.h — C ABI of libforge_b200.so, the B200 (sm_100a) decode library
+ * behind ForgeLM's `--backend b200`.
+ *
+ * The library replaces everything below Sampler.Generate for the
+ * autoregressive token loop of TitanUranus67/forge-lm:
+ *   - src/LLM.Core/Inference/Sampler.cs:78-109   Sampler.Generate (token loop)
+ *   - src/LLM.Core/Model/GptModel.cs:202-222     ForwardLast / ForwardCore
+ *   - src/LLM.Core/Inference/Sampler.cs:14-165   Greedy, Sample, ApplyRepetitionControls
+ * The C# side keeps checkpoint loading, the tokenizer and the CLI; it hands
+ * the fp32 weights (Parameters.Names order, GptModel.cs:14-18) to
+ * fb2_model_create and calls fb2_generate from a B200Backend that the
+ * reference's BackendSelection (src/LLM.Core/Tensor/BackendSelection.cs:160-180)
+ * selects by the name "b200".
+ *
+ * Conventions
+ *   - Every entry point returns FB2_OK (0) or a negative fb2_status; nothing
+ *     aborts or throws across the ABI.  fb2_last_error() gives a message for
+ *     the calling thread's last failure.
+ *   - Plain pointers and sizes only.  Host pointers unless a name says
+ *     "device".  The library copies what it keeps; callers keep ownership.
+ *   - A model is read-only after creation and may be shared by sessions.
+ *     A session is used by one host thread at a time (the reference's CUDA
+ *     backend serialises every call the same way, CudaBackend.cs:36,125).
+ *   - Token ids are int32 in [0, vocab_size).  Arithmetic is fp32, or bf16
+ *     weights with fp32 accumulation when weight_dtype = FB2_WEIGHTS_BF16.
+ */
+#ifndef FORGE_B200_H
+#define FORGE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FB2_ABI_VERSION 1
+
+/* Status codes.  The C# shim maps INVALID_ARG to ArgumentException /
+ * ArgumentOutOfRangeException (Sampler.cs:85-89, GptModel.cs:279-299) and
+ * the device errors to InvalidOperationException (CudaBackend.cs:213). */
+typedef enum {
+    FB2_OK = 0,
+    FB2_INVALID_ARG = -1,
+    FB2_OUT_OF_MEMORY = -2,
+    FB2_CUDA_ERROR = -3,
+    FB2_TIMEOUT = -4,      /* a bounded device wait gave up; the context stays usable */
+    FB2_UNSUPPORTED = -5,  /* shape or option this build does not handle */
+    FB2_NO_DEVICE = -6
+} fb2_status;
+
+typedef enum { FB2_WEIGHTS_FP32 = 0, FB2_WEIGHTS_BF16 = 1 } fb2_weight_dtype;
+
+/* ModelConfig (src/LLM.Core/Model/ModelConfig.cs:8-26): MlpHidden = 4*d_model,
+ * HeadDim = d_model / n_heads. */
+typedef struct {
+    int32_t vocab_size;
+    int32_t context_length;
+    int32_t d_model;
+    int32_t n_layers;
+    int32_t n_heads;
+    int32_t weight_dtype; /* fb2_weight_dtype */
+} fb2_model_desc;
+
+/* Arguments of Sampler.Generate (Sampler.cs:78-80). */
+typedef struct {
+    float temperature;        /* <= 0: greedy argmax, no RNG draw (Sampler.cs:35) */
+    int32_t top_k;            /* <= 0 or >= vocab: no filtering (Sampler.cs:42) */
+    float repetition_penalty; /* finite, >= 1 (Sampler.cs:167-175) */
+    int32_t no_repeat_ngram;  /* >= 0; 0 disables */
+    int32_t eos_id;           /* < 0: no EOS stop; else in [0, vocab) (Sampler.cs:87-88,107) */
+    int32_t max_new_tokens;   /* >= 0 (Sampler.cs:86) */
+} fb2_sampling;
+
+/* Where the uniforms of categorical sampling (Sampler.cs:61) come from. */
+typedef enum {
+    /* seeds[i]: a fresh `new Random(seeds[i])` stream per sequence for this
+     * call (Program.cs:664 creates one per generate). */
+    FB2_RNG_SEEDS = 0,
+    /* The stream kept in the session slot of each sequence, seeded by
+     * fb2_session_seed and carried across calls (chat, Program.cs:730). */
+    FB2_RNG_SESSION = 1,
+    /* uniforms[i * max_new + n]: the caller's NextDouble() values. */
+    FB2_RNG_UNIFORMS = 2
+} fb2_rng_mode;
+
+/* Per-token streaming callback (Program.cs:671-677 prints each id as it is
+ * yielded).  Called on the thread that called fb2_generate, in step order,
+ * once per emitted token.  Return nonzero to stop generation early. */
+typedef int32_t (*fb2_token_cb)(void* user, int32_t seq, int32_t step, int32_t token);
+
+typedef struct fb2_model fb2_model;
+typedef struct fb2_session fb2_session;
+
+typedef struct {
+    int64_t tokens_generated;   /* ids emitted since the last reset */
+    int64_t decode_steps;       /* KV-cached single-row steps run */
+    int64_t prefill_rows;       /* rows pushed through full-window prefill */
+    int64_t reprefills;         /* sliding-window re-prefills (Sampler.cs:93-94) */
+    double prefill_ms;          /* device time (CUDA events) per phase */
+    double decode_ms;
+    double sample_ms;
+    int64_t kernel_launches;    /* kernels the library launched (graph nodes counted) */
+    int32_t device_count;
+    int32_t reserved;
+} fb2_stats_t;
+
+/* ---- library ------------------------------------------------------------- */
+int32_t fb2_version(void);
+const char* fb2_last_error(void);
+int32_t fb2_device_count(int32_t* n);
+
+/* ---- model ----------------------------------------------------------------
+ * Replaces GptModel construction + Checkpoint.LoadCore's upload
+ * (Checkpoint.cs:207-227).  params[i] points to the fp32 host data of
+ * parameter i in registration order (GptModel.cs:14-18, 47-98):
+ *   tok_emb [V,D], pos_emb [ctx,D],
+ *   blocks.{l}.{ln1.w, ln1.b, attn.qkv.w [D,3D], attn.qkv.b, attn.proj.w [D,D],
+ *               attn.proj.b, ln2.w, ln2.b, mlp.fc.w [D,4D], mlp.fc.b,
+ *               mlp.proj.w [4D,D], mlp.proj.b},
+ *   ln_f.w, ln_f.b.
+ * n_params must be 4 + 12*n_layers.  The weights are copied to every listed
+ * device (devices == NULL: device 0 only). */
+int32_t fb2_model_create(const fb2_model_desc* desc, const float* const* params, int32_t n_params,
+                         const int32_t* devices, int32_t n_devices, fb2_model** out);
+void fb2_model_destroy(fb2_model* m);
+
+/* ---- session --------------------------------------------------------------
+ * Owns per-sequence KV caches, token histories, RNG streams and the captured
+ * decode-step graphs.  max_seqs sequences are split into contiguous blocks
+ * over the model's devices. */
+int32_t fb2_session_create(fb2_model* m, int32_t max_seqs, fb2_session** out);
+void fb2_session_destroy(fb2_session* s);
+/* Seeds the FB2_RNG_SESSION stream of slot `seq` as `new Random(seed)`. */
+int32_t fb2_session_seed(fb2_session* s, int32_t seq, int32_t seed);
+/* Runs the session's work for device slot `device_slot` on the caller's
+ * CUDA stream (a cudaStream_t passed as void*; NULL restores the library's
+ * own stream). */
+int32_t fb2_session_set_stream(fb2_session* s, int32_t device_slot, void* cuda_stream);
+
+/* ---- the token loop -------------------------------------------------------
+ * Sampler.Generate (Sampler.cs:78-109) for n_seqs independent sequences.
+ * prompt_tokens holds the prompts back to back; prompt_lens[i] >= 1 each.
+ * out_tokens is [n_seqs * max_new_tokens]; sequence i writes its ids at
+ * out_tokens[i * max_new_tokens ...] and its count to out_counts[i] (fewer
+ * than max_new_tokens only when EOS was sampled; the EOS id is included).
+ * Results equal the reference loop: the window is truncated to the context
+ * length before each forward (a longer window is re-prefilled in full),
+ * repetition controls see the truncated window, one uniform is drawn per
+ * sampled token when temperature > 0. */
+int32_t fb2_generate(fb2_session* s, int32_t n_seqs, const int32_t* prompt_tokens,
+                     const int32_t* prompt_lens, const fb2_sampling* sp, int32_t rng_mode,
+                     const int32_t* seeds, const double* uniforms, int32_t* out_tokens,
+                     int32_t* out_counts, fb2_token_cb cb, void* user);
+
+/* The same loop with device-resident inputs and outputs (single-device
+ * sessions): device_prompt_tokens/device_prompt_lens/device_uniforms and
+ * device_out_tokens/device_out_counts are device pointers on the session's
+ * device.  No host<->device copy is made and the call returns once the work
+ * is enqueued on the session stream (no callback). */
+int32_t fb2_generate_device(fb2_session* s, int32_t n_seqs, const int32_t* device_prompt_tokens,
+                            const int32_t* device_prompt_lens, const int32_t* host_prompt_lens,
+                            const fb2_sampling* sp, int32_t rng_mode, const int32_t* seeds,
+                            const double* device_uniforms, int32_t* device_out_tokens,
+                            int32_t* device_out_counts);
+
+/* ---- parity hooks -----------------------------------------------------------
+ * GptModel.ForwardLast (GptModel.cs:202-209) for n_seqs windows through the
+ * library's prefill path: out_logits is [n_seqs * V]. */
+int32_t fb2_forward_last_logits(fb2_session* s, int32_t n_seqs, const int32_t* tokens,
+                                const int32_t* lens, float* out_logits);
+
+/* Teacher-forced decode: for each sequence, prefill tokens[0..prompt_len)
+ * and then feed tokens[prompt_len..len) one at a time through the KV-cached
+ * decode step.  out_logits receives, per sequence, the last-row logits after
+ * each prefix of length prompt_len..len: [n_seqs * (len - prompt_len + 1) * V].
+ * All sequences share len and prompt_len; len <= context_length. */
+int32_t fb2_teacher_forced_logits(fb2_session* s, int32_t n_seqs, const int32_t* tokens, int32_t len,
+                                  int32_t prompt_len, float* out_logits);
+
+/* Sampler.ApplyRepetitionControls + Sampler.Sample (Sampler.cs:29-69,
+ * 96-104, 111-165) on the device for n logit rows of length V:
+ * windows holds the windows back to back, window_lens[i] each;
+ * uniforms[i] is the NextDouble() value for row i (ignored when
+ * temperature <= 0).  out_ids[n]. */
+int32_t fb2_sample_logits(fb2_session* s, int32_t n, const float* logits, const int32_t* windows,
+                          const int32_t* window_lens, const fb2_sampling* sp, const double* uniforms,
+                          int32_t* out_ids);
+
+/* ---- synthetic weights -------------------------------------------------------
+ * Host-only: fills params[i] (caller-allocated fp32 arrays of the sizes listed
+ * at fb2_model_create) with the weights `new GptModel(config, backend,
+ * new Random(seed))` creates (GptModel.cs:47-98; Box-Muller in double,
+ * Tensor.cs:79-91): tok_emb, pos_emb, qkv.w, fc.w ~ N(0, 0.02); attn.proj.w,
+ * mlp.proj.w ~ N(0, 0.02/sqrt(2L)); LayerNorm weights 1; biases 0. */
+int32_t fb2_init_params(const fb2_model_desc* desc, int32_t seed, float* const* params, int32_t n_params);
+
+/* ---- statistics -------------------------------------------------------------- */
+int32_t fb2_stats(fb2_session* s, fb2_stats_t* out);
+int32_t fb2_stats_reset(fb2_session* s);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FORGE_B200_H */

@@ -1,0 +1,33 @@
+/*
+ * forge_b200_testing.h — test hooks exported by libforge_b200.so.
+ *
+ * Not part of the reference-facing surface (no counterpart in
+ * TitanUranus67/forge-lm).  The GPU tests use them to prove that the device
+ * exponential of the sampler equals the host C runtime's expf, which the
+ * reference sampler calls as MathF.Exp (src/LLM.Core/Inference/Sampler.cs:57).
+ */
+#ifndef FORGE_B200_TESTING_H
+#define FORGE_B200_TESTING_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* y[i] = device exponential of x[i] (host arrays, n > 0). */
+int32_t fb2_test_expf(const float* x, float* y, int64_t n);
+
+/* For each chunk c < nchunks of 2^20 consecutive float bit patterns starting
+ * at lo_bits + c * 2^20: an order-independent 64-bit hash of the device
+ * exponential's output bits (NaN inputs hash as output 0). */
+int32_t fb2_test_expf_hash(uint32_t lo_bits, int32_t nchunks, uint64_t* hashes);
+
+/* n successive NextDouble() values of `new Random(seed)` as the library's
+ * FB2_RNG_SEEDS mode draws them (host only; no device needed). */
+int32_t fb2_test_dotnet_random(int32_t seed, int32_t n, double* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,246 @@
+"""Parity of the CUDA library (through the C ABI) with the CPU oracle.
+
+Tolerances (from the reference, tests/LLM.Core.Tests/GpuBackendTests.cs:90-101,
+601-611): fp32 logits max |a-e| / max(1, |e|) <= 1e-3.  Sampled ids:
+bit-exact given the same logits, window and uniforms.  Greedy / sampled id
+streams: exact, except that a divergence is accepted only at a near-tie of
+the oracle's logits (the two candidates within 1e-4 of each other), the
+documented effect of fp32 reduction order.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+
+
+def relerr(a, e):
+    a = np.asarray(a, np.float64)
+    e = np.asarray(e, np.float64)
+    return float(np.max(np.abs(a - e) / np.maximum(1.0, np.abs(e))))
+
+
+TINY = (12, 6, 8, 1, 2)          # GpuBackendTests.cs:599
+SMALL = (32, 8, 16, 2, 2)        # InferenceTests.cs:17
+C1 = (2256, 256, 256, 4, 4)
+
+
+def make(pkg, O, shape, seed, max_seqs=1):
+    ocfg = O.Config(*shape)
+    params = O.init_params(ocfg, seed)
+    be = pkg.B200Backend(pkg.ModelConfig(*shape), params, devices=[0], max_seqs=max_seqs)
+    return ocfg, params, be
+
+
+# ---------------------------------------------------------------------------
+def test_device_expf_equals_host_libm_exhaustive(pkg, O):
+    """Every float input: the sampler's device exponential returns the host
+    C runtime's expf bits (MathF.Exp, Sampler.cs:57)."""
+    import ctypes as C
+    from forge_lm_b200 import _native as N
+    n = 4096  # 2^32 patterns in chunks of 2^20
+    dev = np.zeros(n, np.uint64)
+    N.check(N.load().fb2_test_expf_hash(0, n, C.c_void_p(dev.ctypes.data)))
+    host = O.expf_hash(0, n)
+    bad = np.nonzero(dev != host)[0]
+    assert bad.size == 0, f"chunks differing from host expf: {bad[:10]}"
+
+
+def test_forward_last_tiny_golden(pkg, O, golden):
+    g = golden["device_logits_tolerance"]
+    ocfg, params, be = make(pkg, O, tuple(g["config"]), g["model_seed"])
+    with be:
+        got = be.forward_last(g["tokens"])
+        want = O.forward(ocfg, params, g["tokens"])[-1]
+        assert relerr(got, want) <= g["tolerance"]
+
+
+@pytest.mark.parametrize("shape,seed", [(SMALL, 1), (C1, 1234)])
+def test_forward_last_ragged_batch(pkg, O, shape, seed):
+    ocfg, params, be = make(pkg, O, shape, seed, max_seqs=5)
+    rng = np.random.default_rng(7)
+    ctx = shape[1]
+    lens = [1, 3, ctx // 2 + 1, ctx - 1, ctx]
+    wins = [rng.integers(0, shape[0], L).astype(np.int32) for L in lens]
+    with be:
+        got = be.forward_last_batch(wins)
+        for i, w in enumerate(wins):
+            assert relerr(got[i], O.forward_last(ocfg, params, w)) <= TOL, f"window len {lens[i]}"
+
+
+def test_teacher_forced_decode_matches_full_forward(pkg, O):
+    """The KV-cached decode step equals ForwardLast of each prefix."""
+    ocfg, params, be = make(pkg, O, C1, 1234, max_seqs=2)
+    rng = np.random.default_rng(3)
+    toks = rng.integers(0, C1[0], (2, 80)).astype(np.int32)
+    with be:
+        got = be.teacher_forced_logits(toks, 32)
+    assert got.shape == (2, 49, C1[0])
+    for s in range(2):
+        for k in range(0, 49, 4):
+            want = O.forward_last(ocfg, params, toks[s, :32 + k])
+            assert relerr(got[s, k], want) <= TOL, (s, k)
+
+
+# ---------------------------------------------------------------------------
+def _rows_cases(V, rng):
+    cases = []
+    for t in range(40):
+        lg = (rng.standard_normal(V) * rng.choice([0.5, 2.0, 8.0])).astype(np.float32)
+        if t % 5 == 1:  # many ties around the k-th value
+            lg = np.round(lg * 2) / 2
+        if t % 7 == 2:
+            lg[rng.integers(0, V, 20)] = -np.inf
+        win = rng.integers(0, V, rng.integers(0, 60)).astype(np.int32)
+        if t % 6 == 3 and len(win) > 4:  # repeated n-grams
+            win = np.concatenate([win[:4], win[:4], win[:3]]).astype(np.int32)
+        cases.append((lg, win))
+    return cases
+
+
+@pytest.mark.parametrize("V", [2256, 16384, 7])
+@pytest.mark.parametrize("temperature,top_k,penalty,ngram", [
+    (0.0, 0, 1.0, 0), (0.7, 30, 1.1, 4), (1.0, 0, 1.0, 0), (0.8, 40, 1.0, 0), (0.5, 1, 2.0, 1),
+    (1.3, 100000, 1.5, 2), (0.9, 5, 1.0, 3)])
+def test_sampler_bit_exact(pkg, O, V, temperature, top_k, penalty, ngram):
+    shape = (V, 8, 16, 1, 2)
+    _, _, be = make(pkg, O, shape, 1)
+    rng = np.random.default_rng(V + top_k)
+    cases = _rows_cases(V, rng)
+    if V == 7:  # all tokens banned -> pre-ban logits restored (Sampler.cs:156-164)
+        cases.append((np.arange(7, dtype=np.float32), np.arange(7, dtype=np.int32)))
+    logits = np.stack([c[0] for c in cases])
+    wins = [c[1] for c in cases]
+    uni = rng.random(len(cases))
+    with be:
+        got = be.sample_logits(logits, wins, temperature, top_k, uni, penalty, ngram)
+    for i, (lg, w) in enumerate(cases):
+        adj = lg
+        if penalty != 1.0 or ngram > 0:
+            adj = O.apply_repetition_controls(lg, w, penalty, ngram)
+        want = O.sample(adj, temperature, top_k, uni[i])
+        assert got[i] == want, f"row {i}: device {got[i]} oracle {want}"
+
+
+def test_sampler_reference_known_answers(pkg, O, golden):
+    """InferenceTests.cs:19-36 on the device sampler."""
+    for key in ("greedy_zero_temperature", "top_k_one_is_argmax"):
+        g = golden[key]
+        V = len(g["logits"])
+        _, _, be = make(pkg, O, (V, 8, 16, 1, 2), 1)
+        r = pkg.DotNetRandom(g["seed"])
+        with be:
+            for _ in range(5):
+                assert pkg.Sampler.sample(be, np.array(g["logits"], np.float32), g["temperature"], g["top_k"],
+                                          r) == g["expected"]
+
+
+# ---------------------------------------------------------------------------
+def check_ids(O, ocfg, params, prompt, got, want, tie=1e-4):
+    """Exact, or diverging only at an oracle near-tie."""
+    got, want = list(map(int, got)), list(map(int, want))
+    if got == want:
+        return
+    n = next(i for i in range(min(len(got), len(want))) if got[i] != want[i])
+    window = (list(prompt) + want[:n])[-ocfg.context_length:]
+    lg = O.forward_last(ocfg, params, window)
+    gap = abs(float(lg[got[n]]) - float(lg[want[n]]))
+    assert gap <= tie * max(1.0, abs(float(lg[want[n]]))), \
+        f"ids diverge at step {n} (device {got[n]}, oracle {want[n]}) with logit gap {gap}"
+
+
+def test_generate_c1_greedy_with_slide(pkg, O):
+    """tiny model, prompt 32, 256 greedy steps; the last
+    31 steps re-prefill the sliding window (Sampler.cs:93-94)."""
+    ocfg, params, be = make(pkg, O, C1, 1234)
+    prompt = np.random.default_rng(42).integers(0, C1[0], 32).astype(np.int32)
+    want = O.generate(ocfg, params, prompt, 256, 0.0, 0, O.DotNetRandom(1))
+    with be:
+        got = be.generate(prompt.tolist(), 256, 0.0, 0, None)
+        st = be.stats()
+    assert len(got) == 256
+    assert st["reprefills"] == 31
+    check_ids(O, ocfg, params, prompt, got, want)
+
+
+def test_generate_sampled_controls(pkg, O):
+    """Sampled decode with temperature, top-k, repetition penalty and
+    no-repeat-ngram (the Forge-98M bs1 options) on a small model."""
+    shape = (2256, 96, 128, 2, 4)
+    ocfg, params, be = make(pkg, O, shape, 5)
+    prompt = np.random.default_rng(1).integers(0, shape[0], 20).astype(np.int32)
+    want = O.generate(ocfg, params, prompt, 120, 0.7, 30, O.DotNetRandom(77), repetition_penalty=1.1,
+                      no_repeat_ngram=4)
+    r = pkg.DotNetRandom(77)
+    with be:
+        got = be.generate(prompt.tolist(), 120, 0.7, 30, r, repetition_penalty=1.1, no_repeat_ngram_size=4)
+    assert r.draws == len(got)  # one draw per sampled token (Sampler.cs:61)
+    check_ids(O, ocfg, params, prompt, got, want)
+
+
+def test_generate_batch_ragged_and_long_prompts(pkg, O):
+    shape = (300, 24, 32, 2, 2)
+    ocfg, params, be = make(pkg, O, shape, 9, max_seqs=5)
+    rng = np.random.default_rng(11)
+    prompts = [rng.integers(0, 300, L).astype(np.int32) for L in (1, 5, 23, 24, 40)]
+    seeds = [3, 4, 5, 6, 7]
+    with be:
+        got = be.generate_batch([p.tolist() for p in prompts], 30, 0.9, 20, seeds=seeds, repetition_penalty=1.2,
+                                no_repeat_ngram_size=2)
+    for i, p in enumerate(prompts):
+        want = O.generate(ocfg, params, p, 30, 0.9, 20, O.DotNetRandom(seeds[i]), repetition_penalty=1.2,
+                          no_repeat_ngram=2)
+        check_ids(O, ocfg, params, p, got[i], want)
+
+
+def test_generate_reference_behaviours(pkg, O, golden):
+    """InferenceTests.cs:80-112, 145-172 on the device path."""
+    g = golden["generate_count_in_range"]
+    ocfg, params, be = make(pkg, O, tuple(g["config"]), g["model_seed"])
+    with be:
+        out = be.generate(g["prompt"], g["max_new"], g["temperature"], g["top_k"], pkg.DotNetRandom(g["rng_seed"]))
+        assert len(out) == g["max_new"] and all(0 <= t < 32 for t in out)
+        want = O.generate(ocfg, params, g["prompt"], g["max_new"], 1.0, 0, O.DotNetRandom(g["rng_seed"]))
+        check_ids(O, ocfg, params, g["prompt"], out, want)
+        with pytest.raises(ValueError):
+            be.generate([1], 1, 1.0, 0, pkg.DotNetRandom(1), repetition_penalty=0.9)
+        with pytest.raises(ValueError):
+            be.generate([1], -1, 1.0, 0, pkg.DotNetRandom(1))
+        with pytest.raises(ValueError):
+            be.generate([], 1, 1.0, 0, pkg.DotNetRandom(1))
+        with pytest.raises(ValueError):
+            be.generate([32], 1, 0.0, 0, None)
+        with pytest.raises(ValueError):
+            be.generate([1], 1, 0.0, 0, None, eos_id=32)
+    g = golden["generate_slides_window"]
+    ocfg, params, be = make(pkg, O, tuple(g["config"]), g["model_seed"])
+    prompt = [i % 32 for i in range(g["prompt_len"])]
+    with be:
+        out = be.generate(prompt, g["max_new"], 0.0, 0, None)
+    assert len(out) == g["max_new"]
+    check_ids(O, ocfg, params, prompt, out, O.generate(ocfg, params, prompt, g["max_new"], 0.0, 0, O.DotNetRandom(1)))
+    g = golden["generate_stops_at_eos"]
+    ocfg, params, be = make(pkg, O, tuple(g["config"]), g["model_seed"])
+    with be:
+        first = be.generate(g["prompt"], 1, 0.0, 0, None)[0]
+        out = be.generate(g["prompt"], g["max_new"], 0.0, 0, None, eos_id=first)
+    assert out == [first]
+
+
+def test_streaming_callback_and_session_rng(pkg, O):
+    """Per-token callback in step order, early stop, and the session RNG
+    carried across calls (chat keeps one Random, Program.cs:730)."""
+    shape = (64, 32, 16, 1, 2)
+    ocfg, params, be = make(pkg, O, shape, 4)
+    seen = []
+    with be:
+        out = be.generate_batch([[1, 2, 3]], 10, 0.8, 0, seeds=[5],
+                                on_token=lambda s, st, t: (seen.append((s, st, t)), st == 6)[1])
+        assert [t for _, _, t in seen] == out[0].tolist() and len(out[0]) == 7
+        assert [st for _, st, _ in seen] == list(range(7))
+    r = O.DotNetRandom(5)
+    want = O.generate(ocfg, params, [1, 2, 3], 7, 0.8, 0, r)
+    check_ids(O, ocfg, params, [1, 2, 3], out[0], want)
