@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--new-tokens", type=int, default=None, help="override the workload's new-token count "
+                    "(smaller cases for profiling; the default is the workload's)")
+    ap.add_argument("--skip-e2e", action="store_true", help="omit the host-buffer e2e leg (profiling runs)")
     return ap.parse_args()
 
 
@@ -189,7 +192,10 @@ def run_reference(args, wl):
 
 def main():
     args = parse()
-    wl = WORKLOADS[args.workload]
+    wl = dict(WORKLOADS[args.workload])
+    if args.new_tokens:
+        wl["new_tokens"] = args.new_tokens
+        wl["name"] += f" [new tokens overridden: {args.new_tokens}]"
     if args.impl == "reference":
         run_reference(args, wl)
         return
@@ -299,6 +305,8 @@ def main():
     peak = float(peaks.get("hbm_gbs", 6650.0))
 
     # ---- e2e: the public host-buffer call, copies inside the timed region ----
+    if args.skip_e2e:
+        step_host = step_device
     step_host()
     barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -307,6 +315,8 @@ def main():
         res = step_host()
     b.record(stream)
     barrier()
+    if args.skip_e2e:
+        res = [d_out[i, :int(c)].cpu().numpy() for i, c in enumerate(d_cnt.cpu().numpy())]
     e2e_ms = max_over_ranks(a.elapsed_time(b))
     e2e_tokens = sum(len(r) for r in res) * args.steps * (world if wl["seqs_total"] is None else 1)
     if wl["seqs_total"] is not None and world > 1:

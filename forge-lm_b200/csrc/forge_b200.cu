@@ -139,9 +139,15 @@ static std::vector<long long> param_numels(const fb2_model_desc& d) {
 // ---------------------------------------------------------------------------
 // kernel launch configuration (per device, set once)
 // ---------------------------------------------------------------------------
-static void configure_kernels() {
-    auto setmax = [](const void* f, int bytes) {
-        CK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+// Opts every kernel that takes dynamic shared memory into the device maximum
+// (the opt-in limit covers static + dynamic shared memory of a block).
+static void configure_kernels(int dev) {
+    int optin = 0;
+    CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    auto setmax = [optin](const void* f, int) {
+        cudaFuncAttributes a;
+        CK(cudaFuncGetAttributes(&a, f));
+        CK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)a.sharedSizeBytes));
     };
     setmax((const void*)k_gemv<1>, 227 * 1024);
     setmax((const void*)k_gemv<2>, 227 * 1024);
@@ -945,7 +951,7 @@ int32_t fb2_model_create(const fb2_model_desc* desc, const float* const* params,
                 cudaDeviceProp prop;
                 CK(cudaGetDeviceProperties(&prop, dev));
                 if (prop.major != 10) fail(FB2_UNSUPPORTED, "this build targets sm_100a (B200) only");
-                configure_kernels();
+                configure_kernels(dev);
                 DeviceModel dm;
                 dm.device = dev;
                 dm.sm_count = prop.multiProcessorCount;
