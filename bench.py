@@ -217,7 +217,11 @@ def main():
     params = pkg.init_params(cfg, WEIGHT_SEED)
     be = pkg.B200Backend(cfg, params, devices=[local], max_seqs=max(count, 1))
     del params
-    stream = torch.cuda.current_stream()
+    # a real (non-legacy) stream: its handle is what the library launches on,
+    # and the CUDA events below are recorded on the same stream
+    stream = torch.cuda.Stream(device=local)
+    torch.cuda.set_stream(stream)
+    assert stream.cuda_stream != 0
     be.set_stream(stream.cuda_stream)
     plen, new = wl["prompt_len"], wl["new_tokens"]
     prompts = prompts_for(first, count, plen, m["vocab_size"])

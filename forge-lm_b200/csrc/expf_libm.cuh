@@ -14,9 +14,11 @@
 namespace fb2 {
 
 __device__ __forceinline__ float expf_libm(float x) {
+    if (x == -INFINITY) return 0.0f;  // both sides return +0
     float r = (float)exp((double)x);
     uint32_t b = __float_as_uint(x);
-    uint32_t lo = 0, hi = FB2_EXPF_FIXUP_COUNT;
+    // the bucket of the top 16 input bits bounds the search to a few entries
+    uint32_t lo = __ldg(&kExpfFixupBucket[b >> 16]), hi = __ldg(&kExpfFixupBucket[(b >> 16) + 1]);
     while (lo < hi) {
         uint32_t mid = (lo + hi) >> 1;
         uint32_t k = kExpfFixupData[2 * mid];

@@ -102,9 +102,17 @@ FB2_DEV float block_kth_largest(const float* vals, int V, int k, uint32_t* hist)
         for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
         __syncthreads();
         const uint32_t prefix = s_prefix, mask = s_mask;
-        for (int i = threadIdx.x; i < V; i += blockDim.x) {
-            uint32_t key = float_key(vals[i]);
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        // warp-aggregated histogram: logits cluster in few bins, so lanes with
+        // the same digit add once (every lane runs the same trip count)
+        for (int base = 0; base < V; base += blockDim.x) {
+            const int i = base + threadIdx.x;
+            uint32_t digit = 256u;
+            if (i < V) {
+                uint32_t key = float_key(vals[i]);
+                if ((key & mask) == prefix) digit = (key >> shift) & 255u;
+            }
+            const unsigned grp = __match_any_sync(0xffffffffu, digit);
+            if (digit < 256u && (threadIdx.x & 31) == __ffs(grp) - 1) atomicAdd(&hist[digit], (uint32_t)__popc(grp));
         }
         __syncthreads();
         if (threadIdx.x < 32) {
