@@ -31,7 +31,7 @@ EXPORTED = [
     "fb2_version", "fb2_last_error", "fb2_device_count", "fb2_model_create", "fb2_model_destroy",
     "fb2_session_create", "fb2_session_destroy", "fb2_session_seed", "fb2_session_set_stream",
     "fb2_generate", "fb2_generate_device", "fb2_forward_last_logits", "fb2_teacher_forced_logits",
-    "fb2_sample_logits", "fb2_init_params", "fb2_stats", "fb2_stats_reset",
+    "fb2_sample_logits", "fb2_forward_last_logits_noalloc", "fb2_init_params", "fb2_stats", "fb2_stats_reset",
 ]
 TEST_EXPORTED = ["fb2_test_expf", "fb2_test_expf_hash", "fb2_test_dotnet_random"]
 
@@ -95,6 +95,7 @@ def load(path: str | None = None):
     L.fb2_teacher_forced_logits.argtypes = [vp, i32, i32p, i32, i32, f32p]
     L.fb2_sample_logits.argtypes = [vp, i32, f32p, i32p, i32p, C.POINTER(Sampling), f64p, i32p]
     L.fb2_init_params.argtypes = [C.POINTER(ModelDesc), i32, C.POINTER(vp), i32]
+    L.fb2_forward_last_logits_noalloc.argtypes = [vp, i32, i32, vp, vp, vp]
     L.fb2_stats.argtypes = [vp, C.POINTER(Stats)]
     L.fb2_stats_reset.argtypes = [vp]
     L.fb2_test_expf.argtypes = [f32p, f32p, i64]

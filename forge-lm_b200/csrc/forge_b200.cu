@@ -886,6 +886,72 @@ static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
 }
 
 // ---------------------------------------------------------------------------
+// Scratch for fb2_forward_last_logits_noalloc: one file-scope device array
+// (8 MiB on every GPU that loads this library, held until the process
+// exits).  Host code must not use `g_noalloc_scratch` as a pointer: its
+// device address comes from cudaGetSymbolAddress, taken once per device.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoallocScratchFloats = (size_t)2 << 20;  // 8 MiB
+constexpr int kNoallocMaxRows = 16;                         // window length limit
+static __device__ __align__(256) float g_noalloc_scratch[kNoallocScratchFloats];
+
+namespace {
+std::mutex g_noalloc_mutex;
+float* g_noalloc_ptr[256] = {};  // device address of the scratch, per device ordinal
+
+// Layout of the scratch for one window of n <= kNoallocMaxRows tokens.
+struct NoallocLayout {
+    size_t x, x2, ln, q, att, h, lnf, kv, part, tickets, ints, total;
+};
+NoallocLayout noalloc_layout(const fb2_model& m) {
+    auto up = [](size_t v) { return (v + 63) / 64 * 64; };  // 256-byte aligned regions
+    const size_t R = kNoallocMaxRows, D = m.D, F = m.F;
+    NoallocLayout L{};
+    size_t o = 0;
+    L.x = o; o += up(R * D);
+    L.x2 = o; o += up(R * D);
+    L.ln = o; o += up(R * D);
+    L.q = o; o += up(R * D);
+    L.att = o; o += up(R * D);
+    L.h = o; o += up(R * F);
+    L.lnf = o; o += up((size_t)kMaxChunkSlots * D);
+    L.kv = o; o += up((size_t)m.L * 2 * m.H * R * m.hd);
+    L.part = o; o += up((size_t)512 * 1024);
+    L.tickets = o; o += up(4096);
+    L.ints = o; o += up(8 * R + 64);
+    L.total = o;
+    return L;
+}
+}  // namespace
+
+// Window tables for one sequence of n tokens: rows 0..n-1 at positions
+// 0..n-1, one query block, last row n-1 written to output row 0; tickets
+// cleared (the array keeps the previous call's contents).
+__global__ void k_noalloc_tables(int n, int* ints, unsigned int* tickets) {
+    int* row_seq = ints;
+    int* row_pos = ints + kNoallocMaxRows;
+    int* hidx = ints + 2 * kNoallocMaxRows;
+    int* ones = ints + 3 * kNoallocMaxRows;
+    int4* qblk = reinterpret_cast<int4*>(ints + 4 * kNoallocMaxRows);
+    int* last_row = ints + 4 * kNoallocMaxRows + 4;
+    int* out_slot = last_row + 1;
+    int* len = last_row + 2;
+    for (int i = threadIdx.x; i < 4096; i += blockDim.x) tickets[i] = 0u;
+    for (int i = threadIdx.x; i < kNoallocMaxRows; i += blockDim.x) {
+        row_seq[i] = 0;
+        row_pos[i] = i;
+        hidx[i] = i;
+        ones[i] = 1;
+    }
+    if (threadIdx.x == 0) {
+        *qblk = make_int4(0, n, 0, 0);
+        *last_row = n - 1;
+        *out_slot = 0;
+        *len = n;
+    }
+}
+
+// ---------------------------------------------------------------------------
 // C ABI
 // ---------------------------------------------------------------------------
 extern "C" {
@@ -1432,6 +1498,86 @@ int32_t fb2_stats_reset(fb2_session* S) {
             s->stats = fb2_stats_t{};
             s->stats.device_count = dc;
         }
+    });
+}
+
+// ---- forward_last without allocation --------------------------------------
+// ForwardLast of one window through the same prefill kernels as
+// fb2_forward_last_logits, with every intermediate (activations, a KV cache
+// sized for the window, split-K partial sums and tickets, row tables) in
+// g_noalloc_scratch.  No cudaMalloc/cudaFree, no host staging: tokens and
+// logits are the caller's device buffers, work is enqueued on the caller's
+// stream and the call returns without waiting.
+int32_t fb2_forward_last_logits_noalloc(fb2_model* m, int32_t device_slot, int32_t n_tokens,
+                                        const int32_t* device_tokens, float* device_logits, void* cuda_stream) {
+    return guarded([&] {
+        if (!m || !device_tokens || !device_logits) fail(FB2_INVALID_ARG, "NULL argument");
+        if (device_slot < 0 || device_slot >= (int)m->devs.size()) fail(FB2_INVALID_ARG, "device slot out of range");
+        if (n_tokens < 1) fail(FB2_INVALID_ARG, "Need at least one token.");
+        if (n_tokens > kNoallocMaxRows || n_tokens > m->ctx)
+            fail(FB2_INVALID_ARG, "fb2_forward_last_logits_noalloc: window of " + std::to_string(n_tokens) +
+                                      " tokens exceeds its limit of " + std::to_string(kNoallocMaxRows) +
+                                      " (and the context length)");
+        const NoallocLayout lay = noalloc_layout(*m);
+        if (lay.total > kNoallocScratchFloats)
+            fail(FB2_UNSUPPORTED, "fb2_forward_last_logits_noalloc: this model needs " +
+                                      std::to_string(lay.total * 4) + " bytes of scratch; the library reserves " +
+                                      std::to_string(kNoallocScratchFloats * 4));
+        const DeviceModel& dm = m->devs[device_slot];
+        DeviceGuard g(dm.device);
+        float* base = nullptr;
+        {
+            std::lock_guard<std::mutex> lk(g_noalloc_mutex);
+            if (dm.device < 0 || dm.device >= 256) fail(FB2_UNSUPPORTED, "device ordinal out of range");
+            if (!g_noalloc_ptr[dm.device]) {
+                // first call on this device: resolve the array's device address
+                // (with this device current)
+                CK(cudaGetSymbolAddress((void**)&g_noalloc_ptr[dm.device], g_noalloc_scratch));
+            }
+            base = g_noalloc_ptr[dm.device];
+        }
+        // A model view whose context is the window limit: the KV cache in the
+        // scratch holds kNoallocMaxRows positions per head.
+        fb2_model view;
+        view.desc = m->desc;
+        view.V = m->V; view.ctx = kNoallocMaxRows; view.D = m->D; view.L = m->L;
+        view.H = m->H; view.hd = m->hd; view.F = m->F;
+        DeviceSession s;
+        s.model = &view;
+        s.dm = &dm;
+        s.device = dm.device;
+        s.nslots = 0;  // head output goes straight to device_logits (row 0)
+        s.stream = static_cast<cudaStream_t>(cuda_stream);
+        s.d_x = base + lay.x; s.d_x2 = base + lay.x2; s.d_ln = base + lay.ln; s.d_q = base + lay.q;
+        s.d_att = base + lay.att; s.d_h = base + lay.h; s.d_lnf = base + lay.lnf;
+        s.d_kv = base + lay.kv;
+        s.kv_layer_stride = 2LL * view.H * view.ctx * view.hd;
+        s.v_offset = (long long)view.H * view.ctx * view.hd;
+        s.kv_slot_stride = s.kv_layer_stride * view.L;
+        s.d_gemv_part = base + lay.part;
+        s.gemv_part_cap = (size_t)512 * 1024;
+        s.d_tickets = reinterpret_cast<unsigned int*>(base + lay.tickets);
+        int* ints = reinterpret_cast<int*>(base + lay.ints);
+        s.d_row_hidx = ints + 2 * kNoallocMaxRows;
+        s.d_ones = ints + 3 * kNoallocMaxRows;
+        s.d_len = ints + 4 * kNoallocMaxRows + 6;
+        s.d_hist = const_cast<int*>(device_tokens);
+        s.hist_cap = n_tokens;
+        s.d_logits = device_logits;
+        k_noalloc_tables<<<1, 256, 0, s.stream>>>(n_tokens, ints, s.d_tickets);
+        // the prefill chunk of run_prefill_chunk, for this single window
+        const int* row_seq = ints;                    // slot 0 for every row
+        const int* row_pos = ints + kNoallocMaxRows;  // positions 0..n-1
+        const int4* qblk = reinterpret_cast<const int4*>(ints + 4 * kNoallocMaxRows);
+        const int* last_row = ints + 4 * kNoallocMaxRows + 4;
+        k_prefill_hidx<<<1, 256, 0, s.stream>>>(n_tokens, row_seq, row_pos, s.d_len, view.ctx, s.d_row_hidx);
+        Rows R{row_seq, row_pos, s.d_row_hidx, s.d_ones};
+        k_embed<<<n_tokens, 128, 0, s.stream>>>(n_tokens, R, s.d_hist, s.hist_cap, dm.tok_emb, dm.pos_emb, view.D,
+                                                view.V, s.d_x);
+        run_layers(s, n_tokens, R, false, 1, qblk);
+        launch_layernorm(s, 1, s.d_x, dm.lnf_w, dm.lnf_b, s.d_lnf, last_row);
+        launch_head(s, 1, s.d_lnf, nullptr, device_logits);
+        CK(cudaGetLastError());
     });
 }
 

@@ -187,6 +187,31 @@ int32_t fb2_sample_logits(fb2_session* s, int32_t n, const float* logits, const 
                           const int32_t* window_lens, const fb2_sampling* sp, const double* uniforms,
                           int32_t* out_ids);
 
+/* ---- forward_last without device allocation -----------------------------------
+ * No counterpart in the reference: an addition for callers that cannot call
+ * cudaMalloc — code that runs while a CUDA stream is being captured, a host
+ * runtime that already owns the device's memory budget through its own
+ * allocator, or a latency-critical path where cudaMalloc's implicit device
+ * synchronisation is not acceptable.
+ *
+ * Computes what fb2_forward_last_logits computes for ONE window of n_tokens
+ * (1 <= n_tokens <= 16, and <= context_length) on the model copy of
+ * device_slot: device_tokens (n_tokens int32) and device_logits (vocab_size
+ * floats) are the caller's device buffers on that device.  All intermediate
+ * data lives in a fixed 8 MiB device array inside the library (reserved on
+ * every GPU that loads it, until the process exits); the call allocates
+ * nothing, enqueues its kernels on cuda_stream (a cudaStream_t as void*) and
+ * returns without waiting.  Models whose intermediates exceed the 8 MiB
+ * (roughly d_model > 1024 or many layers) are rejected with FB2_UNSUPPORTED;
+ * longer windows with FB2_INVALID_ARG.  Token ids are not range-checked on
+ * the host (they stay on the device); ids outside [0, vocab) read as id 0.
+ * The first call on a device looks up the array's device address; make that
+ * first call before any stream capture begins.  Every call shares the one
+ * array: calls whose work overlaps on the GPU (different streams, or other
+ * host threads) race and corrupt each other's results. */
+int32_t fb2_forward_last_logits_noalloc(fb2_model* m, int32_t device_slot, int32_t n_tokens,
+                                        const int32_t* device_tokens, float* device_logits, void* cuda_stream);
+
 /* ---- synthetic weights -------------------------------------------------------
  * Host-only: fills params[i] (caller-allocated fp32 arrays of the sizes listed
  * at fb2_model_create) with the weights `new GptModel(config, backend,
