@@ -1,0 +1,1513 @@
+// decode_mega.cuh — persistent decode kernel for up to 8 sequences (sm_100a).
+//
+// One launch runs `nsteps` KV-cached decode steps of the reference token loop
+// (Sampler.Generate, src/LLM.Core/Inference/Sampler.cs:91-108) for MR rows:
+// embed -> L x [LN1 -> QKV -> attention -> proj+res -> LN2 -> fc+GELU ->
+// proj+res] -> LN_f -> tied head -> repetition controls -> Sample.
+//
+// Structure (grid = one CTA per SM, 288 threads):
+//   thread 256      producer: streams every weight tile of this CTA and the
+//                   K/V chunks of its attention units, in consumption order,
+//                   with cp.async.bulk (TMA, no multicast) into a ring of
+//                   16 KB shared-memory stages guarded by mbarriers.  It
+//                   never waits for activations, so HBM stays busy across
+//                   phase and step boundaries.
+//   threads 0-255   consumers: compute on the staged tiles.
+// Work split: every projection W[K][N] is split by output columns over the
+// CTAs (column strip [K][w] per CTA, re-laid contiguously at model load);
+// the head splits the vocabulary rows; attention splits (row, head, key
+// chunk) units over the CTAs.
+// Cross-CTA data (q, current K/V, attention partials, x2, h, x, candidate
+// counts) is published as 64-bit (tag << 32 | value) words: a reader spins
+// on the word itself, so the poll is the data load.  Tags are unique per
+// (global step, layer).  Every wait is bounded (2 s); on expiry the kernel
+// records an error and all threads leave together at the next check point.
+// Sampling is distributed: each CTA applies the repetition controls to its
+// vocabulary slice and publishes its local top-k with ties (every entry >=
+// the global k-th largest is in some CTA's list), then every CTA computes
+// the same token from the union; CTA 0 writes the bookkeeping.
+#pragma once
+#include "common.cuh"
+#include "expf_libm.cuh"
+#include "sampler.cuh"
+
+namespace fb2 {
+
+constexpr int MK_THREADS = 288;
+constexpr int MK_CONS = 256;
+constexpr int MK_STAGE = 16384;  // bytes per ring stage
+constexpr int MK_MAX_ROWS = 8;
+constexpr int MK_SLICE_MAX = 256;
+constexpr int MK_SURV_MAX = 512;
+constexpr int MK_MAX_TOPK = 64;
+constexpr unsigned long long MK_TIMEOUT_NS = 2000000000ull;
+
+enum MkPhase { MK_QKV = 0, MK_PROJ = 1, MK_FC = 2, MK_PROJ2 = 3 };
+
+struct MkLayer {
+    const float* w[4];  // re-laid column strips
+    const float* b[4];
+    const float *ln1w, *ln1b, *ln2w, *ln2b;
+};
+
+struct MkArgs {
+    int V, ctx, D, L, H, hd, F, nW, nstage, slice_max;
+    const MkLayer* layers;
+    const float *tok_emb, *pos_emb, *lnf_w, *lnf_b;
+    float* kv;
+    long long kv_slot_stride, kv_layer_stride, v_offset;
+    int* hist;
+    int hist_stride;
+    int* len;
+    int* count;
+    int* done;
+    const double* uniforms;
+    int uni_stride;
+    int* out_tokens;
+    int out_stride;
+    float* logits_out;  // [MR][V] raw logits of the last step
+    SampleParams sp;
+    int n_rows;
+    const int* row_slot;  // [n_rows]
+    int bookkeep;         // 0: teacher forcing (no history / output writes)
+    unsigned long long *xq, *xkv, *xx2, *xh, *xx, *xpart, *cand_hdr;
+    float* xacc;  // [units][hd] attention partial sums (published by xpart's release)
+    int maxc;     // max key chunks per (row, head)
+    float* cand_val;
+    int* cand_idx;
+    unsigned int* stepdone;
+    int* err;
+    unsigned int gstep0;
+    int nsteps;
+    unsigned long long* trace;  // optional: [nW][trace_steps][MK_TRACE_POINTS] %globaltimer stamps
+    int trace_steps;
+};
+
+// Trace points per step: 12 per layer for layers 0 and 1 (level A start, after
+// LN1, after QKV, after attention units, after combine weights, after ctx,
+// after proj, after x2 gather, after LN2, after fc, after h gather, after
+// proj2), 24 step start, 25 head input, 27 head logits, 28 candidates,
+// 30 published, 31 token known, 32 step end, 33 + l end of layer l.
+constexpr int MK_TRACE_POINTS = 64;
+
+// ---- small PTX helpers ------------------------------------------------------
+FB2_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+FB2_DEV unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+FB2_DEV void mbar_init(uint64_t* b, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+FB2_DEV void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+FB2_DEV void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+FB2_DEV bool mbar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+FB2_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+FB2_DEV void cons_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Barrier of the 256 consumer threads that also ORs `pred` over them.
+FB2_DEV int cons_sync_or(int pred) {
+    int r;
+    asm volatile(
+        "{ .reg .pred p, q; setp.ne.s32 p, %1, 0; bar.red.or.pred q, 1, 256, p; selp.s32 %0, 1, 0, q; }"
+        : "=r"(r)
+        : "r"(pred)
+        : "memory");
+    return r;
+}
+FB2_DEV void st_pair(unsigned long long* p, float v, uint32_t tag) {
+    unsigned long long w = ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+FB2_DEV unsigned long long ld_pair(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+FB2_DEV unsigned int ld_acquire_u32(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+FB2_DEV void fence_acq_rel() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+FB2_DEV uint32_t mk_tag(unsigned int gs, int layer, int L) { return gs * (unsigned)(L + 1) + (unsigned)layer + 1u; }
+
+// Column strip of CTA c for an N-column projection (balanced split).
+FB2_DEV void strip(int N, int nW, int c, int& n0, int& w) {
+    n0 = (int)(((long long)c * N) / nW);
+    w = (int)(((long long)(c + 1) * N) / nW) - n0;
+}
+// Rows of a [K][w] strip per 16 KB stage (a multiple of 4 so every chunk is a
+// multiple of 16 bytes).
+FB2_DEV int strip_rows(int w, int K) {
+    if (w <= 0) return 0;
+    int R = (MK_STAGE / 4 / w) & ~3;
+    return R < K ? R : K;
+}
+
+// Spins until word p carries `tag` and returns its value.  On timeout sets
+// the error and the CTA's abort flag; after an abort it stops waiting.
+FB2_DEV float wait_pair(const unsigned long long* p, uint32_t tag, int* err, volatile int* abort_flag) {
+    unsigned long long w = ld_pair(p);
+    if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
+    const unsigned long long t0 = gtimer();
+    while (true) {
+        __nanosleep(40);  // back off: waiting threads must not crowd L2 out for the weight stream
+        w = ld_pair(p);
+        if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
+        if (*abort_flag) return 0.f;
+        if (gtimer() - t0 > MK_TIMEOUT_NS) {
+            atomicExch(err, 1);
+            *abort_flag = 1;
+            return 0.f;
+        }
+    }
+}
+// Resolves a word already loaded: returns its value if the tag matches, else
+// keeps polling the address.
+FB2_DEV float resolve_pair(unsigned long long w, const unsigned long long* p, uint32_t tag, int* err,
+                           volatile int* abort_flag) {
+    if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
+    return wait_pair(p, tag, err, abort_flag);
+}
+// Waits until every word k with bit k of `pend` set carries `tag`.  w[k]
+// holds a first load of word addr(k); each retry reloads every word still
+// pending, so a late batch costs its arrival time plus one round trip (not
+// one round trip per word).
+template <int N, class Addr>
+FB2_DEV void resolve_batch(unsigned long long* w, uint32_t pend, Addr addr, uint32_t tag, int* err,
+                           volatile int* abort_flag) {
+    unsigned long long t0 = 0;
+    while (true) {
+        uint32_t still = 0;
+#pragma unroll
+        for (int k = 0; k < N; k++)
+            if (((pend >> k) & 1u) && (uint32_t)(w[k] >> 32) != tag) still |= 1u << k;
+        if (!still || *abort_flag) return;
+        const unsigned long long now = gtimer();
+        if (!t0) t0 = now;
+        else if (now - t0 > MK_TIMEOUT_NS) {
+            atomicExch(err, 1);
+            *abort_flag = 1;
+            return;
+        }
+        __nanosleep(32);
+#pragma unroll
+        for (int k = 0; k < N; k++)
+            if ((still >> k) & 1u) w[k] = ld_pair(addr(k));
+        pend = still;
+    }
+}
+FB2_DEV float pair_value(unsigned long long w) { return __uint_as_float((uint32_t)w); }
+
+// dst[i] = value of src[i] for i < n once every word carries `tag`: each
+// thread loads up to 16 words, then waits on them together.
+FB2_DEV void gather_tagged(const unsigned long long* src, float* dst, int n, uint32_t tag, int* err,
+                           volatile int* abort_flag) {
+    for (int base = 0; base < n; base += 16 * MK_CONS) {
+        unsigned long long w[16];
+        uint32_t pend = 0;
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            const int i = base + k * MK_CONS + (int)threadIdx.x;
+            w[k] = 0ull;
+            if (i < n) {
+                w[k] = ld_pair(src + i);
+                pend |= 1u << k;
+            }
+        }
+        resolve_batch<16>(w, pend, [&](int k) { return src + base + k * MK_CONS + (int)threadIdx.x; }, tag, err,
+                          abort_flag);
+#pragma unroll
+        for (int k = 0; k < 16; k++)
+            if ((pend >> k) & 1u) dst[base + k * MK_CONS + threadIdx.x] = pair_value(w[k]);
+    }
+}
+FB2_DEV void st_pair_release(unsigned long long* p, float v, uint32_t tag) {
+    unsigned long long w = ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+FB2_DEV unsigned long long ld_pair_acquire(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+// Acquire-polls a header word until it carries `tag`.
+FB2_DEV float wait_pair_acquire(const unsigned long long* p, uint32_t tag, int* err, volatile int* abort_flag) {
+    const unsigned long long t0 = gtimer();
+    for (int n = 0;; n++) {
+        if (n) __nanosleep(40);
+        const unsigned long long w = ld_pair_acquire(p);
+        if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
+        if (*abort_flag) return 0.f;
+        if (gtimer() - t0 > MK_TIMEOUT_NS) {
+            atomicExch(err, 1);
+            *abort_flag = 1;
+            return 0.f;
+        }
+    }
+}
+// Exclusive prefix sum over the 256 consumer threads (wsum: 8 ints of shared scratch).
+FB2_DEV int cons_excl_scan(int v, int* wsum, int& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += t;
+    }
+    if (lane == 31) wsum[warp] = x;
+    cons_sync();
+    int base = 0, tot = 0;
+#pragma unroll
+    for (int w8 = 0; w8 < 8; w8++) {
+        const int t = wsum[w8];
+        if (w8 < warp) base += t;
+        tot += t;
+    }
+    cons_sync();
+    total = tot;
+    return base + x - v;
+}
+// Warp 0: the bin (counted from the top of a 256-bin histogram) that holds the
+// k-th largest key, and the count in the bins above it.
+FB2_DEV void radix_pick(const uint32_t* hist, int kk, int& bin, int& above_out) {
+    const int lane = threadIdx.x & 31;
+    uint32_t c[8], local = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        c[j] = hist[lane * 8 + j];
+        local += c[j];
+    }
+    uint32_t incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_down_sync(0xffffffffu, incl, o);
+        if (lane + o < 32) incl += t;
+    }
+    const uint32_t above = incl - local;
+    int found = -1;
+    uint32_t na = 0;
+    if ((int)above < kk && (int)incl >= kk) {
+        uint32_t acc = above;
+#pragma unroll
+        for (int j = 7; j >= 0; j--)
+            if (found < 0) {
+                if ((int)(acc + c[j]) >= kk) {
+                    found = lane * 8 + j;
+                    na = acc;
+                } else acc += c[j];
+            }
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, found >= 0);
+    const int src = bal ? __ffs(bal) - 1 : 0;
+    bin = __shfl_sync(0xffffffffu, found, src);
+    above_out = (int)__shfl_sync(0xffffffffu, na, src);
+    if (bin < 0) bin = 0;
+}
+
+FB2_DEV void wait_full(uint64_t* full, uint32_t it, int nstage, int* err, volatile int* abort_flag) {
+    uint64_t* b = &full[it % nstage];
+    const uint32_t par = (it / nstage) & 1u;
+    if (mbar_try(b, par)) return;
+    const unsigned long long t0 = gtimer();
+    while (!mbar_try(b, par)) {
+        if (*abort_flag) return;
+        if (gtimer() - t0 > MK_TIMEOUT_NS) {
+            atomicExch(err, 2);
+            *abort_flag = 1;
+            return;
+        }
+    }
+}
+
+FB2_DEV void release_stage(uint64_t* empty, uint32_t it, int nstage) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[it % nstage]);
+}
+
+// Sum over the 256 consumer threads through shared scratch `scr` (8 floats).
+FB2_DEV float cons_sum(float v, float* scr) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) scr[threadIdx.x >> 5] = v;
+    cons_sync();
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) t += scr[i];
+    cons_sync();
+    return t;
+}
+
+// LayerNorm parameters of this thread's columns (tid + 256*k), loaded ahead
+// of use so their latency hides behind the wait for the input vector.
+struct LnRegs {
+    float w[8], b[8];
+};
+FB2_DEV LnRegs ln_prefetch(const float* w, const float* b, int D) {
+    LnRegs r;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int i = threadIdx.x + k * MK_CONS;
+        r.w[k] = i < D ? __ldg(w + i) : 0.f;
+        r.b[k] = i < D ? __ldg(b + i) : 0.f;
+    }
+    return r;
+}
+// Sum over the 256 consumer threads into a dedicated 8-float slot (no
+// trailing barrier: each call site uses its own slot).
+FB2_DEV float cons_sum_slot(float v, float* slot) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) slot[threadIdx.x >> 5] = v;
+    cons_sync();
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) t += slot[i];
+    return t;
+}
+// Two-pass LayerNorm of MR rows of length D <= 2048 from src into dst
+// (shared), CpuBackend.cs:377-398.  `slots` = 16*MR floats of scratch that
+// stay untouched until the next barrier-separated phase.
+template <int MR>
+FB2_DEV void mk_layernorm(const float* src, float* dst, int D, const LnRegs& p, float* slots) {
+#pragma unroll 1
+    for (int m = 0; m < MR; m++) {
+        const float* x = src + m * D;
+        float xv[8];
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int i = threadIdx.x + k * MK_CONS;
+            xv[k] = i < D ? x[i] : 0.f;
+            s += xv[k];
+        }
+        const float mu = cons_sum_slot(s, slots + 16 * m) / (float)D;
+        float q = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int i = threadIdx.x + k * MK_CONS;
+            const float d = i < D ? xv[k] - mu : 0.f;
+            q += d * d;
+        }
+        const float rs = 1.0f / sqrtf(cons_sum_slot(q, slots + 16 * m + 8) / (float)D + kLnEps);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int i = threadIdx.x + k * MK_CONS;
+            if (i < D) dst[m * D + i] = (xv[k] - mu) * rs * p.w[k] + p.b[k];
+        }
+    }
+    cons_sync();
+}
+
+// Shared-memory bytes the kernel needs besides the ring.
+inline size_t mk_aux_bytes(int MR, int D, int F, int H, int ctx, int slice_max, int maxc, int nstage) {
+    size_t floats = (size_t)MR * F + 2 * (size_t)MR * D + (size_t)MR * 256 + (size_t)MR * slice_max + 512;
+    size_t ints = 2048 + (size_t)MR * ctx;
+    size_t wts = 2 * (size_t)MR * H * maxc;
+    return 2 * (size_t)nstage * 8 + floats * 4 + ints * 4 + MK_SURV_MAX * 8 + wts * 4;
+}
+
+#define MK_TRACE(pt)                                                                                 \
+    do {                                                                                             \
+        if (a.trace && tid == 0 && s < a.trace_steps && (pt) < MK_TRACE_POINTS)                     \
+            a.trace[((size_t)cta * a.trace_steps + s) * MK_TRACE_POINTS + (pt)] = gtimer();          \
+    } while (0)
+#define MK_TRACE_L(off)                  \
+    do {                                 \
+        if (l < 2) MK_TRACE(l * 12 + (off)); \
+    } while (0)
+
+// ---- the kernel ---------------------------------------------------------------
+template <int MR>
+__global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
+    extern __shared__ __align__(128) unsigned char mk_smem_raw[];
+    const int tid = threadIdx.x;
+    const int cta = blockIdx.x, nW = a.nW;
+    const int D = a.D, F = a.F, L = a.L, H = a.H, hd = a.hd, V = a.V;
+    const int KC = MK_STAGE / (hd * 4);  // keys per attention chunk
+    unsigned char* ring = mk_smem_raw;
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)a.nstage * MK_STAGE);
+    uint64_t* empty = full + a.nstage;
+    float* act = reinterpret_cast<float*>(empty + a.nstage);  // [MR][F]
+    float* xres = act + MR * F;                                // [MR][D]
+    float* x2res = xres + MR * D;                              // [MR][D]
+    float* red = x2res + MR * D;                               // [MR][256]
+    float* slice = red + MR * 256;                             // [MR][slice_max]
+    float* scr = slice + MR * a.slice_max;                     // [512]
+    int* iscr = reinterpret_cast<int*>(scr + 512);             // [2048]
+    int* win = iscr + 2048;                                    // [MR][ctx]
+    float* surv_v = reinterpret_cast<float*>(win + MR * a.ctx);  // [MK_SURV_MAX]
+    int* surv_i = reinterpret_cast<int*>(surv_v + MK_SURV_MAX);  // [MK_SURV_MAX]
+    float* wts_m = reinterpret_cast<float*>(surv_i + MK_SURV_MAX);  // [MR*H][maxc] chunk weights
+    float* wts_l = wts_m + (size_t)MR * H * a.maxc;                 // [MR*H][maxc] chunk sums
+    // iscr regions
+    uint32_t* seen = reinterpret_cast<uint32_t*>(iscr);  // [8] bits of the slice
+    uint32_t* ban = seen + 8;                            // [8]
+    int* wbi = iscr + 16;                                // [8] per-warp argmax index
+    int* rcnt = iscr + 32;                               // [8] candidates per row
+    int* rtok = iscr + 48;                               // [8] token per row
+    int* misc = iscr + 64;                               // [64]
+    int* flag = iscr + 256;                              // [256]
+    int* cnts = iscr + 512;                              // [256]
+    int* offs = iscr + 768;                              // [257]
+
+    __shared__ int s_slot[MK_MAX_ROWS], s_pos0[MK_MAX_ROWS], s_tok[MK_MAX_ROWS], s_cnt0[MK_MAX_ROWS];
+    __shared__ int s_len0[MK_MAX_ROWS], s_dead[MK_MAX_ROWS], s_dummy[MK_MAX_ROWS], s_ubase[MK_MAX_ROWS + 1];
+    __shared__ volatile int s_abort;
+
+    if (tid < MR) {
+        const int m = tid;
+        const bool dummy = m >= a.n_rows;
+        const int slot = a.row_slot[dummy ? 0 : m];
+        const int len = a.len[slot];
+        s_slot[m] = slot;
+        s_dummy[m] = dummy;
+        s_len0[m] = dummy ? 1 : len;
+        s_pos0[m] = dummy ? 0 : len - 1;
+        s_tok[m] = dummy ? 0 : a.hist[(size_t)slot * a.hist_stride + len - 1];
+        s_cnt0[m] = dummy ? 0 : a.count[slot];
+        s_dead[m] = dummy ? 1 : a.done[slot];
+    }
+    if (tid == 0) {
+        s_abort = 0;
+        for (int i = 0; i < a.nstage; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 8);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    // positions at step s (dummy rows stay at 0); attention units (m, h, c)
+    // cover the cached keys [0, pos-1) in chunks of KC
+    auto pos_of = [&](int m, int s) { return s_dummy[m] ? 0 : s_pos0[m] + s; };
+    auto nch_of = [&](int m, int s) {
+        const int old = pos_of(m, s) - 1;
+        return old > 0 ? (old + KC - 1) / KC : 0;
+    };
+
+    // =========================== producer ===================================
+    if (tid >= MK_CONS) {
+        if (tid != MK_CONS) return;
+        uint32_t it = 0;
+        bool ok = true;
+        auto issue = [&](const void* src, uint32_t bytes) {
+            if (!ok) return;
+            const int st = it % a.nstage;
+            if (it >= (uint32_t)a.nstage) {
+                const uint32_t par = ((it / a.nstage) - 1) & 1u;
+                if (!mbar_try(&empty[st], par)) {
+                    const unsigned long long t0 = gtimer();
+                    while (!mbar_try(&empty[st], par)) {
+                        if (s_abort || gtimer() - t0 > MK_TIMEOUT_NS) {
+                            if (!s_abort) atomicExch(a.err, 3);
+                            s_abort = 1;
+                            ok = false;
+                            return;
+                        }
+                    }
+                }
+            }
+            mbar_expect_tx(&full[st], bytes);
+            bulk_g2s(ring + (size_t)st * MK_STAGE, src, bytes, &full[st]);
+            it++;
+        };
+        auto issue_strip = [&](const float* Wt, int K, int N) {
+            int n0, w;
+            strip(N, nW, cta, n0, w);
+            const int R = strip_rows(w, K);
+            if (R == 0) return;
+            const float* base = Wt + (size_t)K * n0;
+            for (int r0 = 0; r0 < K && ok; r0 += R) issue(base + (size_t)r0 * w, (uint32_t)(min(R, K - r0) * w * 4));
+        };
+        for (int s = 0; s < a.nsteps && ok; s++) {
+            const unsigned int gs = a.gstep0 + s;
+            for (int l = 0; l < L && ok; l++) {
+                const MkLayer& ly = a.layers[l];
+                issue_strip(ly.w[MK_QKV], D, 3 * D);
+                if (l == 0 && gs >= 2 && ok) {
+                    // The K/V rows read below were written by steps <= gs-2:
+                    // wait until those steps finished on every CTA, then order
+                    // the async-proxy reads after them.
+                    const unsigned int target = (gs - 1) * (unsigned)nW;
+                    const unsigned long long t0 = gtimer();
+                    while (ld_acquire_u32(a.stepdone) < target) {
+                        __nanosleep(200);
+                        if (s_abort || gtimer() - t0 > MK_TIMEOUT_NS) {
+                            if (!s_abort) atomicExch(a.err, 4);
+                            s_abort = 1;
+                            ok = false;
+                            break;
+                        }
+                    }
+                    asm volatile("fence.proxy.async.global;" ::: "memory");
+                }
+                int u = 0;
+                for (int m = 0; m < MR && ok; m++) {
+                    const int nc = nch_of(m, s), old = pos_of(m, s) - 1;
+                    for (int h = 0; h < H && ok; h++)
+                        for (int c = 0; c < nc && ok; c++, u++) {
+                            if (u % nW != cta) continue;
+                            const int nk = min(KC, old - c * KC);
+                            const float* kb = a.kv + (size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
+                                              ((size_t)h * a.ctx + c * KC) * hd;
+                            issue(kb, (uint32_t)(nk * hd * 4));
+                            issue(kb + a.v_offset, (uint32_t)(nk * hd * 4));
+                        }
+                }
+                issue_strip(ly.w[MK_PROJ], D, D);
+                issue_strip(ly.w[MK_FC], D, F);
+                issue_strip(ly.w[MK_PROJ2], F, D);
+            }
+            const int v0 = (int)(((long long)cta * V) / nW), v1 = (int)(((long long)(cta + 1) * V) / nW);
+            const int Rh = max(1, MK_STAGE / (D * 4));
+            for (int r0 = v0; r0 < v1 && ok; r0 += Rh)
+                issue(a.tok_emb + (size_t)r0 * D, (uint32_t)(min(Rh, v1 - r0) * D * 4));
+        }
+        // wait (bounded) for copies still landing in this CTA's ring
+        for (uint32_t j = (it > (uint32_t)a.nstage ? it - a.nstage : 0); j < it; j++) {
+            const unsigned long long t0 = gtimer();
+            while (!mbar_try(&full[j % a.nstage], (j / a.nstage) & 1u))
+                if (gtimer() - t0 > MK_TIMEOUT_NS) break;
+        }
+        return;
+    }
+
+    // =========================== consumers ==================================
+    const int lane = tid & 31, warp = tid >> 5;
+    const float scale = 1.0f / sqrtf((float)hd);  // Layers.cs:174
+    const SampleParams sp = a.sp;
+    const bool controls = sp.penalty != 1.0f || sp.ngram > 0;
+    const bool sampled = sp.temperature > 0.0f;
+    const bool filter = sp.top_k > 0 && sp.top_k < V;
+    uint32_t it = 0;
+    if (controls)
+        for (int m = 0; m < MR; m++)
+            for (int i = tid; i < s_len0[m] && i < a.ctx; i += MK_CONS)
+                win[m * a.ctx + i] = s_dummy[m] ? 0 : a.hist[(size_t)s_slot[m] * a.hist_stride + i];
+    cons_sync();
+
+    // This CTA's column strip of y = act * W (+ epilogue(m, n, sum)).
+    auto gemv = [&](const float* actv, const float* Wt, int K, int N, auto&& epilogue) {
+        (void)Wt;
+        int n0, w;
+        strip(N, nW, cta, n0, w);
+        const int R = strip_rows(w, K);
+        if (R == 0) return;
+        const int G = MK_CONS / w, g = tid / w, c = tid - g * w;
+        const bool valid = tid < G * w;
+        float acc[MR];
+#pragma unroll
+        for (int m = 0; m < MR; m++) acc[m] = 0.f;
+        for (int r0 = 0; r0 < K; r0 += R) {
+            const int rows = min(R, K - r0);
+            wait_full(full, it, a.nstage, a.err, &s_abort);
+            const float* st = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
+            if (valid) {
+                for (int r = g; r < rows; r += G) {
+                    const float v = st[r * w + c];
+#pragma unroll
+                    for (int m = 0; m < MR; m++) acc[m] += actv[m * K + r0 + r] * v;
+                }
+            }
+            release_stage(empty, it, a.nstage);
+            it++;
+        }
+#pragma unroll
+        for (int m = 0; m < MR; m++) red[m * 256 + tid] = valid ? acc[m] : 0.f;
+        cons_sync();
+        if (tid < w * MR) {
+            const int m = tid / w, cc = tid - m * w;
+            float sum = 0.f;
+            for (int gg = 0; gg < G; gg++) sum += red[m * 256 + gg * w + cc];
+            epilogue(m, n0 + cc, sum);
+        }
+        cons_sync();
+    };
+
+    for (int s = 0; s < a.nsteps; s++) {
+        const unsigned int gs = a.gstep0 + s;
+        if (tid == 0) {
+            int acc = 0;
+            for (int m = 0; m < MR; m++) {
+                s_ubase[m] = acc;
+                acc += H * nch_of(m, s);
+            }
+            s_ubase[MR] = acc;
+        }
+        cons_sync();
+        MK_TRACE(24);
+        for (int l = 0; l < L; l++) {
+            const MkLayer& ly = a.layers[l];
+            const uint32_t tg = mk_tag(gs, l, L);
+            MK_TRACE_L(0);
+            // small parameters of this layer, loaded ahead of their use
+            const LnRegs ln1 = ln_prefetch(ly.ln1w, ly.ln1b, D);
+            const LnRegs ln2 = ln_prefetch(ly.ln2w, ly.ln2b, D);
+            float pb[4];
+            {
+                const int Ns[4] = {3 * D, D, F, D};
+#pragma unroll
+                for (int ph = 0; ph < 4; ph++) {
+                    int n0, w;
+                    strip(Ns[ph], nW, cta, n0, w);
+                    pb[ph] = (w > 0 && tid < w * MR) ? __ldg(ly.b[ph] + n0 + tid % w) : 0.f;
+                }
+            }
+            // ---- level A: x -> LN1 -> QKV (q, K/V to the cache) ----------------
+            if (l == 0) {
+                for (int m = 0; m < MR; m++) {
+                    const float* te = a.tok_emb + (size_t)s_tok[m] * D;
+                    const float* pe = a.pos_emb + (size_t)pos_of(m, s) * D;
+                    for (int i = tid; i < D; i += MK_CONS) xres[m * D + i] = __ldg(te + i) + __ldg(pe + i);
+                }
+            } else {
+                gather_tagged(a.xx, xres, MR * D, mk_tag(gs, l - 1, L), a.err, &s_abort);
+            }
+            if (cons_sync_or(s_abort)) return;
+            mk_layernorm<MR>(xres, act, D, ln1, scr + 384);
+            MK_TRACE_L(1);
+            {
+                auto epi = [&](int m, int n, float v) {
+                    v += pb[MK_QKV];
+                    if (n < D) {
+                        st_pair(a.xq + m * D + n, v, tg);
+                        return;
+                    }
+                    const int which = n < 2 * D ? 0 : 1;
+                    const int cc = n - D - which * D, h = cc / hd, d = cc - h * hd;
+                    if (!s_dummy[m])
+                        a.kv[(size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride + (which ? a.v_offset : 0) +
+                             ((size_t)h * a.ctx + pos_of(m, s)) * hd + d] = v;
+                    st_pair(a.xkv + (size_t)m * 2 * D + (n - D), v, tg);
+                };
+                gemv(act, ly.w[MK_QKV], D, 3 * D, epi);
+                MK_TRACE_L(2);
+            }
+            // ---- level B: attention units over the cached keys [0, pos-1) -----
+            {
+                float* qs = scr;         // [hd]
+                float* sc = scr + 128;   // [KC]
+                float* st2 = scr + 300;  // [2]
+                int u = 0;
+                for (int m = 0; m < MR; m++) {
+                    const int nc = nch_of(m, s), old = pos_of(m, s) - 1;
+                    for (int h = 0; h < H; h++)
+                        for (int c = 0; c < nc; c++, u++) {
+                            if (u % nW != cta) continue;
+                            const int nk = min(KC, old - c * KC);
+                            if (tid < hd) qs[tid] = wait_pair(a.xq + m * D + h * hd + tid, tg, a.err, &s_abort);
+                            cons_sync();
+                            wait_full(full, it, a.nstage, a.err, &s_abort);
+                            const float* Kt = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
+                            const int dpt = hd / 4, part = tid & 3;
+                            for (int j0 = 0; j0 < nk; j0 += MK_CONS / 4) {
+                                const int j = j0 + (tid >> 2);
+                                float d = 0.f;
+                                if (j < nk) {
+                                    const float* kr = Kt + j * hd + part * dpt;
+                                    for (int e = 0; e < dpt; e++) d += qs[part * dpt + e] * kr[e];
+                                }
+                                d += __shfl_xor_sync(0xffffffffu, d, 1);
+                                d += __shfl_xor_sync(0xffffffffu, d, 2);
+                                if (j < nk && part == 0) sc[j] = d * scale;
+                            }
+                            release_stage(empty, it, a.nstage);
+                            it++;
+                            cons_sync();
+                            if (warp == 0) {
+                                float mx = -INFINITY;
+                                for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sc[j]);
+                                mx = warp_max(mx);
+                                float lsum = 0.f;
+                                for (int j = lane; j < nk; j += 32) {
+                                    const float p = __expf(sc[j] - mx);
+                                    sc[j] = p;
+                                    lsum += p;
+                                }
+                                lsum = warp_sum(lsum);
+                                if (lane == 0) {
+                                    st2[0] = mx;
+                                    st2[1] = lsum;
+                                }
+                            }
+                            cons_sync();
+                            wait_full(full, it, a.nstage, a.err, &s_abort);
+                            const float* Vt = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
+                            {
+                                const int G2 = MK_CONS / hd, d = tid % hd, grp = tid / hd;
+                                float accv = 0.f;
+                                for (int j = grp; j < nk; j += G2) accv += sc[j] * Vt[j * hd + d];
+                                red[tid] = accv;
+                            }
+                            release_stage(empty, it, a.nstage);
+                            it++;
+                            cons_sync();
+                            // partial record [max, sum, acc[hd]], every word tagged
+                            unsigned long long* pr = a.xpart + (size_t)u * (hd + 2);
+                            if (tid < hd) {
+                                float t = 0.f;
+                                for (int gg = 0; gg < MK_CONS / hd; gg++) t += red[gg * hd + tid];
+                                st_pair(pr + 2 + tid, t, tg);
+                            }
+                            if (tid == 0) {
+                                st_pair(pr, st2[0], tg);
+                                st_pair(pr + 1, st2[1], tg);
+                            }
+                            cons_sync();
+                        }
+                }
+            }
+            MK_TRACE_L(3);
+            // ---- level C: combine partials + keys pos-1, pos -> ctx -> proj ---
+            // phase 1, an 8-lane group per (row, head): log-sum-exp weights of
+            // the key chunks and of the two directly read keys; ctx starts as
+            // the direct keys' share.  Every load is issued before any is used.
+            {
+                const int grp = tid >> 3, l8 = tid & 7, dpl = hd >> 3;  // hd <= 64
+                for (int p0 = 0; p0 < MR * H; p0 += 32) {
+                    const int p = p0 + grp;
+                    const bool on = p < MR * H;
+                    const int m = on ? p / H : 0, h = on ? p - (p / H) * H : 0;
+                    const int pos = pos_of(m, s), nc = on ? nch_of(m, s) : 0;
+                    const int ub = s_ubase[m] + h * nc;
+                    const int dq = m * D + h * hd + l8 * dpl;           // q / ctx column
+                    const size_t dk = (size_t)m * 2 * D + h * hd + l8 * dpl;  // current K (V at +D)
+                    unsigned long long wq[8], wk[8], wv[8], wmc[4], wlc[4];
+                    float kp[8], vp[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        wq[e] = wk[e] = wv[e] = 0ull;
+                        kp[e] = vp[e] = 0.f;
+                    }
+                    if (on) {
+                        for (int e = 0; e < dpl; e++) {
+                            wq[e] = ld_pair(a.xq + dq + e);
+                            wk[e] = ld_pair(a.xkv + dk + e);
+                            wv[e] = ld_pair(a.xkv + dk + D + e);
+                        }
+                        if (pos >= 1) {
+                            const float* kb = a.kv + (size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
+                                              ((size_t)h * a.ctx + pos - 1) * hd + l8 * dpl;
+                            for (int e = 0; e < dpl; e++) {
+                                kp[e] = __ldcg(kb + e);
+                                vp[e] = __ldcg(kb + a.v_offset + e);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; c4++) {
+                        const int c = l8 + 8 * c4;
+                        wmc[c4] = wlc[c4] = 0ull;
+                        if (on && c < nc) {
+                            const unsigned long long* pr = a.xpart + (size_t)(ub + c) * (hd + 2);
+                            wmc[c4] = ld_pair(pr);
+                            wlc[c4] = ld_pair(pr + 1);
+                        }
+                    }
+                    {
+                        // one wait over all 32 words: q, K, V (8 each), chunk (max, sum) x4
+                        unsigned long long wall[32];
+                        uint32_t pend = 0;
+#pragma unroll
+                        for (int e = 0; e < 8; e++) {
+                            wall[e] = wq[e];
+                            wall[8 + e] = wk[e];
+                            wall[16 + e] = wv[e];
+                            if (on && e < dpl) pend |= (1u << e) | (1u << (8 + e)) | (1u << (16 + e));
+                        }
+#pragma unroll
+                        for (int c4 = 0; c4 < 4; c4++) {
+                            wall[24 + c4] = wmc[c4];
+                            wall[28 + c4] = wlc[c4];
+                            if (on && l8 + 8 * c4 < nc) pend |= (1u << (24 + c4)) | (1u << (28 + c4));
+                        }
+                        auto addr = [&](int k) -> const unsigned long long* {
+                            if (k < 8) return a.xq + dq + k;
+                            if (k < 16) return a.xkv + dk + (k - 8);
+                            if (k < 24) return a.xkv + dk + D + (k - 16);
+                            const int c4 = (k - 24) & 3;
+                            return a.xpart + (size_t)(ub + l8 + 8 * c4) * (hd + 2) + (k < 28 ? 0 : 1);
+                        };
+                        resolve_batch<32>(wall, pend, addr, tg, a.err, &s_abort);
+#pragma unroll
+                        for (int e = 0; e < 8; e++) {
+                            wq[e] = wall[e];
+                            wk[e] = wall[8 + e];
+                            wv[e] = wall[16 + e];
+                        }
+#pragma unroll
+                        for (int c4 = 0; c4 < 4; c4++) {
+                            wmc[c4] = wall[24 + c4];
+                            wlc[c4] = wall[28 + c4];
+                        }
+                    }
+                    float dcur = 0.f, dprev = 0.f, vc[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        vc[e] = 0.f;
+                        if (on && e < dpl) {
+                            const float q = pair_value(wq[e]);
+                            vc[e] = pair_value(wv[e]);
+                            dcur += q * pair_value(wk[e]);
+                            dprev += q * kp[e];
+                        }
+                    }
+                    float mc[4], lc[4], mloc = -INFINITY;
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; c4++) {
+                        const int c = l8 + 8 * c4;
+                        mc[c4] = -INFINITY;
+                        lc[c4] = 0.f;
+                        if (on && c < nc) {
+                            mc[c4] = pair_value(wmc[c4]);
+                            lc[c4] = pair_value(wlc[c4]);
+                            mloc = fmaxf(mloc, mc[c4]);
+                        }
+                    }
+#pragma unroll
+                    for (int o = 1; o < 8; o <<= 1) {
+                        dcur += __shfl_xor_sync(0xffffffffu, dcur, o);
+                        dprev += __shfl_xor_sync(0xffffffffu, dprev, o);
+                        mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+                    }
+                    dcur *= scale;
+                    dprev *= scale;
+                    float M = fmaxf(mloc, dcur);
+                    if (pos >= 1) M = fmaxf(M, dprev);
+                    float ls = 0.f;
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; c4++) {
+                        const int c = l8 + 8 * c4;
+                        if (on && c < nc) {
+                            mc[c4] = __expf(mc[c4] - M);
+                            ls += lc[c4] * mc[c4];
+                        }
+                    }
+#pragma unroll
+                    for (int o = 1; o < 8; o <<= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+                    const float wcur = __expf(dcur - M), wprev = pos >= 1 ? __expf(dprev - M) : 0.f;
+                    const float inv = 1.0f / (ls + wcur + wprev);
+                    if (on) {
+#pragma unroll
+                        for (int c4 = 0; c4 < 4; c4++) {
+                            const int c = l8 + 8 * c4;
+                            if (c < nc) wts_m[(size_t)p * a.maxc + c] = mc[c4] * inv;
+                        }
+                        for (int e = 0; e < dpl; e++) act[dq + e] = (wcur * vc[e] + wprev * vp[e]) * inv;
+                    }
+                }
+            }
+            cons_sync();
+            MK_TRACE_L(4);
+            // phase 2, all threads: ctx += sum_c w_c * partial_c (tagged words,
+            // eight loads in flight per thread)
+            for (int e = tid; e < MR * D; e += MK_CONS) {
+                const int m = e / D, col = e - m * D, h = col / hd, d = col - h * hd;
+                const int nc = nch_of(m, s), ub = s_ubase[m] + h * nc;
+                const float* wrow = wts_m + (size_t)(m * H + h) * a.maxc;
+                float accc = 0.f;
+                for (int c0 = 0; c0 < nc; c0 += 8) {
+                    unsigned long long w8[8];
+                    uint32_t pend = 0;
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        w8[j] = 0ull;
+                        if (c0 + j < nc) {
+                            w8[j] = ld_pair(a.xpart + (size_t)(ub + c0 + j) * (hd + 2) + 2 + d);
+                            pend |= 1u << j;
+                        }
+                    }
+                    resolve_batch<8>(w8, pend, [&](int j) { return a.xpart + (size_t)(ub + c0 + j) * (hd + 2) + 2 + d; },
+                                     tg, a.err, &s_abort);
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        if (c0 + j < nc) accc += wrow[c0 + j] * pair_value(w8[j]);
+                }
+                act[e] += accc;
+            }
+            if (cons_sync_or(s_abort)) return;
+            {
+                auto epi = [&](int m, int n, float v) {
+                    st_pair(a.xx2 + m * D + n, (v + pb[MK_PROJ]) + xres[m * D + n], tg);
+                };
+                MK_TRACE_L(5);
+                gemv(act, ly.w[MK_PROJ], D, D, epi);
+                MK_TRACE_L(6);
+            }
+            // ---- level D: LN2 -> fc + GELU ---------------------------------------
+            gather_tagged(a.xx2, x2res, MR * D, tg, a.err, &s_abort);
+            if (cons_sync_or(s_abort)) return;
+            MK_TRACE_L(7);
+            mk_layernorm<MR>(x2res, act, D, ln2, scr + 384);
+            {
+                auto epi = [&](int m, int n, float v) {
+                    st_pair(a.xh + (size_t)m * F + n, gelu_tanh(v + pb[MK_FC]), tg);
+                };
+                MK_TRACE_L(8);
+                gemv(act, ly.w[MK_FC], D, F, epi);
+                MK_TRACE_L(9);
+            }
+            // ---- level E: proj2 + residual ----------------------------------------
+            gather_tagged(a.xh, act, MR * F, tg, a.err, &s_abort);
+            if (cons_sync_or(s_abort)) return;
+            {
+                auto epi = [&](int m, int n, float v) {
+                    st_pair(a.xx + m * D + n, (v + pb[MK_PROJ2]) + x2res[m * D + n], tg);
+                };
+                MK_TRACE_L(10);
+                gemv(act, ly.w[MK_PROJ2], F, D, epi);
+                MK_TRACE_L(11);
+                if (l < 24) MK_TRACE(33 + l);
+            }
+        }
+        // ---- head: LN_f -> logits of this CTA's vocabulary slice ----------------
+        const uint32_t th = mk_tag(gs, L, L);
+        const LnRegs lnf = ln_prefetch(a.lnf_w, a.lnf_b, D);
+        {
+            gather_tagged(a.xx, xres, MR * D, mk_tag(gs, L - 1, L), a.err, &s_abort);
+            if (cons_sync_or(s_abort)) return;
+        }
+        MK_TRACE(25);
+        mk_layernorm<MR>(xres, act, D, lnf, scr + 384);
+        const int v0 = (int)(((long long)cta * V) / nW), v1 = (int)(((long long)(cta + 1) * V) / nW);
+        const int nsl = v1 - v0;
+        {
+            const int Rh = max(1, MK_STAGE / (D * 4));
+            for (int r0 = v0; r0 < v1; r0 += Rh) {
+                const int rows = min(Rh, v1 - r0);
+                wait_full(full, it, a.nstage, a.err, &s_abort);
+                const float* E = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
+                for (int r = warp; r < rows; r += 8) {
+                    float accm[MR];
+#pragma unroll
+                    for (int m = 0; m < MR; m++) accm[m] = 0.f;
+                    const float4* er = reinterpret_cast<const float4*>(E + (size_t)r * D);
+                    for (int i = lane; i < D / 4; i += 32) {
+                        const float4 e4 = er[i];
+#pragma unroll
+                        for (int m = 0; m < MR; m++) {
+                            const float4 x4 = *reinterpret_cast<const float4*>(act + m * D + i * 4);
+                            accm[m] += x4.x * e4.x + x4.y * e4.y + x4.z * e4.z + x4.w * e4.w;
+                        }
+                    }
+#pragma unroll
+                    for (int m = 0; m < MR; m++) {
+                        const float t = warp_sum(accm[m]);
+                        if (lane == 0) slice[m * a.slice_max + (r0 - v0) + r] = t;
+                    }
+                }
+                release_stage(empty, it, a.nstage);
+                it++;
+            }
+        }
+        cons_sync();
+        MK_TRACE(27);
+        // ---- candidates of this slice (repetition controls applied here) -------
+        for (int m = 0; m < MR; m++) {
+            float* sl = slice + m * a.slice_max;
+            for (int i = tid; i < nsl; i += MK_CONS) a.logits_out[(size_t)m * V + v0 + i] = sl[i];
+            const int wl = min(s_len0[m] + s, a.ctx);
+            const int* wv = win + m * a.ctx + (s_len0[m] + s - wl);
+            if (controls) {
+                if (tid < 16) seen[tid] = 0u;  // clears seen[] and ban[]
+                cons_sync();
+                if (sp.penalty != 1.0f)  // once per distinct window token (Sampler.cs:117-127)
+                    for (int i = tid; i < wl; i += MK_CONS) {
+                        const int t = wv[i] - v0;
+                        if (t >= 0 && t < nsl) atomicOr(&seen[t >> 5], 1u << (t & 31));
+                    }
+                if (sp.ngram > 0 && wl >= sp.ngram - 1) {  // Sampler.cs:129-154
+                    const int n = sp.ngram;
+                    if (n == 1) {
+                        for (int i = tid; i < wl; i += MK_CONS) {
+                            const int t = wv[i] - v0;
+                            if (t >= 0 && t < nsl) atomicOr(&ban[t >> 5], 1u << (t & 31));
+                        }
+                    } else {
+                        const int pre = n - 1, suf = wl - pre;
+                        for (int st0 = tid; st0 + n <= wl; st0 += MK_CONS) {
+                            bool match = true;
+                            for (int j = 0; j < pre; j++)
+                                if (wv[st0 + j] != wv[suf + j]) {
+                                    match = false;
+                                    break;
+                                }
+                            if (!match) continue;
+                            const int t = wv[st0 + pre] - v0;
+                            if (t >= 0 && t < nsl) atomicOr(&ban[t >> 5], 1u << (t & 31));
+                        }
+                    }
+                }
+                cons_sync();
+                for (int i = tid; i < nsl; i += MK_CONS) {
+                    float l = sl[i];
+                    if ((seen[i >> 5] >> (i & 31)) & 1u) l = l < 0.0f ? l * sp.penalty : l / sp.penalty;
+                    if ((ban[i >> 5] >> (i & 31)) & 1u) l = -INFINITY;
+                    sl[i] = l;
+                }
+                cons_sync();
+            }
+            float* cv = a.cand_val + ((size_t)m * nW + cta) * a.slice_max;
+            int* ci = a.cand_idx + ((size_t)m * nW + cta) * a.slice_max;
+            if (!sampled) {  // local first argmax (Sampler.cs:14-20)
+                float bv = -INFINITY;
+                int bi = -1;
+                for (int i = tid; i < nsl; i += MK_CONS) {
+                    const float v = sl[i];
+                    if (v != v) continue;
+                    if (bi < 0 || v > bv) {
+                        bv = v;
+                        bi = i;
+                    }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+                        bv = ov;
+                        bi = oi;
+                    }
+                }
+                if (lane == 0) {
+                    scr[warp] = bv;
+                    wbi[warp] = bi;
+                }
+                cons_sync();
+                if (tid == 0) {
+                    float b = -INFINITY;
+                    int ix = -1;
+                    for (int w8 = 0; w8 < 8; w8++) {
+                        const int oi = wbi[w8];
+                        const float ov = scr[w8];
+                        if (oi >= 0 && (ix < 0 || ov > b || (ov == b && oi < ix))) {
+                            b = ov;
+                            ix = oi;
+                        }
+                    }
+                    int cnt = 0;
+                    if (ix >= 0) {
+                        cv[0] = b;
+                        ci[0] = v0 + ix;
+                        cnt = 1;
+                    }
+                    rcnt[m] = cnt;
+                }
+                cons_sync();
+            } else {
+                for (int i = tid; i < nsl; i += MK_CONS) sl[i] = sl[i] / sp.temperature;  // Sampler.cs:40
+                cons_sync();
+                // keep entries with fewer than k strictly larger ones (ties kept);
+                // the slice's 4 largest entries (ties by lower index) go to the header
+                float* top4 = reinterpret_cast<float*>(misc) + 48 + 4 * m;
+                int* top4i = iscr + 160 + 4 * m;
+                if (tid < 4) {
+                    top4[tid] = -INFINITY;
+                    top4i[tid] = -1;
+                }
+                cons_sync();
+                int f = 0;
+                if (tid < nsl) {
+                    const float v = sl[tid];
+                    int rank = 0, tie = 0;
+                    for (int j = 0; j < nsl; j++) {
+                        const float u = sl[j];
+                        rank += u > v;
+                        tie += (u == v) & (j < tid);
+                    }
+                    f = rank < sp.top_k;
+                    if (rank + tie < 4) {
+                        top4[rank + tie] = v;
+                        top4i[rank + tie] = v0 + tid;
+                    }
+                }
+                flag[tid] = f;
+                // the local k-th largest (smallest kept value) is a lower bound
+                // of the row's k-th largest; -inf when the slice has < k entries
+                float lk = f ? sl[tid] : INFINITY;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) lk = fminf(lk, __shfl_xor_sync(0xffffffffu, lk, o));
+                if (lane == 0) scr[256 + warp] = lk;
+                // exclusive scan of the flags -> candidate order = index order
+                int x = f;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int t = __shfl_up_sync(0xffffffffu, x, o);
+                    if (lane >= o) x += t;
+                }
+                if (lane == 31) misc[warp] = x;
+                cons_sync();
+                int base = 0;
+                for (int w8 = 0; w8 < warp; w8++) base += misc[w8];
+                if (f) {
+                    cv[base + x - 1] = sl[tid];
+                    ci[base + x - 1] = v0 + tid;
+                }
+                if (tid == 0) {
+                    int tot = 0;
+                    float mn = INFINITY;
+                    for (int w8 = 0; w8 < 8; w8++) {
+                        tot += misc[w8];
+                        mn = fminf(mn, scr[256 + w8]);
+                    }
+                    rcnt[m] = tot;
+                    (void)mn;
+                }
+                cons_sync();
+            }
+        }
+        MK_TRACE(28);
+        // publish: release every plain write of this step (K/V cache, logits,
+        // candidates), then per (row, slice) the tagged count and local k-th
+        __threadfence();
+        cons_sync();
+        if (tid < MR) {
+            unsigned long long* hp = a.cand_hdr + ((size_t)tid * nW + cta) * 9;
+            const float* top4 = reinterpret_cast<float*>(misc) + 48 + 4 * tid;
+            const int* top4i = iscr + 160 + 4 * tid;
+            st_pair(hp, __int_as_float(rcnt[tid]), th);
+            for (int q4 = 0; q4 < 4; q4++) {
+                st_pair(hp + 1 + 2 * q4, sampled ? top4[q4] : -INFINITY, th);
+                st_pair(hp + 2 + 2 * q4, __int_as_float(sampled ? top4i[q4] : -1), th);
+            }
+        }
+        MK_TRACE(30);
+        // ---- finalize: every CTA computes the same token for each row ----------
+        for (int m = 0; m < MR; m++) {
+            float* tops = act;                                  // [nW][4] slices' largest values
+            int* topi = reinterpret_cast<int*>(act + 4 * nW);    // [nW][4] their vocabulary ids
+            if (tid < nW) {  // nW <= 256: one slice header per thread
+                const unsigned long long* hp = a.cand_hdr + ((size_t)m * nW + tid) * 9;
+                unsigned long long w[9];
+#pragma unroll
+                for (int q4 = 0; q4 < 9; q4++) w[q4] = ld_pair(hp + q4);
+                resolve_batch<9>(w, 0x1ffu, [&](int k) { return hp + k; }, th, a.err, &s_abort);
+                cnts[tid] = __float_as_int(pair_value(w[0]));
+#pragma unroll
+                for (int q4 = 0; q4 < 4; q4++) {
+                    tops[tid * 4 + q4] = pair_value(w[1 + 2 * q4]);
+                    topi[tid * 4 + q4] = __float_as_int(pair_value(w[2 + 2 * q4]));
+                }
+            }
+            if (cons_sync_or(s_abort)) return;
+            fence_acq_rel();
+            if (!sampled) {
+                // one candidate (the slice's first argmax) per slice
+                float bv = -INFINITY;
+                int bi = -1;
+                if (tid < nW && cnts[tid] > 0) {
+                    const size_t at = ((size_t)m * nW + tid) * a.slice_max;
+                    bv = __ldcg(a.cand_val + at);
+                    bi = __ldcg(a.cand_idx + at);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+                        bv = ov;
+                        bi = oi;
+                    }
+                }
+                if (lane == 0) {
+                    scr[warp] = bv;
+                    wbi[warp] = bi;
+                }
+                cons_sync();
+                if (tid == 0) {
+                    float b = -INFINITY;
+                    int ix = -1;
+                    for (int w8 = 0; w8 < 8; w8++) {
+                        const int oi = wbi[w8];
+                        const float ov = scr[w8];
+                        if (oi >= 0 && (ix < 0 || ov > b || (ov == b && oi < ix))) {
+                            b = ov;
+                            ix = oi;
+                        }
+                    }
+                    rtok[m] = ix < 0 ? 0 : ix;
+                }
+                cons_sync();
+            } else {
+                // lower bound of the row's k-th largest: the k-th largest of the
+                // slices' top values (a subset of the row)
+                float tl = INFINITY;
+                for (int i = tid; i < 4 * nW; i += MK_CONS) {
+                    const float v = tops[i];
+                    int rank = 0;
+                    for (int j = 0; j < 4 * nW; j++) rank += tops[j] > v;
+                    if (rank < sp.top_k) tl = fminf(tl, v);
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) tl = fminf(tl, __shfl_xor_sync(0xffffffffu, tl, o));
+                if (lane == 0) scr[256 + warp] = tl;
+                cons_sync();
+                float tlo = INFINITY;
+                for (int w8 = 0; w8 < 8; w8++) tlo = fminf(tlo, scr[256 + w8]);
+                // stage every candidate >= the bound: from the header when the
+                // slice's 4th largest is below the bound (then every such entry
+                // is among its top 4), else from the slice's list
+                int q = 0;
+                const float* cvs = a.cand_val + ((size_t)m * nW + tid) * a.slice_max;
+                const int* cis = a.cand_idx + ((size_t)m * nW + tid) * a.slice_max;
+                const int mycnt = tid < nW ? cnts[tid] : 0;
+                const bool from_list = tid < nW && !(tops[tid * 4 + 3] < tlo);
+                if (tid < nW) {
+                    if (from_list) {
+                        for (int i = 0; i < mycnt; i++) q += !(__ldcg(cvs + i) < tlo);
+                    } else {
+#pragma unroll
+                        for (int q4 = 0; q4 < 4; q4++) q += topi[tid * 4 + q4] >= 0 && !(tops[tid * 4 + q4] < tlo);
+                    }
+                }
+                int Q;
+                const int off = cons_excl_scan(q, misc + 16, Q);
+                if (Q <= MK_SURV_MAX && tid < nW) {
+                    int o = off;
+                    if (from_list) {
+                        for (int i = 0; i < mycnt; i++) {
+                            const float v = __ldcg(cvs + i);
+                            if (v < tlo) continue;
+                            surv_v[o] = v;
+                            surv_i[o] = __ldcg(cis + i);
+                            o++;
+                        }
+                    } else {
+#pragma unroll
+                        for (int q4 = 0; q4 < 4; q4++)
+                            if (topi[tid * 4 + q4] >= 0 && !(tops[tid * 4 + q4] < tlo)) {
+                                surv_v[o] = tops[tid * 4 + q4];
+                                surv_i[o] = topi[tid * 4 + q4];
+                                o++;
+                            }
+                    }
+                }
+                cons_sync();
+                if (Q <= MK_SURV_MAX) {
+                    // index order (the serial sums follow it): rank by vocabulary id
+                    float rv[2];
+                    int ri[2], rr[2];
+#pragma unroll
+                    for (int j2 = 0; j2 < 2; j2++) {
+                        const int i = tid + j2 * MK_CONS;
+                        rr[j2] = -1;
+                        if (i < Q) {
+                            rv[j2] = surv_v[i];
+                            ri[j2] = surv_i[i];
+                            int r = 0;
+                            for (int j = 0; j < Q; j++) r += surv_i[j] < ri[j2];
+                            rr[j2] = r;
+                        }
+                    }
+                    cons_sync();
+#pragma unroll
+                    for (int j2 = 0; j2 < 2; j2++)
+                        if (rr[j2] >= 0) {
+                            surv_v[rr[j2]] = rv[j2];
+                            surv_i[rr[j2]] = ri[j2];
+                        }
+                    cons_sync();
+                }
+                if (Q <= MK_SURV_MAX) {
+                    // exact threshold: smallest staged value with < k larger ones
+                    float thr = INFINITY, mx = -INFINITY;
+                    for (int i = tid; i < Q; i += MK_CONS) {
+                        const float v = surv_v[i];
+                        mx = fmaxf(mx, v);
+                        int rank = 0;
+                        for (int j = 0; j < Q; j++) rank += surv_v[j] > v;
+                        if (rank < sp.top_k) thr = fminf(thr, v);
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        thr = fminf(thr, __shfl_xor_sync(0xffffffffu, thr, o));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    }
+                    if (lane == 0) {
+                        scr[256 + warp] = thr;
+                        scr[264 + warp] = mx;
+                    }
+                    cons_sync();
+                    float T = INFINITY, M = -INFINITY;
+                    for (int w8 = 0; w8 < 8; w8++) {
+                        T = fminf(T, scr[256 + w8]);
+                        M = fmaxf(M, scr[264 + w8]);
+                    }
+                    // exponentials of the survivors in parallel (Sampler.cs:57),
+                    // zero for the entries below the threshold
+                    for (int i = tid; i < Q; i += MK_CONS) {
+                        const float v = surv_v[i];
+                        surv_v[i] = (v < T) ? 0.0f : expf_libm(v - M);
+                    }
+                    cons_sync();
+                    if (tid == 0) {
+                        const double ud =
+                            a.uniforms[(size_t)s_slot[m] * a.uni_stride + min(s_cnt0[m] + s, max(sp.max_new - 1, 0))];
+                        float sum = 0.0f;  // index order (Sampler.cs:54-59)
+                        for (int i = 0; i < Q; i++) sum += surv_v[i];
+                        const float uu = (float)ud * sum;  // Sampler.cs:61
+                        float accp = 0.0f;
+                        int pick = V - 1;  // rounding fallback (Sampler.cs:68)
+                        for (int i = 0; i < Q; i++) {
+                            accp += surv_v[i];
+                            if (uu < accp) {
+                                pick = surv_i[i];
+                                break;
+                            }
+                        }
+                        if (sum != sum) pick = V - 1;
+                        rtok[m] = pick;
+                    }
+                    cons_sync();
+                } else {
+                    // more candidates above the bound than shared memory stages
+                    // (massive ties): radix-select the threshold over memory,
+                    // each thread scanning its slice's list
+                    uint32_t* hist = reinterpret_cast<uint32_t*>(scr);
+                    if (tid == 0) {
+                        misc[0] = 0;
+                        misc[1] = 0;
+                        misc[2] = sp.top_k;
+                    }
+                    cons_sync();
+                    for (int shift = 24; shift >= 0; shift -= 8) {
+                        hist[tid] = 0u;
+                        const uint32_t prefix = (uint32_t)misc[0], mask = (uint32_t)misc[1];
+                        cons_sync();
+                        for (int i = 0; i < mycnt; i++) {
+                            const float v = __ldcg(cvs + i);
+                            if (v < tlo) continue;
+                            const uint32_t key = float_key(v);
+                            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+                        }
+                        cons_sync();
+                        if (warp == 0) {
+                            const int kk = misc[2];
+                            int bin, above;
+                            radix_pick(hist, kk, bin, above);
+                            if (lane == 0) {
+                                misc[0] = (int)(prefix | ((uint32_t)bin << shift));
+                                misc[1] = (int)(mask | (255u << shift));
+                                misc[2] = kk - above;
+                            }
+                        }
+                        cons_sync();
+                    }
+                    const float T = key_float((uint32_t)misc[0]);
+                    // survivors (>= T), in index order
+                    int ns = 0;
+                    float mx = -INFINITY;
+                    for (int i = 0; i < mycnt; i++) {
+                        const float v = __ldcg(cvs + i);
+                        if (v < T) continue;
+                        ns++;
+                        mx = fmaxf(mx, v);
+                    }
+                    mx = warp_max(mx);
+                    if (lane == 0) scr[264 + warp] = mx;
+                    int S;
+                    const int so = cons_excl_scan(ns, misc + 16, S);
+                    float M = -INFINITY;
+                    for (int w8 = 0; w8 < 8; w8++) M = fmaxf(M, scr[264 + w8]);
+                    if (S <= MK_SURV_MAX) {
+                        int o = so;
+                        for (int i = 0; i < mycnt; i++) {
+                            const float v = __ldcg(cvs + i);
+                            if (v < T) continue;
+                            surv_v[o] = expf_libm(v - M);  // Sampler.cs:57
+                            surv_i[o] = __ldcg(cis + i);
+                            o++;
+                        }
+                    }
+                    cons_sync();
+                    if (tid == 0) {
+                        const double ud =
+                            a.uniforms[(size_t)s_slot[m] * a.uni_stride + min(s_cnt0[m] + s, max(sp.max_new - 1, 0))];
+                        float sum = 0.0f;
+                        int pick = V - 1;
+                        if (S <= MK_SURV_MAX) {
+                            for (int i = 0; i < S; i++) sum += surv_v[i];
+                            const float uu = (float)ud * sum;
+                            float accp = 0.0f;
+                            for (int i = 0; i < S; i++) {
+                                accp += surv_v[i];
+                                if (uu < accp) {
+                                    pick = surv_i[i];
+                                    break;
+                                }
+                            }
+                        } else {  // serial over the lists, one pass each for sum and draw
+                            for (int c = 0; c < nW; c++)
+                                for (int i = 0; i < cnts[c]; i++) {
+                                    const float v = __ldcg(a.cand_val + ((size_t)m * nW + c) * a.slice_max + i);
+                                    if (!(v < T)) sum += expf_libm(v - M);
+                                }
+                            const float uu = (float)ud * sum;
+                            float accp = 0.0f;
+                            for (int c = 0; c < nW && pick == V - 1; c++)
+                                for (int i = 0; i < cnts[c]; i++) {
+                                    const size_t at = ((size_t)m * nW + c) * a.slice_max + i;
+                                    const float v = __ldcg(a.cand_val + at);
+                                    if (v < T) continue;
+                                    accp += expf_libm(v - M);
+                                    if (uu < accp) {
+                                        pick = __ldcg(a.cand_idx + at);
+                                        break;
+                                    }
+                                }
+                        }
+                        if (sum != sum) pick = V - 1;
+                        rtok[m] = pick;
+                    }
+                    cons_sync();
+                }
+            }
+            // bookkeeping (CTA 0) and this CTA's state for the next step
+            if (tid == 0) {
+                const int tok = rtok[m];
+                if (!s_dead[m]) {
+                    const int c = s_cnt0[m] + s;
+                    const bool fin = (sp.eos >= 0 && tok == sp.eos) || c + 1 >= sp.max_new;
+                    if (a.bookkeep && cta == 0) {
+                        const int slot = s_slot[m];
+                        a.out_tokens[(size_t)slot * a.out_stride + c] = tok;
+                        a.hist[(size_t)slot * a.hist_stride + s_len0[m] + s] = tok;
+                        a.len[slot] = s_len0[m] + s + 1;
+                        a.count[slot] = c + 1;
+                        if (fin) a.done[slot] = 1;
+                    }
+                    if (fin) s_dead[m] = 1;
+                }
+                s_tok[m] = tok;
+                if (controls && s_len0[m] + s < a.ctx) win[m * a.ctx + s_len0[m] + s] = tok;
+            }
+            cons_sync();
+        }
+        MK_TRACE(31);
+        if (tid == 0) {
+            __threadfence();
+            atomicAdd(a.stepdone, 1u);
+        }
+        MK_TRACE(32);
+    }
+}
+
+}  // namespace fb2

@@ -26,6 +26,7 @@
 #include "dotnet_random.hpp"
 #include "kernels.cuh"
 #include "sampler.cuh"
+#include "decode_mega.cuh"
 
 using namespace fb2;
 
@@ -114,6 +115,11 @@ struct DeviceModel {
     std::vector<const float*> p;
     std::vector<LayerW> layers;
     const float *tok_emb = nullptr, *pos_emb = nullptr, *lnf_w = nullptr, *lnf_b = nullptr;
+    // persistent decode kernel: projections re-laid as per-CTA column strips
+    bool mk_ok = false;
+    int mk_nW = 0;
+    float* relaid = nullptr;
+    MkLayer* d_mk_layers = nullptr;
 };
 
 struct fb2_model {
@@ -167,6 +173,86 @@ static void configure_kernels(int dev) {
     setmax((const void*)k_head<16>, 227 * 1024);
     setmax((const void*)k_sample_step, 227 * 1024);
     setmax((const void*)k_sample_rows, 227 * 1024);
+    setmax((const void*)k_decode_mega<1>, 0);
+    setmax((const void*)k_decode_mega<2>, 0);
+    setmax((const void*)k_decode_mega<4>, 0);
+    setmax((const void*)k_decode_mega<8>, 0);
+}
+
+// ---------------------------------------------------------------------------
+// persistent decode kernel: geometry and weight layout
+// ---------------------------------------------------------------------------
+static int mk_keys_per_chunk(int hd) { return MK_STAGE / (hd * 4); }
+static int mk_maxc(int ctx, int hd) { return ceil_div(ctx, mk_keys_per_chunk(hd)); }
+static int mk_slice_max(int V, int nW) { return ceil_div(V, nW); }
+
+// Dynamic shared memory of k_decode_mega<MR> with `nstage` ring stages.
+static size_t mk_smem(const fb2_model& m, int MR, int nW, int nstage) {
+    return (size_t)nstage * MK_STAGE +
+           mk_aux_bytes(MR, m.D, m.F, m.H, m.ctx, mk_slice_max(m.V, nW), mk_maxc(m.ctx, m.hd), nstage) + 256;
+}
+
+// Ring stages that fit next to the kernel's other shared memory (0: does not fit).
+static int mk_nstage(const fb2_model& m, int MR, int nW, int device) {
+    int optin = 0;
+    CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+    cudaFuncAttributes fa;
+    const void* f = MR == 1 ? (const void*)k_decode_mega<1>
+                  : MR == 2 ? (const void*)k_decode_mega<2>
+                  : MR == 4 ? (const void*)k_decode_mega<4>
+                            : (const void*)k_decode_mega<8>;
+    CK(cudaFuncGetAttributes(&fa, f));
+    const long long avail = (long long)optin - (long long)fa.sharedSizeBytes;
+    int ns = 16;
+    while (ns >= 4 && (long long)mk_smem(m, MR, nW, ns) > avail) ns--;
+    return ns >= 4 ? ns : 0;
+}
+
+// Re-lays every projection W[K][N] as consecutive column strips [K][w_c],
+// one per CTA (the split k_decode_mega streams), and uploads the layer table.
+static void mk_setup(const fb2_model& m, DeviceModel& dm, const float* const* params) {
+    dm.mk_ok = false;
+    const int nW = dm.sm_count;
+    if (!(m.hd == 32 || m.hd == 64)) return;
+    if (mk_maxc(m.ctx, m.hd) > 32) return;
+    if (m.V <= m.ctx) return;  // the ban of a whole window could then cover the vocabulary
+    if (mk_slice_max(m.V, nW) > MK_SLICE_MAX || nW > 256) return;
+    if (m.D * 4 > MK_STAGE) return;
+    if (mk_nstage(m, 1, nW, dm.device) == 0) return;
+    const size_t D = m.D, F = m.F;
+    const size_t per_layer = 3 * D * D + D * D + D * F + F * D;
+    dm.relaid = dalloc<float>(per_layer * m.L);
+    std::vector<float> tmp(std::max(3 * D * D, D * F));
+    std::vector<MkLayer> host(m.L);
+    for (int l = 0; l < m.L; l++) {
+        const float* const* q = params + 2 + 12 * l;
+        struct { const float* W; size_t K, N; } mats[4] = {{q[2], D, 3 * D}, {q[4], D, D}, {q[8], D, F}, {q[10], F, D}};
+        size_t off = per_layer * l;
+        for (int ph = 0; ph < 4; ph++) {
+            const size_t K = mats[ph].K, N = mats[ph].N;
+            for (int c = 0; c < nW; c++) {
+                const size_t n0 = (size_t)c * N / nW, n1 = (size_t)(c + 1) * N / nW, w = n1 - n0;
+                for (size_t k = 0; k < K; k++)
+                    std::memcpy(&tmp[K * n0 + k * w], mats[ph].W + k * N + n0, w * sizeof(float));
+            }
+            CK(cudaMemcpy(dm.relaid + off, tmp.data(), K * N * sizeof(float), cudaMemcpyHostToDevice));
+            host[l].w[ph] = dm.relaid + off;
+            off += K * N;
+        }
+        const LayerW& lw = dm.layers[l];
+        host[l].b[MK_QKV] = lw.qkv_b;
+        host[l].b[MK_PROJ] = lw.proj_b;
+        host[l].b[MK_FC] = lw.fc_b;
+        host[l].b[MK_PROJ2] = lw.mproj_b;
+        host[l].ln1w = lw.ln1_w;
+        host[l].ln1b = lw.ln1_b;
+        host[l].ln2w = lw.ln2_w;
+        host[l].ln2b = lw.ln2_b;
+    }
+    dm.d_mk_layers = dalloc<MkLayer>(m.L);
+    CK(cudaMemcpy(dm.d_mk_layers, host.data(), m.L * sizeof(MkLayer), cudaMemcpyHostToDevice));
+    dm.mk_nW = nW;
+    dm.mk_ok = true;
 }
 
 // ---------------------------------------------------------------------------
@@ -224,6 +310,19 @@ struct DeviceSession {
 
     std::vector<DotNetRandom> rngs;  // FB2_RNG_SESSION streams of this device's slots
 
+    // persistent decode kernel (k_decode_mega) state
+    bool mk_use = false;
+    unsigned long long *mk_xq = nullptr, *mk_xkv = nullptr, *mk_xx2 = nullptr, *mk_xh = nullptr, *mk_xx = nullptr;
+    unsigned long long *mk_xpart = nullptr, *mk_hdr = nullptr;
+    float *mk_xacc = nullptr, *mk_cval = nullptr;
+    int* mk_cidx = nullptr;
+    unsigned int* mk_stepdone = nullptr;
+    int *mk_err = nullptr, *mk_rows = nullptr;
+    unsigned int mk_gstep = 0;
+    size_t mk_tagged_words = 0;
+    unsigned long long* mk_trace = nullptr;
+    int mk_trace_steps = 0;
+
     // stats
     fb2_stats_t stats{};
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -235,6 +334,55 @@ struct fb2_session {
     std::vector<DeviceSession*> ds;
 };
 
+// Zeroes the persistent kernel's tagged words, counters and error flag and
+// restarts its step numbering (tags compare against 1 + step * (L+1) + layer,
+// so zeroed words never match).
+static void mk_reset(DeviceSession& s) {
+    CK(cudaMemsetAsync(s.mk_xq, 0, s.mk_tagged_words * 8, s.stream));
+    CK(cudaMemsetAsync(s.mk_stepdone, 0, sizeof(unsigned int), s.stream));
+    CK(cudaMemsetAsync(s.mk_err, 0, sizeof(int), s.stream));
+    s.mk_gstep = 0;
+}
+
+// Buffers of k_decode_mega for up to MK_MAX_ROWS rows on this device.
+// FORGE_B200_DECODE=graph keeps the multi-kernel graph path instead.
+static void mk_session_alloc(DeviceSession& s) {
+    const fb2_model& m = *s.model;
+    const DeviceModel& dm = *s.dm;
+    const char* env = getenv("FORGE_B200_DECODE");
+    s.mk_use = dm.mk_ok && !(env && std::string(env) == "graph");
+    if (!s.mk_use) return;
+    const size_t R = MK_MAX_ROWS, D = m.D, F = m.F, nW = dm.mk_nW;
+    const size_t units = R * m.H * mk_maxc(m.ctx, m.hd);
+    s.mk_tagged_words = R * D + R * 2 * D + R * D + R * F + R * D + units * (m.hd + 2) + R * nW * 9;
+    s.mk_xq = dalloc<unsigned long long>(s.mk_tagged_words);
+    s.mk_xkv = s.mk_xq + R * D;
+    s.mk_xx2 = s.mk_xkv + R * 2 * D;
+    s.mk_xh = s.mk_xx2 + R * D;
+    s.mk_xx = s.mk_xh + R * F;
+    s.mk_xpart = s.mk_xx + R * D;
+    s.mk_hdr = s.mk_xpart + units * (m.hd + 2);
+    s.mk_xacc = dalloc<float>(units * m.hd);
+    const size_t slice = mk_slice_max(m.V, (int)nW);
+    s.mk_cval = dalloc<float>(R * nW * slice);
+    s.mk_cidx = dalloc<int>(R * nW * slice);
+    s.mk_stepdone = dalloc<unsigned int>(1);
+    s.mk_err = dalloc<int>(1);
+    s.mk_rows = dalloc<int>(R);
+    if (const char* tr = getenv("FORGE_B200_MK_TRACE")) {  // per-phase timestamps of the first steps
+        s.mk_trace_steps = std::max(0, std::min(64, atoi(tr)));
+        if (s.mk_trace_steps > 0) {
+            s.mk_trace = dalloc<unsigned long long>((size_t)nW * s.mk_trace_steps * MK_TRACE_POINTS);
+            CK(cudaMemset(s.mk_trace, 0, (size_t)nW * s.mk_trace_steps * MK_TRACE_POINTS * 8));
+        }
+    }
+    std::vector<int> rows(R);
+    for (size_t i = 0; i < R; i++) rows[i] = (int)std::min(i, (size_t)std::max(s.nslots - 1, 0));
+    CK(cudaMemcpy(s.mk_rows, rows.data(), R * sizeof(int), cudaMemcpyHostToDevice));
+    mk_reset(s);
+    CK(cudaStreamSynchronize(s.stream));
+}
+
 static void session_free(DeviceSession* s) {
     if (!s) return;
     cudaSetDevice(s->device);
@@ -244,6 +392,8 @@ static void session_free(DeviceSession* s) {
     dfree(s->d_x); dfree(s->d_x2); dfree(s->d_ln); dfree(s->d_q); dfree(s->d_att); dfree(s->d_h);
     dfree(s->d_logits); dfree(s->d_lnf); dfree(s->d_attn_part); dfree(s->d_gemv_part); dfree(s->d_tickets);
     dfree(s->d_tab); dfree(s->d_uni); dfree(s->d_out);
+    dfree(s->mk_xq); dfree(s->mk_xacc); dfree(s->mk_cval); dfree(s->mk_cidx); dfree(s->mk_stepdone);
+    dfree(s->mk_err); dfree(s->mk_rows); dfree(s->mk_trace);
     if (s->h_tab) cudaFreeHost(s->h_tab);
     if (s->tab_event) cudaEventDestroy(s->tab_event);
     if (s->ev0) cudaEventDestroy(s->ev0);
@@ -459,6 +609,71 @@ static void run_decode_step(DeviceSession& s, int n) {
     CK(cudaGraphLaunch(s.graph, s.stream));
     s.stats.kernel_launches += s.graph_kernels;
     s.stats.decode_steps++;
+}
+
+// Whether k_decode_mega can run a decode of n rows with these options: up to
+// 8 rows, greedy or top-k <= 64 (the candidate union stays small).
+static bool mk_eligible(const DeviceSession& s, int n, const fb2_sampling& sp) {
+    if (!s.mk_use || n < 1 || n > MK_MAX_ROWS) return false;
+    if (sp.temperature > 0.0f && !(sp.top_k > 0 && sp.top_k <= MK_MAX_TOPK && sp.top_k < s.model->V)) return false;
+    return true;
+}
+
+// One launch of k_decode_mega: `nsteps` decode steps for slots 0..n-1, none
+// of which may slide within them.  Cooperative launch: one CTA per SM, all
+// resident (the kernel's CTAs wait on one another).
+static void run_mega(DeviceSession& s, int n, int nsteps, const SampleParams& P, const double* d_uni, int* d_out,
+                     int out_stride, bool bookkeep) {
+    const fb2_model& m = *s.model;
+    const DeviceModel& dm = *s.dm;
+    const int MR = n <= 1 ? 1 : n <= 2 ? 2 : n <= 4 ? 4 : 8;
+    const int nW = dm.mk_nW;
+    const int nstage = mk_nstage(m, MR, nW, s.device);
+    if (nstage == 0) fail(FB2_UNSUPPORTED, "persistent decode kernel does not fit shared memory");
+    MkArgs a{};
+    a.V = m.V; a.ctx = m.ctx; a.D = m.D; a.L = m.L; a.H = m.H; a.hd = m.hd; a.F = m.F;
+    a.nW = nW; a.nstage = nstage; a.slice_max = mk_slice_max(m.V, nW);
+    a.layers = dm.d_mk_layers;
+    a.tok_emb = dm.tok_emb; a.pos_emb = dm.pos_emb; a.lnf_w = dm.lnf_w; a.lnf_b = dm.lnf_b;
+    a.kv = s.d_kv; a.kv_slot_stride = s.kv_slot_stride; a.kv_layer_stride = s.kv_layer_stride; a.v_offset = s.v_offset;
+    a.hist = s.d_hist; a.hist_stride = s.hist_cap;
+    a.len = s.d_len; a.count = s.d_count; a.done = s.d_done;
+    a.uniforms = d_uni; a.uni_stride = P.max_new > 0 ? P.max_new : 1;
+    a.out_tokens = d_out; a.out_stride = out_stride;
+    a.logits_out = s.d_logits;
+    a.sp = P;
+    a.n_rows = n;
+    a.row_slot = s.mk_rows;
+    a.bookkeep = bookkeep ? 1 : 0;
+    a.xq = s.mk_xq; a.xkv = s.mk_xkv; a.xx2 = s.mk_xx2; a.xh = s.mk_xh; a.xx = s.mk_xx;
+    a.xpart = s.mk_xpart; a.cand_hdr = s.mk_hdr; a.xacc = s.mk_xacc; a.maxc = mk_maxc(m.ctx, m.hd);
+    a.cand_val = s.mk_cval; a.cand_idx = s.mk_cidx;
+    a.stepdone = s.mk_stepdone; a.err = s.mk_err;
+    a.gstep0 = s.mk_gstep; a.nsteps = nsteps;
+    a.trace = s.mk_trace; a.trace_steps = s.mk_trace_steps;
+    const size_t smem = mk_smem(m, MR, nW, nstage);
+    void* args[] = {&a};
+    const void* f = MR == 1 ? (const void*)k_decode_mega<1>
+                  : MR == 2 ? (const void*)k_decode_mega<2>
+                  : MR == 4 ? (const void*)k_decode_mega<4>
+                            : (const void*)k_decode_mega<8>;
+    CK(cudaLaunchCooperativeKernel(f, dim3(nW), dim3(MK_THREADS), args, smem, s.stream));
+    s.stats.kernel_launches++;
+    s.stats.decode_steps += nsteps;
+    s.mk_gstep += nsteps;
+}
+
+// Host check of the persistent kernel's error flag (after a synchronize);
+// resets its state and fails with FB2_TIMEOUT when a bounded wait expired.
+static void mk_check(DeviceSession& s) {
+    if (!s.mk_use) return;
+    int err = 0;
+    CK(cudaMemcpy(&err, s.mk_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err != 0) {
+        mk_reset(s);
+        CK(cudaStreamSynchronize(s.stream));
+        fail(FB2_TIMEOUT, "persistent decode kernel: a bounded wait expired (code " + std::to_string(err) + ")");
+    }
 }
 
 // Prefill of one chunk: rows described by the uploaded tables.
@@ -838,7 +1053,30 @@ static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
         sample_all();
         CK(cudaGetLastError());
         bool stop = job.cb ? stream_callbacks(0) : false;
-        for (int step = 1; step < max_new && !stop; step++) {
+        int step = 1;
+        // Persistent kernel for every step before the first slide: one launch
+        // (a step per launch when a callback streams tokens; 64-step launches
+        // with an EOS so finished batches stop early).
+        if (!stop && mk_eligible(s, n, sp)) {
+            const int mk_end = std::min(max_new, slide_at[order[0]]);
+            while (step < mk_end && !stop) {
+                int ns = mk_end - step;
+                if (job.cb) ns = 1;
+                else if (sp.eos_id >= 0) ns = std::min(ns, 64);
+                run_mega(s, n, ns, P, d_uni, d_out, max_new, true);
+                step += ns;
+                if (job.cb) stop = stream_callbacks(step - 1);
+                else if (sp.eos_id >= 0 && step < mk_end) {
+                    std::vector<int> hd(n);
+                    CK(cudaMemcpyAsync(hd.data(), s.d_done, n * sizeof(int), cudaMemcpyDeviceToHost, s.stream));
+                    CK(cudaStreamSynchronize(s.stream));
+                    bool all_done = true;
+                    for (int i = 0; i < n; i++) all_done = all_done && hd[i];
+                    if (all_done) stop = true;
+                }
+            }
+        }
+        for (; step < max_new && !stop; step++) {
             // slots with slide_at <= step re-prefill; the rest decode
             int k = 0;
             while (k < n && slide_at[order[k]] <= step) k++;
@@ -875,6 +1113,7 @@ static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
     if (max_new > 0)
         CK(cudaMemcpyAsync(job.out_tokens, d_out, (size_t)n * max_new * sizeof(int), cudaMemcpyDeviceToHost, s.stream));
     CK(cudaStreamSynchronize(s.stream));
+    mk_check(s);
     float ms = 0.f;
     if (cudaEventElapsedTime(&ms, s.ev0, s.ev1) == cudaSuccess) s.stats.decode_ms += ms;
     for (int i = 0; i < n; i++) {
@@ -1036,11 +1275,14 @@ int32_t fb2_model_create(const fb2_model_desc* desc, const float* const* params,
                 }
                 D.lnf_w = D.p[2 + 12 * d.n_layers];
                 D.lnf_b = D.p[3 + 12 * d.n_layers];
+                mk_setup(*m, D, params);
             }
         } catch (...) {
             for (auto& dm : m->devs) {
                 cudaSetDevice(dm.device);
                 dfree(dm.blob);
+                dfree(dm.relaid);
+                dfree(dm.d_mk_layers);
             }
             delete m;
             throw;
@@ -1054,6 +1296,8 @@ void fb2_model_destroy(fb2_model* m) {
     for (auto& dm : m->devs) {
         cudaSetDevice(dm.device);
         dfree(dm.blob);
+        dfree(dm.relaid);
+        dfree(dm.d_mk_layers);
     }
     delete m;
 }
@@ -1129,6 +1373,7 @@ int32_t fb2_session_create(fb2_model* m, int32_t max_seqs, fb2_session** out) {
                 CK(cudaMemset(s->d_tickets, 0, 4096 * 4));
                 s->rngs.assign(cnt, DotNetRandom(0));
                 s->stats.device_count = nd;
+                mk_session_alloc(*s);
             }
         } catch (...) {
             for (auto s : S->ds) session_free(s);
@@ -1374,10 +1619,17 @@ int32_t fb2_teacher_forced_logits(fb2_session* S, int32_t n_seqs, const int32_t*
             plan_prefill(s, all, wl, tab, plans);
             upload_tables(s, tab, nullptr);
             for (const ChunkPlan& c : plans) run_prefill_chunk(s, c, s.d_tab);
+            fb2_sampling greedy{};
+            greedy.temperature = 0.0f;
+            greedy.repetition_penalty = 1.0f;
+            greedy.eos_id = -1;
+            greedy.max_new_tokens = 1;
+            const bool mk = mk_eligible(s, n, greedy);
             for (int st = 0; st < steps; st++) {
                 if (st > 0) {
                     s.stats.kernel_launches++; k_bump_len<<<ceil_div(n, 128), 128, 0, s.stream>>>(n, s.d_len);
-                    run_decode_step(s, n);
+                    if (mk) run_mega(s, n, 1, to_params(greedy), nullptr, nullptr, 1, false);
+                    else run_decode_step(s, n);
                 }
                 CK(cudaGetLastError());
                 for (int i = 0; i < n; i++)
@@ -1582,6 +1834,24 @@ int32_t fb2_forward_last_logits_noalloc(fb2_model* m, int32_t device_slot, int32
 }
 
 // ---- test hooks (not part of the reference surface) -------------------------
+// Copies the persistent kernel's per-phase %globaltimer stamps of its last
+// traced launch (FORGE_B200_MK_TRACE=<steps> at session creation) into out:
+// [CTAs][steps][64] uint64; *n_ctas / *n_steps receive the shape.
+int32_t fb2_test_mk_trace(fb2_session* S, uint64_t* out, int64_t capacity, int32_t* n_ctas, int32_t* n_steps) {
+    return guarded([&] {
+        if (!S || !n_ctas || !n_steps) fail(FB2_INVALID_ARG, "NULL argument");
+        DeviceSession& s = *S->ds[0];
+        *n_ctas = s.mk_trace ? s.dm->mk_nW : 0;
+        *n_steps = s.mk_trace ? s.mk_trace_steps : 0;
+        if (!s.mk_trace || !out) return;
+        const size_t n = (size_t)s.dm->mk_nW * s.mk_trace_steps * MK_TRACE_POINTS;
+        if ((size_t)capacity < n) fail(FB2_INVALID_ARG, "capacity too small");
+        DeviceGuard g(s.device);
+        CK(cudaStreamSynchronize(s.stream));
+        CK(cudaMemcpy(out, s.mk_trace, n * 8, cudaMemcpyDeviceToHost));
+    });
+}
+
 // n successive NextDouble() values of `new Random(seed)` as the library
 // restates it (host code; needs no device).
 int32_t fb2_test_dotnet_random(int32_t seed, int32_t n, double* out) {

@@ -27,6 +27,13 @@ int32_t fb2_test_expf_hash(uint32_t lo_bits, int32_t nchunks, uint64_t* hashes);
  * FB2_RNG_SEEDS mode draws them (host only; no device needed). */
 int32_t fb2_test_dotnet_random(int32_t seed, int32_t n, double* out);
 
+struct fb2_session;
+/* The persistent decode kernel's per-phase %globaltimer stamps of the first
+ * steps of its last launch, when the session was created with
+ * FORGE_B200_MK_TRACE=<steps>: out is [CTAs][steps][64] uint64. */
+int32_t fb2_test_mk_trace(struct fb2_session* s, uint64_t* out, int64_t capacity, int32_t* n_ctas,
+                          int32_t* n_steps);
+
 #ifdef __cplusplus
 }
 #endif
