@@ -429,9 +429,14 @@ inline size_t mk_aux_bytes(int MR, int D, int F, int H, int ctx, int slice_max, 
         if (a.trace && tid == 0 && s < a.trace_steps && (pt) < MK_TRACE_POINTS)                     \
             a.trace[((size_t)cta * a.trace_steps + s) * MK_TRACE_POINTS + (pt)] = gtimer();          \
     } while (0)
+#define MK_TRACE_ANY(pt)                                                                             \
+    do {                                                                                             \
+        if (a.trace && s < a.trace_steps && (pt) < MK_TRACE_POINTS)                                  \
+            a.trace[((size_t)cta * a.trace_steps + s) * MK_TRACE_POINTS + (pt)] = gtimer();          \
+    } while (0)
 #define MK_TRACE_L(off)                  \
     do {                                 \
-        if (l < 2) MK_TRACE(l * 12 + (off)); \
+        if (l < 1) MK_TRACE(l * 12 + (off)); \
     } while (0)
 
 // ---- the kernel ---------------------------------------------------------------
@@ -559,18 +564,20 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     }
                     asm volatile("fence.proxy.async.global;" ::: "memory");
                 }
-                int u = 0;
+                // units u = (m, h, c) in row-major order; this CTA owns u = cta (mod nW)
+                int ubase = 0;
                 for (int m = 0; m < MR && ok; m++) {
-                    const int nc = nch_of(m, s), old = pos_of(m, s) - 1;
-                    for (int h = 0; h < H && ok; h++)
-                        for (int c = 0; c < nc && ok; c++, u++) {
-                            if (u % nW != cta) continue;
-                            const int nk = min(KC, old - c * KC);
-                            const float* kb = a.kv + (size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
-                                              ((size_t)h * a.ctx + c * KC) * hd;
-                            issue(kb, (uint32_t)(nk * hd * 4));
-                            issue(kb + a.v_offset, (uint32_t)(nk * hd * 4));
-                        }
+                    const int nc = nch_of(m, s), old = pos_of(m, s) - 1, nu = H * nc;
+                    for (int u = ubase + ((cta - ubase) % nW + nW) % nW; u < ubase + nu && ok; u += nW) {
+                        const int h = (u - ubase) / nc, c = (u - ubase) - h * nc;
+                        if (l == 1 && u == cta) MK_TRACE_ANY(63);
+                        const int nk = min(KC, old - c * KC);
+                        const float* kb = a.kv + (size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
+                                          ((size_t)h * a.ctx + c * KC) * hd;
+                        issue(kb, (uint32_t)(nk * hd * 4));
+                        issue(kb + a.v_offset, (uint32_t)(nk * hd * 4));
+                    }
+                    ubase += nu;
                 }
                 issue_strip(ly.w[MK_PROJ], D, D);
                 issue_strip(ly.w[MK_FC], D, F);
@@ -706,16 +713,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 float* qs = scr;         // [hd]
                 float* sc = scr + 128;   // [KC]
                 float* st2 = scr + 300;  // [2]
-                int u = 0;
                 for (int m = 0; m < MR; m++) {
-                    const int nc = nch_of(m, s), old = pos_of(m, s) - 1;
-                    for (int h = 0; h < H; h++)
-                        for (int c = 0; c < nc; c++, u++) {
-                            if (u % nW != cta) continue;
+                    const int nc = nch_of(m, s), old = pos_of(m, s) - 1, ubase = s_ubase[m];
+                    for (int u = ubase + ((cta - ubase) % nW + nW) % nW; u < ubase + H * nc; u += nW) {
+                        {
+                            const int h = (u - ubase) / nc, c = (u - ubase) - h * nc;
                             const int nk = min(KC, old - c * KC);
                             if (tid < hd) qs[tid] = wait_pair(a.xq + m * D + h * hd + tid, tg, a.err, &s_abort);
                             cons_sync();
+                            if (l < 2 && u == cta) MK_TRACE(57 + 3 * l);
                             wait_full(full, it, a.nstage, a.err, &s_abort);
+                            if (l < 2 && u == cta) MK_TRACE(58 + 3 * l);
                             const float* Kt = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
                             const int dpt = hd / 4, part = tid & 3;
                             for (int j0 = 0; j0 < nk; j0 += MK_CONS / 4) {
@@ -750,6 +758,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                             }
                             cons_sync();
                             wait_full(full, it, a.nstage, a.err, &s_abort);
+                            if (l < 2 && u == cta) MK_TRACE(59 + 3 * l);
                             const float* Vt = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
                             {
                                 const int G2 = MK_CONS / hd, d = tid % hd, grp = tid / hd;
@@ -757,9 +766,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                                 for (int j = grp; j < nk; j += G2) accv += sc[j] * Vt[j * hd + d];
                                 red[tid] = accv;
                             }
+                            if (l == 0 && u == cta) MK_TRACE(12);
                             release_stage(empty, it, a.nstage);
                             it++;
                             cons_sync();
+                            if (l == 0 && u == cta) MK_TRACE(13);
                             // partial record [max, sum, acc[hd]], every word tagged
                             unsigned long long* pr = a.xpart + (size_t)u * (hd + 2);
                             if (tid < hd) {
@@ -772,7 +783,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                                 st_pair(pr + 1, st2[1], tg);
                             }
                             cons_sync();
+                            if (l == 0 && u == cta) MK_TRACE(14);
                         }
+                    }
                 }
             }
             MK_TRACE_L(3);
@@ -798,7 +811,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                         kp[e] = vp[e] = 0.f;
                     }
                     if (on) {
-                        for (int e = 0; e < dpl; e++) {
+#pragma unroll
+                        for (int e = 0; e < 8; e++) {
+                            if (e >= dpl) break;
                             wq[e] = ld_pair(a.xq + dq + e);
                             wk[e] = ld_pair(a.xkv + dk + e);
                             wv[e] = ld_pair(a.xkv + dk + D + e);
@@ -806,7 +821,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                         if (pos >= 1) {
                             const float* kb = a.kv + (size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
                                               ((size_t)h * a.ctx + pos - 1) * hd + l8 * dpl;
-                            for (int e = 0; e < dpl; e++) {
+#pragma unroll
+                            for (int e = 0; e < 8; e++) {
+                                if (e >= dpl) break;
                                 kp[e] = __ldcg(kb + e);
                                 vp[e] = __ldcg(kb + a.v_offset + e);
                             }
@@ -911,7 +928,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                             const int c = l8 + 8 * c4;
                             if (c < nc) wts_m[(size_t)p * a.maxc + c] = mc[c4] * inv;
                         }
-                        for (int e = 0; e < dpl; e++) act[dq + e] = (wcur * vc[e] + wprev * vp[e]) * inv;
+#pragma unroll
+                        for (int e = 0; e < 8; e++)
+                            if (e < dpl) act[dq + e] = (wcur * vc[e] + wprev * vp[e]) * inv;
                     }
                 }
             }
