@@ -89,6 +89,7 @@ struct MkArgs {
 // proj2), 24 step start, 25 head input, 27 head logits, 28 candidates,
 // 30 published, 31 token known, 32 step end, 33 + l end of layer l.
 constexpr int MK_TRACE_POINTS = 64;
+constexpr int MK_ERR_LAYOUT = 16;  // error code: a shared-memory region would be misaligned
 
 // ---- small PTX helpers ------------------------------------------------------
 FB2_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -220,7 +221,7 @@ FB2_DEV float pair_value(unsigned long long w) { return __uint_as_float((uint32_
 
 // dst[i] = value of src[i] for i < n once every word carries `tag`: each
 // thread loads up to 16 words, then waits on them together.
-FB2_DEV void gather_tagged(const unsigned long long* src, float* dst, int n, uint32_t tag, int* err,
+__device__ __noinline__ void gather_tagged(const unsigned long long* src, float* dst, int n, uint32_t tag, int* err,
                            volatile int* abort_flag) {
     for (int base = 0; base < n; base += 16 * MK_CONS) {
         unsigned long long w[16];
@@ -386,7 +387,7 @@ FB2_DEV float cons_sum_slot(float v, float* slot) {
 // (shared), CpuBackend.cs:377-398.  `slots` = 16*MR floats of scratch that
 // stay untouched until the next barrier-separated phase.
 template <int MR>
-FB2_DEV void mk_layernorm(const float* src, float* dst, int D, const LnRegs& p, float* slots) {
+__device__ __noinline__ void mk_layernorm(const float* src, float* dst, int D, const LnRegs p, float* slots) {
 #pragma unroll 1
     for (int m = 0; m < MR; m++) {
         const float* x = src + m * D;
@@ -418,7 +419,7 @@ FB2_DEV void mk_layernorm(const float* src, float* dst, int D, const LnRegs& p, 
 
 // Shared-memory bytes the kernel needs besides the ring.
 inline size_t mk_aux_bytes(int MR, int D, int F, int H, int ctx, int slice_max, int maxc, int nstage) {
-    size_t floats = (size_t)MR * F + 2 * (size_t)MR * D + (size_t)MR * 256 + (size_t)MR * slice_max + 512;
+    size_t floats = (size_t)MR * F + 2 * (size_t)MR * D + (size_t)MR * 256 + (size_t)MR * slice_max + 512 + 512;
     size_t ints = 2048 + (size_t)MR * ctx;
     size_t wts = 2 * (size_t)MR * H * maxc;
     return 2 * (size_t)nstage * 8 + floats * 4 + ints * 4 + MK_SURV_MAX * 8 + wts * 4;
@@ -456,7 +457,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     float* red = x2res + MR * D;                               // [MR][256]
     float* slice = red + MR * 256;                             // [MR][slice_max]
     float* scr = slice + MR * a.slice_max;                     // [512]
-    int* iscr = reinterpret_cast<int*>(scr + 512);             // [2048]
+    float* uacc = scr + 512;                                   // [8][64] attention unit: per-warp p.V
+    int* iscr = reinterpret_cast<int*>(uacc + 512);            // [2048]
     int* win = iscr + 2048;                                    // [MR][ctx]
     float* surv_v = reinterpret_cast<float*>(win + MR * a.ctx);  // [MK_SURV_MAX]
     int* surv_i = reinterpret_cast<int*>(surv_v + MK_SURV_MAX);  // [MK_SURV_MAX]
@@ -477,6 +479,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     __shared__ int s_len0[MK_MAX_ROWS], s_dead[MK_MAX_ROWS], s_dummy[MK_MAX_ROWS], s_ubase[MK_MAX_ROWS + 1];
     __shared__ volatile int s_abort;
 
+    // float4 accesses to the scratch regions need slice_max % 4 == 0
+    if ((a.slice_max & 3) != 0) {
+        if (tid == 0) atomicExch(a.err, MK_ERR_LAYOUT);
+        return;
+    }
     if (tid < MR) {
         const int m = tid;
         const bool dummy = m >= a.n_rows;
@@ -612,41 +619,76 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     cons_sync();
 
     // This CTA's column strip of y = act * W (+ epilogue(m, n, sum)).
-    auto gemv = [&](const float* actv, const float* Wt, int K, int N, auto&& epilogue) {
-        (void)Wt;
+    // This CTA's column strip of y = act * W, then epilogue(m, n, sum) once
+    // per output.  Row groups g (of G) accumulate four independent partial
+    // sums; the G partials of a column are reduced by one warp (shuffles) when
+    // G is large, else serially.  No trailing barrier: every caller's next
+    // phase starts with a barrier before `red` is written again.
+    auto gemv = [&](const float* actv, int K, int N, auto&& epilogue) {
         int n0, w;
         strip(N, nW, cta, n0, w);
         const int R = strip_rows(w, K);
         if (R == 0) return;
         const int G = MK_CONS / w, g = tid / w, c = tid - g * w;
         const bool valid = tid < G * w;
-        float acc[MR];
+        float acc[MR][4];
 #pragma unroll
-        for (int m = 0; m < MR; m++) acc[m] = 0.f;
+        for (int m = 0; m < MR; m++) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
         for (int r0 = 0; r0 < K; r0 += R) {
             const int rows = min(R, K - r0);
             wait_full(full, it, a.nstage, a.err, &s_abort);
             const float* st = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
             if (valid) {
-                for (int r = g; r < rows; r += G) {
+                const float* av = actv + r0;
+                int r = g;
+                for (; r + 3 * G < rows; r += 4 * G) {
+                    const float v0 = st[r * w + c], v1 = st[(r + G) * w + c];
+                    const float v2 = st[(r + 2 * G) * w + c], v3 = st[(r + 3 * G) * w + c];
+#pragma unroll
+                    for (int m = 0; m < MR; m++) {
+                        acc[m][0] += av[m * K + r] * v0;
+                        acc[m][1] += av[m * K + r + G] * v1;
+                        acc[m][2] += av[m * K + r + 2 * G] * v2;
+                        acc[m][3] += av[m * K + r + 3 * G] * v3;
+                    }
+                }
+                for (; r < rows; r += G) {
                     const float v = st[r * w + c];
 #pragma unroll
-                    for (int m = 0; m < MR; m++) acc[m] += actv[m * K + r0 + r] * v;
+                    for (int m = 0; m < MR; m++) acc[m][0] += av[m * K + r] * v;
                 }
             }
             release_stage(empty, it, a.nstage);
             it++;
         }
 #pragma unroll
-        for (int m = 0; m < MR; m++) red[m * 256 + tid] = valid ? acc[m] : 0.f;
+        for (int m = 0; m < MR; m++)
+            red[m * 256 + tid] = valid ? (acc[m][0] + acc[m][1]) + (acc[m][2] + acc[m][3]) : 0.f;
         cons_sync();
-        if (tid < w * MR) {
+        const int np = MR * w;  // outputs of this strip
+        if (G >= 24 && np <= 32) {
+            // one warp per output: lanes sum G partials, then shuffle
+            for (int p = warp; p < np; p += 8) {
+                const int m = p / w, cc = p - m * w;
+                float t = 0.f;
+                for (int gg = lane; gg < G; gg += 32) t += red[m * 256 + gg * w + cc];
+                t = warp_sum(t);
+                if (lane == 0) epilogue(m, n0 + cc, t);
+            }
+        } else if (tid < np) {
             const int m = tid / w, cc = tid - m * w;
-            float sum = 0.f;
-            for (int gg = 0; gg < G; gg++) sum += red[m * 256 + gg * w + cc];
-            epilogue(m, n0 + cc, sum);
+            const float* rp = red + m * 256 + cc;
+            float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+            int gg = 0;
+            for (; gg + 3 < G; gg += 4) {
+                t0 += rp[gg * w];
+                t1 += rp[(gg + 1) * w];
+                t2 += rp[(gg + 2) * w];
+                t3 += rp[(gg + 3) * w];
+            }
+            for (; gg < G; gg++) t0 += rp[gg * w];
+            epilogue(m, n0 + cc, (t0 + t1) + (t2 + t3));
         }
-        cons_sync();
     };
 
     for (int s = 0; s < a.nsteps; s++) {
@@ -705,85 +747,85 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                              ((size_t)h * a.ctx + pos_of(m, s)) * hd + d] = v;
                     st_pair(a.xkv + (size_t)m * 2 * D + (n - D), v, tg);
                 };
-                gemv(act, ly.w[MK_QKV], D, 3 * D, epi);
+                gemv(act, D, 3 * D, epi);
                 MK_TRACE_L(2);
             }
             // ---- level B: attention units over the cached keys [0, pos-1) -----
+            // Unit (m, h, c) = keys [c*KC, c*KC + nk) of head h.  Warp w takes
+            // KC/8 keys (lpk lanes per key, 16 dims a lane), keeps its own
+            // max / sum / p.V, and the 8 warps merge once at the end.
             {
-                float* qs = scr;         // [hd]
-                float* sc = scr + 128;   // [KC]
-                float* st2 = scr + 300;  // [2]
+                float* qs = scr;                  // [hd]
+                float* wm = scr + 128;            // [8] warp max
+                float* wl = scr + 136;            // [8] warp sum
+                float* wacc = uacc;               // [8][hd] warp p.V
+                const int kpw = KC / 8, lpk = 32 / kpw;  // keys per warp, lanes per key (16 dims a lane)
+                const int kw = lane / lpk, part = lane - kw * lpk;
                 for (int m = 0; m < MR; m++) {
                     const int nc = nch_of(m, s), old = pos_of(m, s) - 1, ubase = s_ubase[m];
                     for (int u = ubase + ((cta - ubase) % nW + nW) % nW; u < ubase + H * nc; u += nW) {
-                        {
-                            const int h = (u - ubase) / nc, c = (u - ubase) - h * nc;
-                            const int nk = min(KC, old - c * KC);
-                            if (tid < hd) qs[tid] = wait_pair(a.xq + m * D + h * hd + tid, tg, a.err, &s_abort);
-                            cons_sync();
-                            if (l < 2 && u == cta) MK_TRACE(57 + 3 * l);
-                            wait_full(full, it, a.nstage, a.err, &s_abort);
-                            if (l < 2 && u == cta) MK_TRACE(58 + 3 * l);
-                            const float* Kt = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
-                            const int dpt = hd / 4, part = tid & 3;
-                            for (int j0 = 0; j0 < nk; j0 += MK_CONS / 4) {
-                                const int j = j0 + (tid >> 2);
-                                float d = 0.f;
-                                if (j < nk) {
-                                    const float* kr = Kt + j * hd + part * dpt;
-                                    for (int e = 0; e < dpt; e++) d += qs[part * dpt + e] * kr[e];
-                                }
-                                d += __shfl_xor_sync(0xffffffffu, d, 1);
-                                d += __shfl_xor_sync(0xffffffffu, d, 2);
-                                if (j < nk && part == 0) sc[j] = d * scale;
+                        const int h = (u - ubase) / nc, c = (u - ubase) - h * nc;
+                        const int nk = min(KC, old - c * KC);
+                        if (tid < hd) qs[tid] = wait_pair(a.xq + m * D + h * hd + tid, tg, a.err, &s_abort);
+                        cons_sync();
+                        wait_full(full, it, a.nstage, a.err, &s_abort);
+                        const float* Kt = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
+                        const int j = warp * kpw + kw;  // this lane's key
+                        float d = 0.f;
+                        if (j < nk) {
+                            const float4* kr = reinterpret_cast<const float4*>(Kt + j * hd) + part;
+                            const float4* qr = reinterpret_cast<const float4*>(qs) + part;
+#pragma unroll
+                            for (int e4 = 0; e4 < 4; e4++) {  // dims 4*(part + lpk*e4) .. +3
+                                const float4 k4 = kr[lpk * e4], q4 = qr[lpk * e4];
+                                d += q4.x * k4.x + q4.y * k4.y + q4.z * k4.z + q4.w * k4.w;
                             }
-                            release_stage(empty, it, a.nstage);
-                            it++;
-                            cons_sync();
-                            if (warp == 0) {
-                                float mx = -INFINITY;
-                                for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sc[j]);
-                                mx = warp_max(mx);
-                                float lsum = 0.f;
-                                for (int j = lane; j < nk; j += 32) {
-                                    const float p = __expf(sc[j] - mx);
-                                    sc[j] = p;
-                                    lsum += p;
-                                }
-                                lsum = warp_sum(lsum);
-                                if (lane == 0) {
-                                    st2[0] = mx;
-                                    st2[1] = lsum;
-                                }
+                        }
+                        for (int o = 1; o < lpk; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                        const float sc = j < nk ? d * scale : -INFINITY;
+                        release_stage(empty, it, a.nstage);
+                        it++;
+                        const float mw = warp_max(sc);
+                        const float p = j < nk ? __expf(sc - mw) : 0.f;
+                        const float lw = warp_sum(part == 0 ? p : 0.f);
+                        wait_full(full, it, a.nstage, a.err, &s_abort);
+                        const float* Vt = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
+                        float a0 = 0.f, a1 = 0.f;
+                        for (int kk = 0; kk < kpw; kk++) {
+                            const float pk = __shfl_sync(0xffffffffu, p, kk * lpk);
+                            const int jj = warp * kpw + kk;
+                            if (jj < nk) {
+                                a0 += pk * Vt[jj * hd + lane];
+                                if (hd > 32) a1 += pk * Vt[jj * hd + lane + 32];
                             }
-                            cons_sync();
-                            wait_full(full, it, a.nstage, a.err, &s_abort);
-                            if (l < 2 && u == cta) MK_TRACE(59 + 3 * l);
-                            const float* Vt = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
-                            {
-                                const int G2 = MK_CONS / hd, d = tid % hd, grp = tid / hd;
-                                float accv = 0.f;
-                                for (int j = grp; j < nk; j += G2) accv += sc[j] * Vt[j * hd + d];
-                                red[tid] = accv;
+                        }
+                        release_stage(empty, it, a.nstage);
+                        it++;
+                        wacc[warp * hd + lane] = a0;
+                        if (hd > 32) wacc[warp * hd + lane + 32] = a1;
+                        if (lane == 0) {
+                            wm[warp] = mw;
+                            wl[warp] = lw;
+                        }
+                        cons_sync();
+                        // partial record [max, sum, acc[hd]], every word tagged
+                        if (tid < hd) {
+                            float M = -INFINITY;
+#pragma unroll
+                            for (int w8 = 0; w8 < 8; w8++) M = fmaxf(M, wm[w8]);
+                            float L = 0.f, A = 0.f;
+#pragma unroll
+                            for (int w8 = 0; w8 < 8; w8++) {
+                                const float f = wm[w8] == -INFINITY ? 0.f : __expf(wm[w8] - M);
+                                L += wl[w8] * f;
+                                A += wacc[w8 * hd + tid] * f;
                             }
-                            if (l == 0 && u == cta) MK_TRACE(12);
-                            release_stage(empty, it, a.nstage);
-                            it++;
-                            cons_sync();
-                            if (l == 0 && u == cta) MK_TRACE(13);
-                            // partial record [max, sum, acc[hd]], every word tagged
                             unsigned long long* pr = a.xpart + (size_t)u * (hd + 2);
-                            if (tid < hd) {
-                                float t = 0.f;
-                                for (int gg = 0; gg < MK_CONS / hd; gg++) t += red[gg * hd + tid];
-                                st_pair(pr + 2 + tid, t, tg);
-                            }
+                            st_pair(pr + 2 + tid, A, tg);
                             if (tid == 0) {
-                                st_pair(pr, st2[0], tg);
-                                st_pair(pr + 1, st2[1], tg);
+                                st_pair(pr, M, tg);
+                                st_pair(pr + 1, L, tg);
                             }
-                            cons_sync();
-                            if (l == 0 && u == cta) MK_TRACE(14);
                         }
                     }
                 }
@@ -968,7 +1010,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     st_pair(a.xx2 + m * D + n, (v + pb[MK_PROJ]) + xres[m * D + n], tg);
                 };
                 MK_TRACE_L(5);
-                gemv(act, ly.w[MK_PROJ], D, D, epi);
+                gemv(act, D, D, epi);
                 MK_TRACE_L(6);
             }
             // ---- level D: LN2 -> fc + GELU ---------------------------------------
@@ -981,7 +1023,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     st_pair(a.xh + (size_t)m * F + n, gelu_tanh(v + pb[MK_FC]), tg);
                 };
                 MK_TRACE_L(8);
-                gemv(act, ly.w[MK_FC], D, F, epi);
+                gemv(act, D, F, epi);
                 MK_TRACE_L(9);
             }
             // ---- level E: proj2 + residual ----------------------------------------
@@ -992,7 +1034,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     st_pair(a.xx + m * D + n, (v + pb[MK_PROJ2]) + x2res[m * D + n], tg);
                 };
                 MK_TRACE_L(10);
-                gemv(act, ly.w[MK_PROJ2], F, D, epi);
+                gemv(act, F, D, epi);
                 MK_TRACE_L(11);
                 if (l < 24) MK_TRACE(33 + l);
             }

@@ -184,7 +184,9 @@ static void configure_kernels(int dev) {
 // ---------------------------------------------------------------------------
 static int mk_keys_per_chunk(int hd) { return MK_STAGE / (hd * 4); }
 static int mk_maxc(int ctx, int hd) { return ceil_div(ctx, mk_keys_per_chunk(hd)); }
-static int mk_slice_max(int V, int nW) { return ceil_div(V, nW); }
+// Vocabulary entries per CTA slice, rounded up to a multiple of 4 so every
+// shared-memory region after the slices stays 16-byte aligned.
+static int mk_slice_max(int V, int nW) { return (ceil_div(V, nW) + 3) & ~3; }
 
 // Dynamic shared memory of k_decode_mega<MR> with `nstage` ring stages.
 static size_t mk_smem(const fb2_model& m, int MR, int nW, int nstage) {
@@ -672,6 +674,7 @@ static void mk_check(DeviceSession& s) {
     if (err != 0) {
         mk_reset(s);
         CK(cudaStreamSynchronize(s.stream));
+        if (err == MK_ERR_LAYOUT) fail(FB2_CUDA_ERROR, "persistent decode kernel: shared-memory layout not 16-byte aligned");
         fail(FB2_TIMEOUT, "persistent decode kernel: a bounded wait expired (code " + std::to_string(err) + ")");
     }
 }

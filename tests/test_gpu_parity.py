@@ -181,6 +181,32 @@ def test_generate_sampled_controls(pkg, O):
     check_ids(O, ocfg, params, prompt, got, want)
 
 
+def test_forge98m_vocabulary_persistent_and_graph_paths(pkg, O, monkeypatch):
+    """The Forge-98M vocabulary (V 16384: 148 slices of 111 entries) on a
+    small body, through the persistent decode kernel and, with
+    FORGE_B200_DECODE=graph, through the CUDA-graph step: teacher-forced
+    logits and sampled ids with every repetition control."""
+    shape = (16384, 160, 128, 2, 2)
+    ocfg = O.Config(*shape)
+    params = O.init_params(ocfg, 21)
+    rng = np.random.default_rng(8)
+    prompt = rng.integers(0, shape[0], 40).astype(np.int32)
+    toks = rng.integers(0, shape[0], (1, 72)).astype(np.int32)
+    want = O.generate(ocfg, params, prompt, 90, 0.7, 30, O.DotNetRandom(5), repetition_penalty=1.1,
+                      no_repeat_ngram=4)
+    for mode in ("persistent", "graph"):
+        if mode == "graph":
+            monkeypatch.setenv("FORGE_B200_DECODE", "graph")
+        be = pkg.B200Backend(pkg.ModelConfig(*shape), params, devices=[0])
+        with be:
+            got = be.generate(prompt.tolist(), 90, 0.7, 30, pkg.DotNetRandom(5), repetition_penalty=1.1,
+                              no_repeat_ngram_size=4)
+            tf = be.teacher_forced_logits(toks, 40)
+        check_ids(O, ocfg, params, prompt, got, want)
+        for k in (0, 13, 31):
+            assert relerr(tf[0, k], O.forward_last(ocfg, params, toks[0, :40 + k])) <= TOL, (mode, k)
+
+
 def test_generate_batch_ragged_and_long_prompts(pkg, O):
     shape = (300, 24, 32, 2, 2)
     ocfg, params, be = make(pkg, O, shape, 9, max_seqs=5)
