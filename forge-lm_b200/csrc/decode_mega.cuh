@@ -425,6 +425,81 @@ inline size_t mk_aux_bytes(int MR, int D, int F, int H, int ctx, int slice_max, 
     return 2 * (size_t)nstage * 8 + floats * 4 + ints * 4 + MK_SURV_MAX * 8 + wts * 4;
 }
 
+// y[m][c] = sum_k act[m][k] * W[k][n0 + c] over this CTA's strip, with the
+// strip's weights arriving through the ring.  Row groups g (of G) keep four
+// independent partial sums; the G partials of an output are reduced by one
+// warp (shuffles) when G is large, else serially.  Results land in ys[MR*w]
+// behind a barrier.  Returns the ring position after the strip.
+template <int MR>
+__device__ __noinline__ uint32_t mk_gemv_strip(const float* actv, int K, int N, int cta, int nW, unsigned char* ring,
+                                               uint64_t* full, uint64_t* empty, int nstage, uint32_t it, float* red,
+                                               float* ys, int* err, volatile int* abort_flag) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int n0, w;
+    strip(N, nW, cta, n0, w);
+    const int R = strip_rows(w, K);
+    const int G = MK_CONS / w, g = tid / w, c = tid - g * w;
+    const bool valid = tid < G * w;
+    float acc[MR][4];
+#pragma unroll
+    for (int m = 0; m < MR; m++) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
+    for (int r0 = 0; r0 < K; r0 += R) {
+        const int rows = min(R, K - r0);
+        wait_full(full, it, nstage, err, abort_flag);
+        const float* st = reinterpret_cast<const float*>(ring + (size_t)(it % nstage) * MK_STAGE);
+        if (valid) {
+            const float* av = actv + r0;
+            int r = g;
+            for (; r + 3 * G < rows; r += 4 * G) {
+                const float v0 = st[r * w + c], v1 = st[(r + G) * w + c];
+                const float v2 = st[(r + 2 * G) * w + c], v3 = st[(r + 3 * G) * w + c];
+#pragma unroll
+                for (int m = 0; m < MR; m++) {
+                    acc[m][0] += av[m * K + r] * v0;
+                    acc[m][1] += av[m * K + r + G] * v1;
+                    acc[m][2] += av[m * K + r + 2 * G] * v2;
+                    acc[m][3] += av[m * K + r + 3 * G] * v3;
+                }
+            }
+            for (; r < rows; r += G) {
+                const float v = st[r * w + c];
+#pragma unroll
+                for (int m = 0; m < MR; m++) acc[m][0] += av[m * K + r] * v;
+            }
+        }
+        release_stage(empty, it, nstage);
+        it++;
+    }
+#pragma unroll
+    for (int m = 0; m < MR; m++) red[m * 256 + tid] = valid ? (acc[m][0] + acc[m][1]) + (acc[m][2] + acc[m][3]) : 0.f;
+    cons_sync();
+    const int np = MR * w;
+    if (G >= 24 && np <= 32) {
+        for (int p = warp; p < np; p += 8) {
+            const int m = p / w, cc = p - m * w;
+            float t = 0.f;
+            for (int gg = lane; gg < G; gg += 32) t += red[m * 256 + gg * w + cc];
+            t = warp_sum(t);
+            if (lane == 0) ys[p] = t;
+        }
+    } else if (tid < np) {
+        const int m = tid / w, cc = tid - m * w;
+        const float* rp = red + m * 256 + cc;
+        float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+        int gg = 0;
+        for (; gg + 3 < G; gg += 4) {
+            t0 += rp[gg * w];
+            t1 += rp[(gg + 1) * w];
+            t2 += rp[(gg + 2) * w];
+            t3 += rp[(gg + 3) * w];
+        }
+        for (; gg < G; gg++) t0 += rp[gg * w];
+        ys[tid] = (t0 + t1) + (t2 + t3);
+    }
+    cons_sync();
+    return it;
+}
+
 #define MK_TRACE(pt)                                                                                 \
     do {                                                                                             \
         if (a.trace && tid == 0 && s < a.trace_steps && (pt) < MK_TRACE_POINTS)                     \
@@ -620,75 +695,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
 
     // This CTA's column strip of y = act * W (+ epilogue(m, n, sum)).
     // This CTA's column strip of y = act * W, then epilogue(m, n, sum) once
-    // per output.  Row groups g (of G) accumulate four independent partial
-    // sums; the G partials of a column are reduced by one warp (shuffles) when
-    // G is large, else serially.  No trailing barrier: every caller's next
-    // phase starts with a barrier before `red` is written again.
+    // per output (one shared, out-of-line copy of the strip code).
     auto gemv = [&](const float* actv, int K, int N, auto&& epilogue) {
         int n0, w;
         strip(N, nW, cta, n0, w);
-        const int R = strip_rows(w, K);
-        if (R == 0) return;
-        const int G = MK_CONS / w, g = tid / w, c = tid - g * w;
-        const bool valid = tid < G * w;
-        float acc[MR][4];
-#pragma unroll
-        for (int m = 0; m < MR; m++) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
-        for (int r0 = 0; r0 < K; r0 += R) {
-            const int rows = min(R, K - r0);
-            wait_full(full, it, a.nstage, a.err, &s_abort);
-            const float* st = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
-            if (valid) {
-                const float* av = actv + r0;
-                int r = g;
-                for (; r + 3 * G < rows; r += 4 * G) {
-                    const float v0 = st[r * w + c], v1 = st[(r + G) * w + c];
-                    const float v2 = st[(r + 2 * G) * w + c], v3 = st[(r + 3 * G) * w + c];
-#pragma unroll
-                    for (int m = 0; m < MR; m++) {
-                        acc[m][0] += av[m * K + r] * v0;
-                        acc[m][1] += av[m * K + r + G] * v1;
-                        acc[m][2] += av[m * K + r + 2 * G] * v2;
-                        acc[m][3] += av[m * K + r + 3 * G] * v3;
-                    }
-                }
-                for (; r < rows; r += G) {
-                    const float v = st[r * w + c];
-#pragma unroll
-                    for (int m = 0; m < MR; m++) acc[m][0] += av[m * K + r] * v;
-                }
-            }
-            release_stage(empty, it, a.nstage);
-            it++;
-        }
-#pragma unroll
-        for (int m = 0; m < MR; m++)
-            red[m * 256 + tid] = valid ? (acc[m][0] + acc[m][1]) + (acc[m][2] + acc[m][3]) : 0.f;
-        cons_sync();
-        const int np = MR * w;  // outputs of this strip
-        if (G >= 24 && np <= 32) {
-            // one warp per output: lanes sum G partials, then shuffle
-            for (int p = warp; p < np; p += 8) {
-                const int m = p / w, cc = p - m * w;
-                float t = 0.f;
-                for (int gg = lane; gg < G; gg += 32) t += red[m * 256 + gg * w + cc];
-                t = warp_sum(t);
-                if (lane == 0) epilogue(m, n0 + cc, t);
-            }
-        } else if (tid < np) {
-            const int m = tid / w, cc = tid - m * w;
-            const float* rp = red + m * 256 + cc;
-            float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
-            int gg = 0;
-            for (; gg + 3 < G; gg += 4) {
-                t0 += rp[gg * w];
-                t1 += rp[(gg + 1) * w];
-                t2 += rp[(gg + 2) * w];
-                t3 += rp[(gg + 3) * w];
-            }
-            for (; gg < G; gg++) t0 += rp[gg * w];
-            epilogue(m, n0 + cc, (t0 + t1) + (t2 + t3));
-        }
+        if (w <= 0) return;
+        it = mk_gemv_strip<MR>(actv, K, N, cta, nW, ring, full, empty, a.nstage, it, red, uacc, a.err, &s_abort);
+        for (int p = tid; p < MR * w; p += MK_CONS) epilogue(p / w, n0 + p % w, uacc[p]);
     };
 
     for (int s = 0; s < a.nsteps; s++) {

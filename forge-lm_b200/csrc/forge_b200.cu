@@ -220,6 +220,7 @@ static void mk_setup(const fb2_model& m, DeviceModel& dm, const float* const* pa
     if (m.V <= m.ctx) return;  // the ban of a whole window could then cover the vocabulary
     if (mk_slice_max(m.V, nW) > MK_SLICE_MAX || nW > 256) return;
     if (m.D * 4 > MK_STAGE) return;
+    if (8 * ceil_div(4 * m.D, nW) > 512) return;  // strip outputs staged in a 512-float scratch
     if (mk_nstage(m, 1, nW, dm.device) == 0) return;
     const size_t D = m.D, F = m.F;
     const size_t per_layer = 3 * D * D + D * D + D * F + F * D;
