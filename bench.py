@@ -75,14 +75,18 @@ def prompts_for(first: int, count: int, plen: int, vocab: int) -> list[np.ndarra
     return [np.random.default_rng(42 + first + i).integers(0, vocab, plen).astype(np.int32) for i in range(count)]
 
 
-def algorithmic_bytes_per_token(m: dict, T: int) -> float:
-    """Bytes one decode step must move for one sequence whose attention spans
-    T keys: every block weight and bias, ln_f, the tied head (tok_emb), the
-    token and position rows, and the K/V cache of T positions."""
+def weight_bytes(m: dict) -> float:
+    """Bytes of every parameter one decode step streams once (shared by all
+    sequences of the step): block weights and biases, ln_f, the tied head."""
     D, L, V = m["d_model"], m["n_layers"], m["vocab_size"]
-    block = 12 * D * D + 13 * D
-    weights = L * block + 2 * D + V * D + 2 * D
-    return 4.0 * weights + 4.0 * 2 * L * T * D
+    return 4.0 * (L * (12 * D * D + 13 * D) + 2 * D + V * D)
+
+
+def sequence_bytes(m: dict, T: int) -> float:
+    """Bytes one decode step moves per sequence whose attention spans T keys:
+    its token and position rows and the K/V cache of T positions."""
+    D, L = m["d_model"], m["n_layers"]
+    return 4.0 * 2 * D + 4.0 * 2 * L * T * D
 
 
 class ClockSampler:
@@ -204,9 +208,10 @@ def main():
     import __graft_entry__ as graft
 
     rank, world, local = dist_env()
-    if world > 1:
-        dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300))
     torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
     pkg = graft.load_package()
     m = wl["model"]
     cfg = pkg.ModelConfig(**m)
@@ -292,14 +297,16 @@ def main():
         return a.elapsed_time(b) / reps
 
     short_kw = dict(gen_kw, max_new_tokens=1)
+    be.reset_stats()
     t_long = timed(step_device)
+    persistent = be.stats()["persistent_steps"] > 0
     t_short = timed(lambda: be.generate_device(d_prompts.data_ptr(), d_lens.data_ptr(), [plen] * count,
                                                out_tokens_ptr=d_out.data_ptr(), out_counts_ptr=d_cnt.data_ptr(),
                                                seeds=seeds, **short_kw))
     step_ms = (t_long - t_short) / max(new - 1, 1)
     Ts = [plen + n for n in range(1, new)]
-    bytes_tok = float(np.mean([algorithmic_bytes_per_token(m, min(T, m["context_length"])) for T in Ts]))
-    achieved_gbs = count * bytes_tok / (step_ms / 1000.0) / 1e9
+    bytes_step = weight_bytes(m) + count * float(np.mean([sequence_bytes(m, min(T, m["context_length"])) for T in Ts]))
+    achieved_gbs = bytes_step / (step_ms / 1000.0) / 1e9
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -348,10 +355,12 @@ def main():
                        "sequences_per_gpu": count, "prompt_len": plen, "new_tokens": new,
                        "parallelism": f"request-parallel x{world} (independent sequences, no collective)",
                        "l2": "inputs larger than L2: every decode step streams 390 MB of weights"},
-            "roofline": {"bound": "hbm", "kernel": "decode step (CUDA graph replay)",
+            "roofline": {"bound": "hbm",
+                         "kernel": "k_decode_mega (persistent decode kernel: cp.async.bulk weight stream, on-device "
+                                   "sampler)" if persistent else "decode step (CUDA graph replay of the step kernels)",
                          "achieved": achieved_gbs, "peak": peak, "unit": "GB/s", "frac": achieved_gbs / peak,
                          "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
-                         "traffic": None, "step_ms": step_ms, "algorithmic_bytes_per_step": count * bytes_tok},
+                         "traffic": None, "step_ms": step_ms, "algorithmic_bytes_per_step": bytes_step},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": int(st.get("kernel_launches", 0)),

@@ -663,6 +663,7 @@ static void run_mega(DeviceSession& s, int n, int nsteps, const SampleParams& P,
     CK(cudaLaunchCooperativeKernel(f, dim3(nW), dim3(MK_THREADS), args, smem, s.stream));
     s.stats.kernel_launches++;
     s.stats.decode_steps += nsteps;
+    s.stats.persistent_steps += nsteps;
     s.mk_gstep += nsteps;
 }
 
@@ -1740,6 +1741,7 @@ int32_t fb2_stats(fb2_session* S, fb2_stats_t* out) {
             t.decode_ms += s->stats.decode_ms;
             t.sample_ms += s->stats.sample_ms;
             t.kernel_launches += s->stats.kernel_launches;
+            t.persistent_steps += s->stats.persistent_steps;
         }
         t.device_count = (int)S->ds.size();
         *out = t;

@@ -103,6 +103,7 @@ typedef struct {
     int64_t kernel_launches;    /* kernels the library launched (graph nodes counted) */
     int32_t device_count;
     int32_t reserved;
+    int64_t persistent_steps;   /* decode steps run inside the persistent decode kernel */
 } fb2_stats_t;
 
 /* ---- library ------------------------------------------------------------- */
