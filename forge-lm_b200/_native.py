@@ -33,7 +33,8 @@ EXPORTED = [
     "fb2_generate", "fb2_generate_device", "fb2_forward_last_logits", "fb2_teacher_forced_logits",
     "fb2_sample_logits", "fb2_forward_last_logits_noalloc", "fb2_init_params", "fb2_stats", "fb2_stats_reset",
 ]
-TEST_EXPORTED = ["fb2_test_expf", "fb2_test_expf_hash", "fb2_test_dotnet_random", "fb2_test_mk_trace"]
+TEST_EXPORTED = ["fb2_test_expf", "fb2_test_expf_hash", "fb2_test_dotnet_random", "fb2_test_mk_trace",
+                 "fb2_test_gemm_tc"]
 
 
 class ModelDesc(C.Structure):
@@ -102,6 +103,7 @@ def load(path: str | None = None):
     L.fb2_test_expf_hash.argtypes = [C.c_uint32, i32, vp]
     L.fb2_test_dotnet_random.argtypes = [i32, i32, vp]
     L.fb2_test_mk_trace.argtypes = [vp, vp, i64, C.POINTER(i32), C.POINTER(i32)]
+    L.fb2_test_gemm_tc.argtypes = [i32, i32, i32, vp, vp, vp]
     for name in EXPORTED + TEST_EXPORTED:
         fn = getattr(L, name)
         if fn.restype is C.c_int:  # default

@@ -538,7 +538,6 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     float* surv_v = reinterpret_cast<float*>(win + MR * a.ctx);  // [MK_SURV_MAX]
     int* surv_i = reinterpret_cast<int*>(surv_v + MK_SURV_MAX);  // [MK_SURV_MAX]
     float* wts_m = reinterpret_cast<float*>(surv_i + MK_SURV_MAX);  // [MR*H][maxc] chunk weights
-    float* wts_l = wts_m + (size_t)MR * H * a.maxc;                 // [MR*H][maxc] chunk sums
     // iscr regions
     uint32_t* seen = reinterpret_cast<uint32_t*>(iscr);  // [8] bits of the slice
     uint32_t* ban = seen + 8;                            // [8]
@@ -548,7 +547,6 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     int* misc = iscr + 64;                               // [64]
     int* flag = iscr + 256;                              // [256]
     int* cnts = iscr + 512;                              // [256]
-    int* offs = iscr + 768;                              // [257]
 
     __shared__ int s_slot[MK_MAX_ROWS], s_pos0[MK_MAX_ROWS], s_tok[MK_MAX_ROWS], s_cnt0[MK_MAX_ROWS];
     __shared__ int s_len0[MK_MAX_ROWS], s_dead[MK_MAX_ROWS], s_dummy[MK_MAX_ROWS], s_ubase[MK_MAX_ROWS + 1];
@@ -685,7 +683,6 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     const SampleParams sp = a.sp;
     const bool controls = sp.penalty != 1.0f || sp.ngram > 0;
     const bool sampled = sp.temperature > 0.0f;
-    const bool filter = sp.top_k > 0 && sp.top_k < V;
     uint32_t it = 0;
     if (controls)
         for (int m = 0; m < MR; m++)

@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
@@ -27,6 +28,9 @@
 #include "kernels.cuh"
 #include "sampler.cuh"
 #include "decode_mega.cuh"
+#include "gemm_tc.cuh"
+
+#include <cudaTypedefs.h>
 
 using namespace fb2;
 
@@ -120,6 +124,11 @@ struct DeviceModel {
     int mk_nW = 0;
     float* relaid = nullptr;
     MkLayer* d_mk_layers = nullptr;
+    // tensor-core GEMM: TF32 hi/lo halves of the four projections per layer
+    // (qkv, proj, fc, mlp proj) and their TMA descriptors
+    bool tc_ok = false;
+    float* tc_blob = nullptr;
+    std::vector<std::array<CUtensorMap, 8>> tc_maps;  // per layer: {hi, lo} x 4 matrices
 };
 
 struct fb2_model {
@@ -172,6 +181,7 @@ static void configure_kernels(int dev) {
     setmax((const void*)k_head<8>, 227 * 1024);
     setmax((const void*)k_head<16>, 227 * 1024);
     setmax((const void*)k_sample_step, 227 * 1024);
+    setmax((const void*)k_gemm_tc, 227 * 1024);
     setmax((const void*)k_sample_rows, 227 * 1024);
     setmax((const void*)k_decode_mega<1>, 0);
     setmax((const void*)k_decode_mega<2>, 0);
@@ -208,6 +218,73 @@ static int mk_nstage(const fb2_model& m, int MR, int nW, int device) {
     int ns = 16;
     while (ns >= 4 && (long long)mk_smem(m, MR, nW, ns) > avail) ns--;
     return ns >= 4 ? ns : 0;
+}
+
+// ---- tensor-core GEMM support ----------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 tc_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+// 2-D fp32 row-major [outer][inner] map, 128-byte swizzled boxes of
+// 32 x box_outer elements.
+static bool tc_encode(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer, uint32_t box_outer) {
+    auto fn = tc_encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {inner * 4};
+    const cuuint32_t box[2] = {32, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+static void launch_split_tf32(cudaStream_t st, const float* x, size_t n, float* hi, float* lo) {
+    const size_t n4 = n / 4;
+    const int blocks = (int)std::min<size_t>(4096, (n4 + 255) / 256);
+    k_split_tf32<<<std::max(blocks, 1), 256, 0, st>>>(reinterpret_cast<const float4*>(x), n4,
+                                                      reinterpret_cast<float4*>(hi), reinterpret_cast<float4*>(lo));
+}
+static void launch_split_tf32_transpose(cudaStream_t st, const float* W, int K, int N, float* hiT, float* loT) {
+    k_split_tf32_transpose<<<dim3(ceil_div(N, 32), ceil_div(K, 32)), dim3(32, 8), 0, st>>>(W, K, N, hiT, loT);
+}
+// TF32 hi/lo copies of every projection, transposed to W^T [N][K], and their
+// descriptors (boxes of 32 K x 128 N rows).  FORGE_B200_GEMM=simt leaves the
+// tensor-core path off.
+static void tc_setup(const fb2_model& m, DeviceModel& dm) {
+    dm.tc_ok = false;
+    const char* env = getenv("FORGE_B200_GEMM");
+    if (env && std::string(env) == "simt") return;
+    if (!tc_encode_fn() || (m.D % 32) != 0) return;
+    const size_t D = m.D, F = m.F;
+    const size_t per_layer = 3 * D * D + D * D + D * F + F * D;
+    dm.tc_blob = dalloc<float>(2 * per_layer * m.L);
+    dm.tc_maps.resize(m.L);
+    for (int l = 0; l < m.L; l++) {
+        const LayerW& w = dm.layers[l];
+        const float* src[4] = {w.qkv_w, w.proj_w, w.fc_w, w.mproj_w};
+        const size_t Ks[4] = {D, D, D, F}, Ns[4] = {3 * D, D, F, D};
+        float* at = dm.tc_blob + 2 * per_layer * l;
+        for (int j = 0; j < 4; j++) {
+            const size_t n = Ks[j] * Ns[j];
+            float* hi = at;
+            float* lo = at + n;
+            launch_split_tf32_transpose(0, src[j], (int)Ks[j], (int)Ns[j], hi, lo);
+            if (!tc_encode(&dm.tc_maps[l][2 * j], hi, Ks[j], Ns[j], TC_BN) ||
+                !tc_encode(&dm.tc_maps[l][2 * j + 1], lo, Ks[j], Ns[j], TC_BN))
+                return;
+            at += 2 * n;
+        }
+    }
+    CK(cudaDeviceSynchronize());
+    dm.tc_ok = true;
 }
 
 // Re-lays every projection W[K][N] as consecutive column strips [K][w_c],
@@ -286,6 +363,8 @@ struct DeviceSession {
     int *d_row_seq = nullptr, *d_row_pos = nullptr, *d_row_hidx = nullptr, *d_row_active = nullptr;
     int* d_ones = nullptr;
     float *d_x = nullptr, *d_x2 = nullptr, *d_ln = nullptr, *d_q = nullptr, *d_att = nullptr, *d_h = nullptr;
+    float *d_ahi = nullptr, *d_alo = nullptr;  // TF32 halves of a GEMM's A operand
+    int* d_tc_err = nullptr;
     float *d_logits = nullptr, *d_lnf = nullptr;
     float* d_attn_part = nullptr;
     int attn_nsplit = 0;
@@ -393,6 +472,7 @@ static void session_free(DeviceSession* s) {
     dfree(s->d_len); dfree(s->d_count); dfree(s->d_done); dfree(s->d_hist); dfree(s->d_kv);
     dfree(s->d_row_seq); dfree(s->d_row_pos); dfree(s->d_row_hidx); dfree(s->d_row_active); dfree(s->d_ones);
     dfree(s->d_x); dfree(s->d_x2); dfree(s->d_ln); dfree(s->d_q); dfree(s->d_att); dfree(s->d_h);
+    dfree(s->d_ahi); dfree(s->d_alo); dfree(s->d_tc_err);
     dfree(s->d_logits); dfree(s->d_lnf); dfree(s->d_attn_part); dfree(s->d_gemv_part); dfree(s->d_tickets);
     dfree(s->d_tab); dfree(s->d_uni); dfree(s->d_out);
     dfree(s->mk_xq); dfree(s->mk_xacc); dfree(s->mk_cval); dfree(s->mk_cidx); dfree(s->mk_stepdone);
@@ -436,6 +516,30 @@ static void launch_gemv_mr(DeviceSession& s, int M, int K, int N, const float* A
 }
 
 // y = A * W (+ epilogue) for M rows.
+static void launch_linear(DeviceSession& s, int M, int K, int N, const float* A, const float* W, Epi e);
+
+// Rows from which a projection runs on the tensor cores (3xTF32 GEMM).
+constexpr int kTcMinRows = 128;
+
+// y = A * W (+ epilogue) for M rows.  `bmaps` (TF32 hi/lo descriptors of W)
+// selects the tensor-core GEMM for M >= kTcMinRows.
+static void launch_linear(DeviceSession& s, int M, int K, int N, const float* A, const float* W, Epi e,
+                          const CUtensorMap* bmaps) {
+    if (bmaps && s.d_ahi && M >= kTcMinRows && (K % 4) == 0 && (N % 4) == 0) {
+        launch_split_tf32(s.stream, A, (size_t)M * K, s.d_ahi, s.d_alo);
+        s.stats.kernel_launches++;
+        TcMaps maps;
+        if (!tc_encode(&maps.a_hi, s.d_ahi, K, M, TC_BM) || !tc_encode(&maps.a_lo, s.d_alo, K, M, TC_BM))
+            fail(FB2_CUDA_ERROR, "cuTensorMapEncodeTiled failed for a GEMM operand");
+        maps.b_hi = bmaps[0];
+        maps.b_lo = bmaps[1];
+        dim3 grid(ceil_div(N, TC_BN), ceil_div(M, TC_BM));
+        s.stats.kernel_launches++; k_gemm_tc<<<grid, 128, TC_SMEM, s.stream>>>(maps, M, N, K, e, s.d_tc_err);
+        return;
+    }
+    launch_linear(s, M, K, N, A, W, e);
+}
+
 static void launch_linear(DeviceSession& s, int M, int K, int N, const float* A, const float* W, Epi e) {
     if (M <= kMaxGemvRows) {
         if (M <= 1) launch_gemv_mr<1>(s, M, K, N, A, W, e);
@@ -563,13 +667,14 @@ static void run_layers(DeviceSession& s, int M, Rows R, bool decode, int nqblk, 
         eq.hd = m.hd;
         eq.ctx = m.ctx;
         eq.R = R;
-        launch_linear(s, M, m.D, 3 * m.D, s.d_ln, w.qkv_w, eq);
+        const CUtensorMap* tcm = s.dm->tc_ok ? s.dm->tc_maps[l].data() : nullptr;
+        launch_linear(s, M, m.D, 3 * m.D, s.d_ln, w.qkv_w, eq, tcm);
         if (decode) launch_attn_decode(s, M, l, R);
         else launch_attn_prefill(s, nqblk, qblk, l);
-        launch_linear(s, M, m.D, m.D, s.d_att, w.proj_w, make_epi(EPI_RESID, w.proj_b, s.d_x, s.d_x2));
+        launch_linear(s, M, m.D, m.D, s.d_att, w.proj_w, make_epi(EPI_RESID, w.proj_b, s.d_x, s.d_x2), tcm ? tcm + 2 : nullptr);
         launch_layernorm(s, M, s.d_x2, w.ln2_w, w.ln2_b, s.d_ln, nullptr);
-        launch_linear(s, M, m.D, m.F, s.d_ln, w.fc_w, make_epi(EPI_GELU, w.fc_b, nullptr, s.d_h));
-        launch_linear(s, M, m.F, m.D, s.d_h, w.mproj_w, make_epi(EPI_RESID, w.mproj_b, s.d_x2, s.d_x));
+        launch_linear(s, M, m.D, m.F, s.d_ln, w.fc_w, make_epi(EPI_GELU, w.fc_b, nullptr, s.d_h), tcm ? tcm + 4 : nullptr);
+        launch_linear(s, M, m.F, m.D, s.d_h, w.mproj_w, make_epi(EPI_RESID, w.mproj_b, s.d_x2, s.d_x), tcm ? tcm + 6 : nullptr);
     }
 }
 
@@ -670,6 +775,14 @@ static void run_mega(DeviceSession& s, int n, int nsteps, const SampleParams& P,
 // Host check of the persistent kernel's error flag (after a synchronize);
 // resets its state and fails with FB2_TIMEOUT when a bounded wait expired.
 static void mk_check(DeviceSession& s) {
+    if (s.d_tc_err) {  // tensor-core GEMM: a bounded wait expired
+        int terr = 0;
+        CK(cudaMemcpy(&terr, s.d_tc_err, sizeof(int), cudaMemcpyDeviceToHost));
+        if (terr != 0) {
+            CK(cudaMemset(s.d_tc_err, 0, sizeof(int)));
+            fail(FB2_TIMEOUT, "tensor-core GEMM: a bounded wait expired (code " + std::to_string(terr) + ")");
+        }
+    }
     if (!s.mk_use) return;
     int err = 0;
     CK(cudaMemcpy(&err, s.mk_err, sizeof(int), cudaMemcpyDeviceToHost));
@@ -1281,6 +1394,7 @@ int32_t fb2_model_create(const fb2_model_desc* desc, const float* const* params,
                 D.lnf_w = D.p[2 + 12 * d.n_layers];
                 D.lnf_b = D.p[3 + 12 * d.n_layers];
                 mk_setup(*m, D, params);
+                tc_setup(*m, D);
             }
         } catch (...) {
             for (auto& dm : m->devs) {
@@ -1288,6 +1402,7 @@ int32_t fb2_model_create(const fb2_model_desc* desc, const float* const* params,
                 dfree(dm.blob);
                 dfree(dm.relaid);
                 dfree(dm.d_mk_layers);
+                dfree(dm.tc_blob);
             }
             delete m;
             throw;
@@ -1303,6 +1418,7 @@ void fb2_model_destroy(fb2_model* m) {
         dfree(dm.blob);
         dfree(dm.relaid);
         dfree(dm.d_mk_layers);
+        dfree(dm.tc_blob);
     }
     delete m;
 }
@@ -1368,6 +1484,12 @@ int32_t fb2_session_create(fb2_model* m, int32_t max_seqs, fb2_session** out) {
                 s->d_q = dalloc<float>(rc * D);
                 s->d_att = dalloc<float>(rc * D);
                 s->d_h = dalloc<float>(rc * F);
+                if (s->dm->tc_ok) {
+                    s->d_ahi = dalloc<float>(rc * F);
+                    s->d_alo = dalloc<float>(rc * F);
+                    s->d_tc_err = dalloc<int>(1);
+                    CK(cudaMemset(s->d_tc_err, 0, sizeof(int)));
+                }
                 s->d_logits = dalloc<float>((size_t)(cnt + kMaxChunkSlots) * m->V);
                 s->d_lnf = dalloc<float>((size_t)std::max(cnt, kMaxChunkSlots) * D);
                 s->attn_nsplit = ceil_div(m->ctx, kAttnChunk);
@@ -1843,6 +1965,49 @@ int32_t fb2_forward_last_logits_noalloc(fb2_model* m, int32_t device_slot, int32
 // Copies the persistent kernel's per-phase %globaltimer stamps of its last
 // traced launch (FORGE_B200_MK_TRACE=<steps> at session creation) into out:
 // [CTAs][steps][64] uint64; *n_ctas / *n_steps receive the shape.
+int32_t fb2_test_gemm_tc(int32_t M, int32_t N, int32_t K, const float* A, const float* W, float* out) {
+    return guarded([&] {
+        if (!A || !W || !out) fail(FB2_INVALID_ARG, "NULL argument");
+        if (M <= 0 || N <= 0 || K <= 0 || (N % 4) || (K % 4)) fail(FB2_INVALID_ARG, "bad GEMM shape");
+        if (!tc_encode_fn()) fail(FB2_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+        int dev = 0;
+        CK(cudaGetDevice(&dev));
+        configure_kernels(dev);
+        const size_t na = (size_t)M * K, nw = (size_t)K * N, no = (size_t)M * N;
+        float* buf = dalloc<float>(3 * na + 3 * nw + no + (size_t)N);
+        float *a = buf, *ahi = a + na, *alo = ahi + na, *w = alo + na, *whi = w + nw, *wlo = whi + nw, *o = wlo + nw;
+        float* bias = o + no;
+        int* err = dalloc<int>(1);
+        try {
+            CK(cudaMemcpy(a, A, na * 4, cudaMemcpyHostToDevice));
+            CK(cudaMemcpy(w, W, nw * 4, cudaMemcpyHostToDevice));
+            CK(cudaMemset(bias, 0, (size_t)N * 4));
+            CK(cudaMemset(err, 0, sizeof(int)));
+            launch_split_tf32(0, a, na, ahi, alo);
+            launch_split_tf32_transpose(0, w, K, N, whi, wlo);
+            TcMaps maps;
+            if (!tc_encode(&maps.a_hi, ahi, K, M, TC_BM) || !tc_encode(&maps.a_lo, alo, K, M, TC_BM) ||
+                !tc_encode(&maps.b_hi, whi, K, N, TC_BN) || !tc_encode(&maps.b_lo, wlo, K, N, TC_BN))
+                fail(FB2_CUDA_ERROR, "cuTensorMapEncodeTiled failed");
+            Epi e = make_epi(EPI_BIAS, bias, nullptr, o);
+            dim3 grid(ceil_div(N, TC_BN), ceil_div(M, TC_BM));
+            k_gemm_tc<<<grid, 128, TC_SMEM>>>(maps, M, N, K, e, err);
+            CK(cudaGetLastError());
+            CK(cudaDeviceSynchronize());
+            int herr = 0;
+            CK(cudaMemcpy(&herr, err, sizeof(int), cudaMemcpyDeviceToHost));
+            if (herr) fail(FB2_TIMEOUT, "tensor-core GEMM: a bounded wait expired");
+            CK(cudaMemcpy(out, o, no * 4, cudaMemcpyDeviceToHost));
+        } catch (...) {
+            dfree(buf);
+            dfree(err);
+            throw;
+        }
+        dfree(buf);
+        dfree(err);
+    });
+}
+
 int32_t fb2_test_mk_trace(fb2_session* S, uint64_t* out, int64_t capacity, int32_t* n_ctas, int32_t* n_steps) {
     return guarded([&] {
         if (!S || !n_ctas || !n_steps) fail(FB2_INVALID_ARG, "NULL argument");

@@ -1,0 +1,305 @@
+// Tensor-core GEMM for the prefill / batched projections (sm_100a).
+//
+// y[M,N] = A[M,K] * W[K,N] (+ the Epi epilogue of kernels.cuh), fp32 in and
+// out, computed on the 5th-generation tensor cores in TF32 with the 3xTF32
+// error compensation: every fp32 operand x is carried as hi = x rounded to
+// the nearest TF32 value and lo = x - hi, itself rounded to TF32 (both exact
+// for the tensor cores, which read the top 19 bits), and
+//   A*W ~= A_hi*W_hi + A_hi*W_lo + A_lo*W_hi
+// accumulates in fp32 in tensor memory (each operand is carried to ~2^-22
+// relative, unbiased; the dropped lo*lo term is ~2^-22), which keeps the
+// result within the fp32 parity tolerance of the reference's
+// CpuBackend.MatMulNN (CpuBackend.cs:118-164).
+//
+// The weight halves are stored transposed, W^T [N][K], so both operands are
+// K-major tiles (rows of 32 fp32 = 128 bytes, 128-byte swizzled).
+//
+// One CTA computes a 128 x 128 output tile:
+//   warp 0 / lane 0  TMA producer: per 32-deep k block, A_hi and A_lo tiles
+//                    (128 rows of A) and W_hi, W_lo tiles (128 rows of W^T)
+//                    into a 3-stage ring guarded by full/empty mbarriers;
+//   warp 1 / lane 0  MMA issuer: 4 k-steps x 3 tcgen05.mma (M128 N128 K8)
+//                    per stage into one TMEM accumulator, tcgen05.commit
+//                    frees the stage; a final commit signals the epilogue;
+//   warps 0-3        epilogue: tcgen05.ld of the thread's accumulator row
+//                    (TMEM lane = row), 16 columns at a time, into epi_store4.
+// Every mbarrier wait is bounded (kTcTimeoutNs); on expiry the CTA records
+// an error, stops issuing, waits (bounded) for work in flight, frees its TMEM
+// and returns.
+#pragma once
+#include <cuda.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace fb2 {
+
+constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32, TC_STAGES = 3;
+constexpr int TC_TILE_A = TC_BM * TC_BK * 4;                      // 16 KB
+constexpr int TC_TILE_B = TC_BN * TC_BK * 4;                      // 16 KB
+constexpr int TC_STAGE_BYTES = 2 * TC_TILE_A + 2 * TC_TILE_B;     // 64 KB
+constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024;        // + alignment slack
+constexpr unsigned long long kTcTimeoutNs = 2000000000ull;
+constexpr int TC_ERR_TIMEOUT = 1;
+
+struct TcMaps {
+    CUtensorMap a_hi, a_lo, b_hi, b_lo;
+};
+
+namespace tc {
+
+FB2_DEV uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+FB2_DEV unsigned long long now_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+FB2_DEV void bar_init(uint64_t* b, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(b)), "r"(count) : "memory");
+}
+FB2_DEV void bar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)), "r"(bytes) : "memory");
+}
+FB2_DEV bool bar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_addr(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for phase `parity` of barrier b; false on expiry or abort.
+FB2_DEV bool bar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
+    if (bar_try(b, parity)) return true;
+    const unsigned long long t0 = now_ns();
+    while (!bar_try(b, parity)) {
+        if (*abort_flag) return false;
+        if (now_ns() - t0 > kTcTimeoutNs) {
+            *abort_flag = 1;
+            return false;
+        }
+    }
+    return true;
+}
+FB2_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+// Shared-memory matrix descriptor (sm_100 format, version 1) for a
+// 128-byte-swizzled tile whose 1024-byte swizzle atoms start 1024-aligned.
+FB2_DEV uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+    d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+    return d;
+}
+// Instruction descriptor: A, B TF32, both K-major, D F32, M x N.
+constexpr uint32_t idesc_tf32(int M, int N) {
+    return (1u << 4)                    // D format F32
+           | (2u << 7) | (2u << 10)     // A, B format TF32
+           | (0u << 15) | (0u << 16)    // A, B K-major
+           | ((uint32_t)(N >> 3) << 17)  // N / 8
+           | ((uint32_t)(M >> 4) << 24);  // M / 16
+}
+FB2_DEV void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p; }" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+FB2_DEV void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+FB2_DEV void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+FB2_DEV void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// 32 lanes x 16 consecutive 32-bit columns of TMEM into registers.
+FB2_DEV void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+}  // namespace tc
+
+// Round to the nearest TF32 value (ties to even), kept in an fp32 container.
+FB2_DEV float tf32_round(float x) {
+    const uint32_t b = __float_as_uint(x);
+    if ((b & 0x7F800000u) == 0x7F800000u) return x;  // inf / nan unchanged
+    return __uint_as_float((b + 0x0FFFu + ((b >> 13) & 1u)) & 0xFFFFE000u);
+}
+FB2_DEV void tf32_split(float x, float& hi, float& lo) {
+    hi = tf32_round(x);
+    lo = tf32_round(x - hi);
+}
+
+// W [K][N] -> W^T halves hiT, loT [N][K] (32 x 32 tiles through shared memory).
+__global__ void k_split_tf32_transpose(const float* __restrict__ W, int K, int N, float* __restrict__ hiT,
+                                       float* __restrict__ loT) {
+    __shared__ float t[32][33];
+    const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int k = k0 + r, n = n0 + threadIdx.x;
+        t[r][threadIdx.x] = (k < K && n < N) ? W[(size_t)k * N + n] : 0.f;
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int n = n0 + r, k = k0 + threadIdx.x;
+        if (n < N && k < K) {
+            float h, l;
+            tf32_split(t[threadIdx.x][r], h, l);
+            hiT[(size_t)n * K + k] = h;
+            loT[(size_t)n * K + k] = l;
+        }
+    }
+}
+
+// x -> (hi, lo) TF32 halves.
+__global__ void k_split_tf32(const float4* __restrict__ x, size_t n4, float4* __restrict__ hi, float4* __restrict__ lo) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const float4 v = x[i];
+        float4 h, l;
+        tf32_split(v.x, h.x, l.x);
+        tf32_split(v.y, h.y, l.y);
+        tf32_split(v.z, h.z, l.z);
+        tf32_split(v.w, h.w, l.w);
+        hi[i] = h;
+        lo[i] = l;
+    }
+}
+
+__global__ void __launch_bounds__(128, 1) k_gemm_tc(const __grid_constant__ TcMaps maps, int M, int N, int K, Epi e,
+                                                    int* err) {
+    extern __shared__ unsigned char tc_smem_raw[];
+    __shared__ __align__(8) uint64_t full[TC_STAGES], empty[TC_STAGES], accb;
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int s_abort;
+    unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int m0 = blockIdx.y * TC_BM, n0 = blockIdx.x * TC_BN;
+    const int nk = (K + TC_BK - 1) / TC_BK;
+
+    if (tid == 0) {
+        s_abort = 0;
+        for (int i = 0; i < TC_STAGES; i++) {
+            tc::bar_init(&full[i], 1);
+            tc::bar_init(&empty[i], 1);
+        }
+        tc::bar_init(&accb, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc::smem_addr(&tmem_base)),
+                     "r"((uint32_t)TC_BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = tmem_base;
+
+    if (warp == 0 && lane == 0) {
+        // ---- producer ----
+        for (int kb = 0; kb < nk; kb++) {
+            const int st = kb % TC_STAGES;
+            if (kb >= TC_STAGES && !tc::bar_wait(&empty[st], ((kb / TC_STAGES) - 1) & 1, &s_abort)) break;
+            unsigned char* sb = sm + (size_t)st * TC_STAGE_BYTES;
+            tc::bar_expect_tx(&full[st], TC_STAGE_BYTES);
+            const int k0 = kb * TC_BK;
+            tc::tma_load_2d(sb, &maps.a_hi, k0, m0, &full[st]);
+            tc::tma_load_2d(sb + TC_TILE_A, &maps.a_lo, k0, m0, &full[st]);
+            tc::tma_load_2d(sb + 2 * TC_TILE_A, &maps.b_hi, k0, n0, &full[st]);
+            tc::tma_load_2d(sb + 2 * TC_TILE_A + TC_TILE_B, &maps.b_lo, k0, n0, &full[st]);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer ----
+        constexpr uint32_t idesc = tc::idesc_tf32(TC_BM, TC_BN);
+        int kb = 0;
+        for (; kb < nk; kb++) {
+            const int st = kb % TC_STAGES;
+            if (!tc::bar_wait(&full[st], (kb / TC_STAGES) & 1, &s_abort)) break;
+            tc::fence_after();
+            const uint32_t sa = tc::smem_addr(sm + (size_t)st * TC_STAGE_BYTES);
+            const uint32_t a_hi = sa, a_lo = sa + TC_TILE_A, b_hi = sa + 2 * TC_TILE_A, b_lo = b_hi + TC_TILE_B;
+#pragma unroll
+            for (int ks = 0; ks < TC_BK / 8; ks++) {
+                // K-major rows of 128 B, 8-row swizzle atoms 1024 B apart;
+                // a k-step (8 TF32) is 32 B along the rows
+                const uint64_t dah = tc::sw128_desc(a_hi + ks * 32, 16, 1024);
+                const uint64_t dal = tc::sw128_desc(a_lo + ks * 32, 16, 1024);
+                const uint64_t dbh = tc::sw128_desc(b_hi + ks * 32, 16, 1024);
+                const uint64_t dbl = tc::sw128_desc(b_lo + ks * 32, 16, 1024);
+                tc::mma_tf32(tmem, dah, dbh, idesc, (kb | ks) != 0);
+                tc::mma_tf32(tmem, dah, dbl, idesc, 1u);
+                tc::mma_tf32(tmem, dal, dbh, idesc, 1u);
+            }
+            tc::mma_commit(&empty[st]);
+        }
+        tc::mma_commit(&accb);  // fires once every MMA issued above has completed
+    }
+    __syncwarp();
+
+    // ---- epilogue: thread (warp w, lane i) owns accumulator row 32w + i ----
+    // The issuer always commits `accb`, after an abort too, so this wait
+    // (bounded, not cut short by the abort flag) also drains the MMAs in
+    // flight before the accumulator is freed.
+    bool ok = tc::bar_try(&accb, 0);
+    if (!ok) {
+        const unsigned long long t0 = tc::now_ns();
+        while (!(ok = tc::bar_try(&accb, 0)) && tc::now_ns() - t0 < kTcTimeoutNs) {
+        }
+        if (!ok) s_abort = 1;
+    }
+    __syncwarp();
+    tc::fence_after();
+    if (ok && !s_abort) {
+        const int row = m0 + warp * 32 + lane;
+#pragma unroll 1
+        for (int c0 = 0; c0 < TC_BN; c0 += 16) {
+            float v[16];
+            tc::tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+            if (row < M) {
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int n = n0 + c0 + 4 * q;
+                    if (n < N) epi_store4(e, row, n, N, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+                }
+            }
+        }
+    }
+    if (s_abort && tid == 0) {
+        atomicExch(err, TC_ERR_TIMEOUT);
+        // copies the issuer never consumed may still be landing: wait for
+        // every stage's latest fill (bounded) before the CTA's memory goes
+        for (int st = 0; st < TC_STAGES && st < nk; st++) {
+            const int last = st + ((nk - 1 - st) / TC_STAGES) * TC_STAGES;  // last k block using stage st
+            const unsigned long long t0 = tc::now_ns();
+            while (!tc::bar_try(&full[st], (last / TC_STAGES) & 1) && tc::now_ns() - t0 < kTcTimeoutNs / 4) {
+            }
+        }
+    }
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)TC_BN) : "memory");
+    }
+}
+
+}  // namespace fb2

@@ -34,6 +34,11 @@ struct fb2_session;
 int32_t fb2_test_mk_trace(struct fb2_session* s, uint64_t* out, int64_t capacity, int32_t* n_ctas,
                           int32_t* n_steps);
 
+/* out[M][N] = A[M][K] * W[K][N] through the tensor-core 3xTF32 GEMM on the
+ * current device (host arrays; M, N, K > 0, N and K multiples of 4).
+ * FB2_UNSUPPORTED when the tensor-core path is unavailable. */
+int32_t fb2_test_gemm_tc(int32_t M, int32_t N, int32_t K, const float* A, const float* W, float* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -86,6 +86,25 @@ def test_teacher_forced_decode_matches_full_forward(pkg, O):
 
 
 # ---------------------------------------------------------------------------
+@pytest.mark.parametrize("M,N,K", [(128, 128, 32), (300, 200, 100), (1024, 768, 768), (256, 3072, 768),
+                                   (200, 768, 3072)])
+def test_tensor_core_gemm_3xtf32(pkg, M, N, K):
+    """The tcgen05 3xTF32 GEMM of the prefill projections against an fp64
+    product, ragged M, N, K.  The bound (relative to the largest output) is
+    3xTF32 accuracy with the tensor cores' fp32 accumulation, which grows with
+    the depth K: 2e-5 up to K = 768, 5e-5 at K = 3072.  A single TF32 product
+    would be ~1e-3, the logits tolerance of the parity tests."""
+    from forge_lm_b200 import _native as nat
+    rng = np.random.default_rng(M * 7 + N * 3 + K)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    W = (rng.standard_normal((K, N)) * 0.05).astype(np.float32)
+    out = np.full((M, N), np.nan, np.float32)
+    nat.check(nat.load().fb2_test_gemm_tc(M, N, K, A.ctypes.data, W.ctypes.data, out.ctypes.data))
+    want = A.astype(np.float64) @ W.astype(np.float64)
+    err = float(np.max(np.abs(out - want)) / np.max(np.abs(want)))
+    assert err < (2e-5 if K <= 768 else 5e-5), err
+
+
 def _rows_cases(V, rng):
     cases = []
     for t in range(40):
