@@ -101,6 +101,7 @@ void dfree(T*& p) {
 inline int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 
 constexpr int kMaxGemvRows = 16;
+constexpr int kTcSplitMax = 32;  // k splits of the decode tensor-core GEMM
 constexpr int kMaxChunkSlots = 64;  // sequences per prefill chunk (head scratch rows)
 constexpr int kGemvMaxKChunk = 256;
 }  // namespace
@@ -128,7 +129,7 @@ struct DeviceModel {
     // (qkv, proj, fc, mlp proj) and their TMA descriptors
     bool tc_ok = false;
     float* tc_blob = nullptr;
-    std::vector<std::array<CUtensorMap, 8>> tc_maps;  // per layer: {hi, lo} x 4 matrices
+    std::vector<std::array<CUtensorMap, 8>> tc_maps;  // per layer: {hi, lo} x 4 matrices (W^T, 128-row boxes)
 };
 
 struct fb2_model {
@@ -181,7 +182,9 @@ static void configure_kernels(int dev) {
     setmax((const void*)k_head<8>, 227 * 1024);
     setmax((const void*)k_head<16>, 227 * 1024);
     setmax((const void*)k_sample_step, 227 * 1024);
-    setmax((const void*)k_gemm_tc, 227 * 1024);
+    setmax((const void*)k_gemm_tc<128>, 227 * 1024);
+    setmax((const void*)k_gemm_tc_swab<64>, 227 * 1024);
+    setmax((const void*)k_gemm_tc_swab<128>, 227 * 1024);
     setmax((const void*)k_sample_rows, 227 * 1024);
     setmax((const void*)k_decode_mega<1>, 0);
     setmax((const void*)k_decode_mega<2>, 0);
@@ -277,8 +280,8 @@ static void tc_setup(const fb2_model& m, DeviceModel& dm) {
             float* hi = at;
             float* lo = at + n;
             launch_split_tf32_transpose(0, src[j], (int)Ks[j], (int)Ns[j], hi, lo);
-            if (!tc_encode(&dm.tc_maps[l][2 * j], hi, Ks[j], Ns[j], TC_BN) ||
-                !tc_encode(&dm.tc_maps[l][2 * j + 1], lo, Ks[j], Ns[j], TC_BN))
+            if (!tc_encode(&dm.tc_maps[l][2 * j], hi, Ks[j], Ns[j], 128) ||
+                !tc_encode(&dm.tc_maps[l][2 * j + 1], lo, Ks[j], Ns[j], 128))
                 return;
             at += 2 * n;
         }
@@ -365,6 +368,8 @@ struct DeviceSession {
     float *d_x = nullptr, *d_x2 = nullptr, *d_ln = nullptr, *d_q = nullptr, *d_att = nullptr, *d_h = nullptr;
     float *d_ahi = nullptr, *d_alo = nullptr;  // TF32 halves of a GEMM's A operand
     int* d_tc_err = nullptr;
+    float* d_tc_part = nullptr;  // split-K partial tiles of the decode GEMM
+    size_t tc_part_cap = 0;
     float *d_logits = nullptr, *d_lnf = nullptr;
     float* d_attn_part = nullptr;
     int attn_nsplit = 0;
@@ -472,7 +477,7 @@ static void session_free(DeviceSession* s) {
     dfree(s->d_len); dfree(s->d_count); dfree(s->d_done); dfree(s->d_hist); dfree(s->d_kv);
     dfree(s->d_row_seq); dfree(s->d_row_pos); dfree(s->d_row_hidx); dfree(s->d_row_active); dfree(s->d_ones);
     dfree(s->d_x); dfree(s->d_x2); dfree(s->d_ln); dfree(s->d_q); dfree(s->d_att); dfree(s->d_h);
-    dfree(s->d_ahi); dfree(s->d_alo); dfree(s->d_tc_err);
+    dfree(s->d_ahi); dfree(s->d_alo); dfree(s->d_tc_err); dfree(s->d_tc_part);
     dfree(s->d_logits); dfree(s->d_lnf); dfree(s->d_attn_part); dfree(s->d_gemv_part); dfree(s->d_tickets);
     dfree(s->d_tab); dfree(s->d_uni); dfree(s->d_out);
     dfree(s->mk_xq); dfree(s->mk_xacc); dfree(s->mk_cval); dfree(s->mk_cidx); dfree(s->mk_stepdone);
@@ -518,25 +523,54 @@ static void launch_gemv_mr(DeviceSession& s, int M, int K, int N, const float* A
 // y = A * W (+ epilogue) for M rows.
 static void launch_linear(DeviceSession& s, int M, int K, int N, const float* A, const float* W, Epi e);
 
-// Rows from which a projection runs on the tensor cores (3xTF32 GEMM).
-constexpr int kTcMinRows = 128;
+// Tensor-core (3xTF32) GEMM: from kTcMinRows rows, 128 x 128 output tiles;
+// decode batches of kMaxGemvRows+1 .. kTcMinRows-1 rows use the swapped
+// operands (weights as the 128-row side, read once) with split-K.
+constexpr int kTcMinRows = 512;
+
+// The launch of one tensor-core projection; false when it does not apply.
+static bool launch_gemm_tc(cudaStream_t st, int sm_count, int M, int K, int N, const float* A, float* ahi, float* alo,
+                           const CUtensorMap* bmaps, Epi e, int* err, float* part, size_t part_cap, int64_t* launches) {
+    if (M <= kMaxGemvRows || (K % 4) || (N % 4)) return false;
+    launch_split_tf32(st, A, (size_t)M * K, ahi, alo);
+    (*launches)++;
+    TcMaps maps;
+    maps.b_hi = bmaps[0];
+    maps.b_lo = bmaps[1];
+    if (M >= kTcMinRows) {
+        if (!tc_encode(&maps.a_hi, ahi, K, M, TC_BM) || !tc_encode(&maps.a_lo, alo, K, M, TC_BM))
+            fail(FB2_CUDA_ERROR, "cuTensorMapEncodeTiled failed for a GEMM operand");
+        (*launches)++;
+        k_gemm_tc<128><<<dim3(ceil_div(N, 128), ceil_div(M, TC_BM)), 128, TcCfg<128>::SMEM, st>>>(maps, M, N, K, e, err);
+        return true;
+    }
+    const int bnb = M <= 64 ? 64 : 128;
+    if (!tc_encode(&maps.a_hi, ahi, K, M, bnb) || !tc_encode(&maps.a_lo, alo, K, M, bnb))
+        fail(FB2_CUDA_ERROR, "cuTensorMapEncodeTiled failed for a GEMM operand");
+    const int tiles = ceil_div(N, 128) * ceil_div(M, bnb), nk = ceil_div(K, TC_BK);
+    int S = std::max(1, std::min({kTcSplitMax, nk, sm_count / tiles}));
+    S = ceil_div(nk, ceil_div(nk, S));  // balanced k blocks per split
+    if ((size_t)S * M * N > part_cap) S = 1;
+    dim3 grid(ceil_div(N, 128), ceil_div(M, bnb), S);
+    (*launches)++;
+    if (bnb == 64) k_gemm_tc_swab<64><<<grid, 128, TcSwabCfg<64>::SMEM, st>>>(maps, M, N, K, e, err, part);
+    else k_gemm_tc_swab<128><<<grid, 128, TcSwabCfg<128>::SMEM, st>>>(maps, M, N, K, e, err, part);
+    if (S > 1) {
+        const size_t n4 = (size_t)M * N / 4;
+        (*launches)++;
+        k_splitk_reduce<<<(int)std::min<size_t>((n4 + 255) / 256, 4 * (size_t)sm_count), 256, 0, st>>>(part, S, M, N, e);
+    }
+    return true;
+}
 
 // y = A * W (+ epilogue) for M rows.  `bmaps` (TF32 hi/lo descriptors of W)
-// selects the tensor-core GEMM for M >= kTcMinRows.
+// selects the tensor-core GEMM when it applies.
 static void launch_linear(DeviceSession& s, int M, int K, int N, const float* A, const float* W, Epi e,
                           const CUtensorMap* bmaps) {
-    if (bmaps && s.d_ahi && M >= kTcMinRows && (K % 4) == 0 && (N % 4) == 0) {
-        launch_split_tf32(s.stream, A, (size_t)M * K, s.d_ahi, s.d_alo);
-        s.stats.kernel_launches++;
-        TcMaps maps;
-        if (!tc_encode(&maps.a_hi, s.d_ahi, K, M, TC_BM) || !tc_encode(&maps.a_lo, s.d_alo, K, M, TC_BM))
-            fail(FB2_CUDA_ERROR, "cuTensorMapEncodeTiled failed for a GEMM operand");
-        maps.b_hi = bmaps[0];
-        maps.b_lo = bmaps[1];
-        dim3 grid(ceil_div(N, TC_BN), ceil_div(M, TC_BM));
-        s.stats.kernel_launches++; k_gemm_tc<<<grid, 128, TC_SMEM, s.stream>>>(maps, M, N, K, e, s.d_tc_err);
+    if (bmaps && s.d_ahi &&
+        launch_gemm_tc(s.stream, s.dm->sm_count, M, K, N, A, s.d_ahi, s.d_alo, bmaps, e, s.d_tc_err, s.d_tc_part,
+                       s.tc_part_cap, &s.stats.kernel_launches))
         return;
-    }
     launch_linear(s, M, K, N, A, W, e);
 }
 
@@ -1489,6 +1523,8 @@ int32_t fb2_session_create(fb2_model* m, int32_t max_seqs, fb2_session** out) {
                     s->d_alo = dalloc<float>(rc * F);
                     s->d_tc_err = dalloc<int>(1);
                     CK(cudaMemset(s->d_tc_err, 0, sizeof(int)));
+                    s->tc_part_cap = (size_t)kTcSplitMax * 128 * (size_t)(4 * D);
+                    s->d_tc_part = dalloc<float>(s->tc_part_cap);
                 }
                 s->d_logits = dalloc<float>((size_t)(cnt + kMaxChunkSlots) * m->V);
                 s->d_lnf = dalloc<float>((size_t)std::max(cnt, kMaxChunkSlots) * D);
@@ -1978,20 +2014,22 @@ int32_t fb2_test_gemm_tc(int32_t M, int32_t N, int32_t K, const float* A, const 
         float *a = buf, *ahi = a + na, *alo = ahi + na, *w = alo + na, *whi = w + nw, *wlo = whi + nw, *o = wlo + nw;
         float* bias = o + no;
         int* err = dalloc<int>(1);
+        float* part = nullptr;
         try {
             CK(cudaMemcpy(a, A, na * 4, cudaMemcpyHostToDevice));
             CK(cudaMemcpy(w, W, nw * 4, cudaMemcpyHostToDevice));
             CK(cudaMemset(bias, 0, (size_t)N * 4));
             CK(cudaMemset(err, 0, sizeof(int)));
-            launch_split_tf32(0, a, na, ahi, alo);
             launch_split_tf32_transpose(0, w, K, N, whi, wlo);
-            TcMaps maps;
-            if (!tc_encode(&maps.a_hi, ahi, K, M, TC_BM) || !tc_encode(&maps.a_lo, alo, K, M, TC_BM) ||
-                !tc_encode(&maps.b_hi, whi, K, N, TC_BN) || !tc_encode(&maps.b_lo, wlo, K, N, TC_BN))
+            CUtensorMap bm[2];
+            if (!tc_encode(&bm[0], whi, K, N, 128) || !tc_encode(&bm[1], wlo, K, N, 128))
                 fail(FB2_CUDA_ERROR, "cuTensorMapEncodeTiled failed");
+            const size_t cap = (size_t)kTcSplitMax * M * N;
+            part = dalloc<float>(cap);
+            int64_t launches = 0;
             Epi e = make_epi(EPI_BIAS, bias, nullptr, o);
-            dim3 grid(ceil_div(N, TC_BN), ceil_div(M, TC_BM));
-            k_gemm_tc<<<grid, 128, TC_SMEM>>>(maps, M, N, K, e, err);
+            if (!launch_gemm_tc(0, 148, M, K, N, a, ahi, alo, bm, e, err, part, cap, &launches))
+                fail(FB2_UNSUPPORTED, "the tensor-core GEMM takes more than 16 rows");
             CK(cudaGetLastError());
             CK(cudaDeviceSynchronize());
             int herr = 0;
@@ -2001,10 +2039,12 @@ int32_t fb2_test_gemm_tc(int32_t M, int32_t N, int32_t K, const float* A, const 
         } catch (...) {
             dfree(buf);
             dfree(err);
+            dfree(part);
             throw;
         }
         dfree(buf);
         dfree(err);
+        dfree(part);
     });
 }
 

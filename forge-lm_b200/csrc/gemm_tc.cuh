@@ -35,11 +35,18 @@
 
 namespace fb2 {
 
-constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 32, TC_STAGES = 3;
-constexpr int TC_TILE_A = TC_BM * TC_BK * 4;                      // 16 KB
-constexpr int TC_TILE_B = TC_BN * TC_BK * 4;                      // 16 KB
-constexpr int TC_STAGE_BYTES = 2 * TC_TILE_A + 2 * TC_TILE_B;     // 64 KB
-constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024;        // + alignment slack
+constexpr int TC_BM = 128, TC_BK = 32;
+constexpr int TC_TILE_A = TC_BM * TC_BK * 4;  // 16 KB: 128 rows x 32 fp32
+
+// Tile shape of the prefill GEMM (one CTA per 128 x BN output tile).
+template <int BN>
+struct TcCfg {
+    static constexpr int TILE_B = BN * TC_BK * 4;
+    static constexpr int STAGE = 2 * TC_TILE_A + 2 * TILE_B;
+    static constexpr int STAGES = (200 * 1024) / STAGE > 8 ? 8 : (200 * 1024) / STAGE;
+    static constexpr int SMEM = STAGES * STAGE + 1024;  // + alignment slack
+    static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+};
 constexpr unsigned long long kTcTimeoutNs = 2000000000ull;
 constexpr int TC_ERR_TIMEOUT = 1;
 
@@ -183,20 +190,24 @@ __global__ void k_split_tf32(const float4* __restrict__ x, size_t n4, float4* __
     }
 }
 
+// gridDim = (ceil(N/BN), ceil(M/128)).
+template <int BN>
 __global__ void __launch_bounds__(128, 1) k_gemm_tc(const __grid_constant__ TcMaps maps, int M, int N, int K, Epi e,
                                                     int* err) {
+    using Cfg = TcCfg<BN>;
+    constexpr int STAGES = Cfg::STAGES, STAGE = Cfg::STAGE, TILE_B = Cfg::TILE_B;
     extern __shared__ unsigned char tc_smem_raw[];
-    __shared__ __align__(8) uint64_t full[TC_STAGES], empty[TC_STAGES], accb;
+    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], accb;
     __shared__ uint32_t tmem_base;
     __shared__ volatile int s_abort;
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int m0 = blockIdx.y * TC_BM, n0 = blockIdx.x * TC_BN;
+    const int m0 = blockIdx.y * TC_BM, n0 = blockIdx.x * BN;
     const int nk = (K + TC_BK - 1) / TC_BK;
 
     if (tid == 0) {
         s_abort = 0;
-        for (int i = 0; i < TC_STAGES; i++) {
+        for (int i = 0; i < STAGES; i++) {
             tc::bar_init(&full[i], 1);
             tc::bar_init(&empty[i], 1);
         }
@@ -205,7 +216,7 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(const __grid_constant__ TcMa
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc::smem_addr(&tmem_base)),
-                     "r"((uint32_t)TC_BN)
+                     "r"((uint32_t)Cfg::TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -216,27 +227,26 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(const __grid_constant__ TcMa
 
     if (warp == 0 && lane == 0) {
         // ---- producer ----
-        for (int kb = 0; kb < nk; kb++) {
-            const int st = kb % TC_STAGES;
-            if (kb >= TC_STAGES && !tc::bar_wait(&empty[st], ((kb / TC_STAGES) - 1) & 1, &s_abort)) break;
-            unsigned char* sb = sm + (size_t)st * TC_STAGE_BYTES;
-            tc::bar_expect_tx(&full[st], TC_STAGE_BYTES);
-            const int k0 = kb * TC_BK;
+        for (int i = 0; i < nk; i++) {
+            const int st = i % STAGES;
+            if (i >= STAGES && !tc::bar_wait(&empty[st], ((i / STAGES) - 1) & 1, &s_abort)) break;
+            unsigned char* sb = sm + (size_t)st * STAGE;
+            tc::bar_expect_tx(&full[st], STAGE);
+            const int k0 = i * TC_BK;
             tc::tma_load_2d(sb, &maps.a_hi, k0, m0, &full[st]);
             tc::tma_load_2d(sb + TC_TILE_A, &maps.a_lo, k0, m0, &full[st]);
             tc::tma_load_2d(sb + 2 * TC_TILE_A, &maps.b_hi, k0, n0, &full[st]);
-            tc::tma_load_2d(sb + 2 * TC_TILE_A + TC_TILE_B, &maps.b_lo, k0, n0, &full[st]);
+            tc::tma_load_2d(sb + 2 * TC_TILE_A + TILE_B, &maps.b_lo, k0, n0, &full[st]);
         }
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer ----
-        constexpr uint32_t idesc = tc::idesc_tf32(TC_BM, TC_BN);
-        int kb = 0;
-        for (; kb < nk; kb++) {
-            const int st = kb % TC_STAGES;
-            if (!tc::bar_wait(&full[st], (kb / TC_STAGES) & 1, &s_abort)) break;
+        constexpr uint32_t idesc = tc::idesc_tf32(TC_BM, BN);
+        for (int i = 0; i < nk; i++) {
+            const int st = i % STAGES;
+            if (!tc::bar_wait(&full[st], (i / STAGES) & 1, &s_abort)) break;
             tc::fence_after();
-            const uint32_t sa = tc::smem_addr(sm + (size_t)st * TC_STAGE_BYTES);
-            const uint32_t a_hi = sa, a_lo = sa + TC_TILE_A, b_hi = sa + 2 * TC_TILE_A, b_lo = b_hi + TC_TILE_B;
+            const uint32_t sa = tc::smem_addr(sm + (size_t)st * STAGE);
+            const uint32_t a_hi = sa, a_lo = sa + TC_TILE_A, b_hi = sa + 2 * TC_TILE_A, b_lo = b_hi + TILE_B;
 #pragma unroll
             for (int ks = 0; ks < TC_BK / 8; ks++) {
                 // K-major rows of 128 B, 8-row swizzle atoms 1024 B apart;
@@ -245,7 +255,7 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(const __grid_constant__ TcMa
                 const uint64_t dal = tc::sw128_desc(a_lo + ks * 32, 16, 1024);
                 const uint64_t dbh = tc::sw128_desc(b_hi + ks * 32, 16, 1024);
                 const uint64_t dbl = tc::sw128_desc(b_lo + ks * 32, 16, 1024);
-                tc::mma_tf32(tmem, dah, dbh, idesc, (kb | ks) != 0);
+                tc::mma_tf32(tmem, dah, dbh, idesc, (i | ks) != 0);
                 tc::mma_tf32(tmem, dah, dbl, idesc, 1u);
                 tc::mma_tf32(tmem, dal, dbh, idesc, 1u);
             }
@@ -268,17 +278,18 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(const __grid_constant__ TcMa
     }
     __syncwarp();
     tc::fence_after();
-    if (ok && !s_abort) {
-        const int row = m0 + warp * 32 + lane;
+    const int row = m0 + warp * 32 + lane;
+    if (ok && !s_abort && nk > 0) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < TC_BN; c0 += 16) {
+        for (int c0 = 0; c0 < BN; c0 += 16) {
             float v[16];
             tc::tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
             if (row < M) {
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
                     const int n = n0 + c0 + 4 * q;
-                    if (n < N) epi_store4(e, row, n, N, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+                    if (n >= N) continue;
+                    epi_store4(e, row, n, N, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
                 }
             }
         }
@@ -287,10 +298,10 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(const __grid_constant__ TcMa
         atomicExch(err, TC_ERR_TIMEOUT);
         // copies the issuer never consumed may still be landing: wait for
         // every stage's latest fill (bounded) before the CTA's memory goes
-        for (int st = 0; st < TC_STAGES && st < nk; st++) {
-            const int last = st + ((nk - 1 - st) / TC_STAGES) * TC_STAGES;  // last k block using stage st
+        for (int st = 0; st < STAGES && st < nk; st++) {
+            const int last = st + ((nk - 1 - st) / STAGES) * STAGES;  // last k block using stage st
             const unsigned long long t0 = tc::now_ns();
-            while (!tc::bar_try(&full[st], (last / TC_STAGES) & 1) && tc::now_ns() - t0 < kTcTimeoutNs / 4) {
+            while (!tc::bar_try(&full[st], (last / STAGES) & 1) && tc::now_ns() - t0 < kTcTimeoutNs / 4) {
             }
         }
     }
@@ -298,7 +309,159 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(const __grid_constant__ TcMa
     __syncthreads();
     if (warp == 0) {
         tc::fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)TC_BN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)Cfg::TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Decode batches (17..128 rows): the same 3xTF32 tensor-core product with the
+// operands swapped, y^T = W^T * A^T.  The weights (W^T [N][K], K-major) are
+// the 128-row MMA operand, read exactly once per step across the grid; the
+// batch rows (A [M][K]) are the BNB-column operand.  TMEM lane = output
+// column n, TMEM column = batch row m.  gridDim = (ceil(N/128),
+// ceil(M/BNB), S): with S > 1 each CTA writes partial[z][M][N] and
+// k_splitk_reduce sums the splits in order and applies the epilogue.
+template <int BNB>
+struct TcSwabCfg {
+    static constexpr int TILE_B = BNB * TC_BK * 4;
+    static constexpr int STAGE = 2 * TC_TILE_A + 2 * TILE_B;
+    static constexpr int STAGES = (200 * 1024) / STAGE > 8 ? 8 : (200 * 1024) / STAGE;
+    static constexpr int SMEM = STAGES * STAGE + 1024;
+};
+
+template <int BNB>
+__global__ void __launch_bounds__(128, 1) k_gemm_tc_swab(const __grid_constant__ TcMaps maps, int M, int N, int K,
+                                                         Epi e, int* err, float* __restrict__ partial) {
+    using Cfg = TcSwabCfg<BNB>;
+    constexpr int STAGES = Cfg::STAGES, STAGE = Cfg::STAGE, TILE_B = Cfg::TILE_B;
+    extern __shared__ unsigned char tc_smem_raw[];
+    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], accb;
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int s_abort;
+    unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * 128, m0 = blockIdx.y * BNB;
+    const int S = gridDim.z, z = blockIdx.z;
+    const int nk_all = (K + TC_BK - 1) / TC_BK;
+    const int kb0 = (int)(((long long)z * nk_all) / S), kb1 = (int)(((long long)(z + 1) * nk_all) / S);
+    const int nk = kb1 - kb0;
+
+    if (tid == 0) {
+        s_abort = 0;
+        for (int i = 0; i < STAGES; i++) {
+            tc::bar_init(&full[i], 1);
+            tc::bar_init(&empty[i], 1);
+        }
+        tc::bar_init(&accb, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc::smem_addr(&tmem_base)),
+                     "r"((uint32_t)BNB)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = tmem_base;
+
+    if (warp == 0 && lane == 0) {
+        for (int i = 0; i < nk; i++) {
+            const int st = i % STAGES;
+            if (i >= STAGES && !tc::bar_wait(&empty[st], ((i / STAGES) - 1) & 1, &s_abort)) break;
+            unsigned char* sb = sm + (size_t)st * STAGE;
+            tc::bar_expect_tx(&full[st], STAGE);
+            const int k0 = (kb0 + i) * TC_BK;
+            // maps.b_* = weights W^T (128-row boxes), maps.a_* = batch rows (BNB-row boxes)
+            tc::tma_load_2d(sb, &maps.b_hi, k0, n0, &full[st]);
+            tc::tma_load_2d(sb + TC_TILE_A, &maps.b_lo, k0, n0, &full[st]);
+            tc::tma_load_2d(sb + 2 * TC_TILE_A, &maps.a_hi, k0, m0, &full[st]);
+            tc::tma_load_2d(sb + 2 * TC_TILE_A + TILE_B, &maps.a_lo, k0, m0, &full[st]);
+        }
+    } else if (warp == 1 && lane == 0) {
+        constexpr uint32_t idesc = tc::idesc_tf32(128, BNB);
+        for (int i = 0; i < nk; i++) {
+            const int st = i % STAGES;
+            if (!tc::bar_wait(&full[st], (i / STAGES) & 1, &s_abort)) break;
+            tc::fence_after();
+            const uint32_t sa = tc::smem_addr(sm + (size_t)st * STAGE);
+            const uint32_t w_hi = sa, w_lo = sa + TC_TILE_A, x_hi = sa + 2 * TC_TILE_A, x_lo = x_hi + TILE_B;
+#pragma unroll
+            for (int ks = 0; ks < TC_BK / 8; ks++) {
+                const uint64_t dwh = tc::sw128_desc(w_hi + ks * 32, 16, 1024);
+                const uint64_t dwl = tc::sw128_desc(w_lo + ks * 32, 16, 1024);
+                const uint64_t dxh = tc::sw128_desc(x_hi + ks * 32, 16, 1024);
+                const uint64_t dxl = tc::sw128_desc(x_lo + ks * 32, 16, 1024);
+                tc::mma_tf32(tmem, dwh, dxh, idesc, (i | ks) != 0);
+                tc::mma_tf32(tmem, dwh, dxl, idesc, 1u);
+                tc::mma_tf32(tmem, dwl, dxh, idesc, 1u);
+            }
+            tc::mma_commit(&empty[st]);
+        }
+        tc::mma_commit(&accb);
+    }
+    __syncwarp();
+
+    bool ok = tc::bar_try(&accb, 0);
+    if (!ok) {
+        const unsigned long long t0 = tc::now_ns();
+        while (!(ok = tc::bar_try(&accb, 0)) && tc::now_ns() - t0 < kTcTimeoutNs) {
+        }
+        if (!ok) s_abort = 1;
+    }
+    __syncwarp();
+    tc::fence_after();
+    const int n = n0 + warp * 32 + lane;  // this thread's output column (TMEM lane)
+    if (ok && !s_abort && nk > 0) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BNB; c0 += 16) {
+            float v[16];
+            tc::tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+            if (n < N) {
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const int m = m0 + c0 + i;
+                    if (m >= M) break;
+                    if (S == 1) epi_store1(e, m, n, N, v[i]);
+                    else partial[((size_t)z * M + m) * N + n] = v[i];
+                }
+            }
+        }
+    }
+    if (s_abort && tid == 0) {
+        atomicExch(err, TC_ERR_TIMEOUT);
+        for (int st = 0; st < STAGES && st < nk; st++) {
+            const int last = st + ((nk - 1 - st) / STAGES) * STAGES;
+            const unsigned long long t0 = tc::now_ns();
+            while (!tc::bar_try(&full[st], (last / STAGES) & 1) && tc::now_ns() - t0 < kTcTimeoutNs / 4) {
+            }
+        }
+    }
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BNB) : "memory");
+    }
+}
+
+// y[m][n..n+3] = epilogue(sum over z = 0..S-1 of partial[z][m][n..n+3]).
+__global__ void k_splitk_reduce(const float* __restrict__ partial, int S, int M, int N, Epi e) {
+    const int n4 = N / 4;
+    const size_t total = (size_t)M * n4;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int m = (int)(i / n4), n = (int)(i - (size_t)m * n4) * 4;
+        float4 acc = __ldcg(reinterpret_cast<const float4*>(partial + (size_t)m * N + n));
+        for (int z = 1; z < S; z++) {
+            const float4 p = __ldcg(reinterpret_cast<const float4*>(partial + ((size_t)z * M + m) * N + n));
+            acc.x += p.x;
+            acc.y += p.y;
+            acc.z += p.z;
+            acc.w += p.w;
+        }
+        epi_store4(e, m, n, N, acc);
     }
 }
 

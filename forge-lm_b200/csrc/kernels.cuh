@@ -118,6 +118,31 @@ struct Epi {
     Rows R;
 };
 
+// One output element through the same epilogue as epi_store4.
+FB2_DEV void epi_store1(const Epi& e, int m, int n, int N, float a) {
+    a += e.bias[n];
+    if (e.kind == EPI_RESID) {
+        a += e.resid[(size_t)m * N + n];
+    } else if (e.kind == EPI_GELU) {
+        a = gelu_tanh(a);
+    } else if (e.kind == EPI_QKV) {
+        const int D = e.D;
+        if (n < D) {
+            e.out[(size_t)m * D + n] = a;
+            return;
+        }
+        if (!e.R.active[m]) return;
+        const int pos = e.R.pos[m];
+        if (pos < 0 || pos >= e.ctx) return;
+        const int which = n < 2 * D ? 0 : 1;
+        const int c = n - D - which * D;
+        const int h = c / e.hd, d = c - h * e.hd;
+        e.kv_layer[(size_t)e.R.seq[m] * e.kv_slot_stride + (which ? e.v_offset : 0) + ((size_t)h * e.ctx + pos) * e.hd + d] = a;
+        return;
+    }
+    e.out[(size_t)m * N + n] = a;
+}
+
 FB2_DEV void epi_store4(const Epi& e, int m, int n, int N, float4 a) {
     float4 bb = *reinterpret_cast<const float4*>(e.bias + n);
     a.x += bb.x; a.y += bb.y; a.z += bb.z; a.w += bb.w;

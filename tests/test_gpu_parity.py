@@ -87,10 +87,12 @@ def test_teacher_forced_decode_matches_full_forward(pkg, O):
 
 # ---------------------------------------------------------------------------
 @pytest.mark.parametrize("M,N,K", [(128, 128, 32), (300, 200, 100), (1024, 768, 768), (256, 3072, 768),
-                                   (200, 768, 3072)])
+                                   (200, 768, 3072), (17, 768, 768), (64, 2304, 768), (64, 768, 3072),
+                                   (100, 36, 100)])
 def test_tensor_core_gemm_3xtf32(pkg, M, N, K):
-    """The tcgen05 3xTF32 GEMM of the prefill projections against an fp64
-    product, ragged M, N, K.  The bound (relative to the largest output) is
+    """The tcgen05 3xTF32 GEMM of the projections against an fp64 product,
+    ragged M, N, K: 128-column tiles (M >= 128) and 32-column split-K tiles
+    (decode batches, M < 128).  The bound (relative to the largest output) is
     3xTF32 accuracy with the tensor cores' fp32 accumulation, which grows with
     the depth K: 2e-5 up to K = 768, 5e-5 at K = 3072.  A single TF32 product
     would be ~1e-3, the logits tolerance of the parity tests."""
