@@ -176,6 +176,9 @@ static void configure_kernels(int dev) {
     setmax((const void*)k_attn_prefill<32>, 227 * 1024);
     setmax((const void*)k_attn_prefill<64>, 227 * 1024);
     setmax((const void*)k_attn_prefill<128>, 227 * 1024);
+    setmax((const void*)k_attn_prefill_rt<32>, 227 * 1024);
+    setmax((const void*)k_attn_prefill_rt<64>, 227 * 1024);
+    setmax((const void*)k_attn_prefill_rt<128>, 227 * 1024);
     setmax((const void*)k_head<1>, 227 * 1024);
     setmax((const void*)k_head<2>, 227 * 1024);
     setmax((const void*)k_head<4>, 227 * 1024);
@@ -647,6 +650,13 @@ static void launch_attn_prefill_hd(DeviceSession& s, int nblk, const int4* qblk,
     const fb2_model& m = *s.model;
     float scale = 1.0f / sqrtf((float)m.hd);
     const float* kvl = s.d_kv + (size_t)layer * s.kv_layer_stride;
+    if constexpr (HD == 32 || HD == 64 || HD == 128) {
+        const size_t smem = (size_t)(64 * (HD + 4) * 2 + 64 * HD + 64 * 68) * 4;
+        s.stats.kernel_launches++;
+        k_attn_prefill_rt<HD><<<dim3(nblk, m.H), 256, smem, s.stream>>>(s.d_q, kvl, s.kv_slot_stride, s.v_offset, m.H,
+                                                                        m.ctx, scale, qblk, s.d_att);
+        return;
+    }
     size_t smem = (size_t)(64 * (HD + 1) * 2 + 64 * HD + 64 * 65) * 4;
     s.stats.kernel_launches++; k_attn_prefill<HD><<<dim3(nblk, m.H), 256, smem, s.stream>>>(s.d_q, kvl, s.kv_slot_stride, s.v_offset, m.H,
                                                                  m.ctx, scale, qblk, s.d_att);

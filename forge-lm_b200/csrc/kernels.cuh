@@ -557,6 +557,141 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const float* __restrict__ 
 }
 
 // ---------------------------------------------------------------------------
+// Prefill attention, register-tiled (HD in {32, 64, 128}): the same causal
+// flash-style online softmax as k_attn_prefill, with thread (tq, tk) of the
+// 16 x 16 grid computing scores of queries 4tq..4tq+3 against keys tk + 16j
+// (float4 loads along the head dimension), and then the 4 queries' context
+// for dims tk*HD/16 .. +HD/16.  qblk[b] = {first row, count, seq, first
+// position}; one CTA per (query block of <= 64 rows, head).
+// ---------------------------------------------------------------------------
+template <int HD>
+__global__ void __launch_bounds__(256) k_attn_prefill_rt(const float* __restrict__ q, const float* __restrict__ kv_layer,
+                                                         long long kv_slot_stride, long long v_offset, int H, int ctx,
+                                                         float scale, const int4* __restrict__ qblk,
+                                                         float* __restrict__ ctx_out) {
+    constexpr int BQ = 64, BK = 64, LD = HD + 4, LP = BK + 4, DPT = HD / 16;
+    static_assert(HD % 16 == 0 && HD <= 128, "head dim");
+    extern __shared__ __align__(16) float sm[];
+    float* Qs = sm;               // [BQ][LD]
+    float* Ks = Qs + BQ * LD;     // [BK][LD]
+    float* Vs = Ks + BK * LD;     // [BK][HD]
+    float* Ps = Vs + BK * HD;     // [BQ][LP]
+    const int4 blk = qblk[blockIdx.x];
+    const int h = blockIdx.y;
+    const int row0 = blk.x, nq = blk.y, seq = blk.z, p0 = blk.w;
+    const int D = H * HD;
+    const int tid = threadIdx.x, tq = tid >> 4, tk = tid & 15;
+    for (int i = tid; i < BQ * (HD / 4); i += 256) {
+        const int r = i / (HD / 4), d4 = i - r * (HD / 4);
+        const float4 v = r < nq ? *reinterpret_cast<const float4*>(q + (size_t)(row0 + r) * D + h * HD + 4 * d4)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(Qs + r * LD + 4 * d4) = v;
+    }
+    const float* Kb = kv_layer + (size_t)seq * kv_slot_stride + (size_t)h * ctx * HD;
+    const float* Vb = Kb + v_offset;
+    float o[4][DPT];
+    float m[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int e = 0; e < DPT; e++) o[i][e] = 0.f;
+    }
+    const int last_key = p0 + nq - 1;
+    for (int kt = 0; kt <= last_key; kt += BK) {
+        __syncthreads();
+        for (int i = tid; i < BK * (HD / 4); i += 256) {
+            const int j = i / (HD / 4), d4 = i - j * (HD / 4);
+            const bool ok = kt + j <= last_key;
+            const float4 kk = ok ? *reinterpret_cast<const float4*>(Kb + (size_t)(kt + j) * HD + 4 * d4)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 vv = ok ? *reinterpret_cast<const float4*>(Vb + (size_t)(kt + j) * HD + 4 * d4)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(Ks + j * LD + 4 * d4) = kk;
+            *reinterpret_cast<float4*>(Vs + j * HD + 4 * d4) = vv;
+        }
+        __syncthreads();
+        float sc[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) sc[i][j] = 0.f;
+#pragma unroll 4
+        for (int d = 0; d < HD; d += 4) {
+            float4 qa[4], ka[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) qa[i] = *reinterpret_cast<const float4*>(Qs + (4 * tq + i) * LD + d);
+#pragma unroll
+            for (int j = 0; j < 4; j++) ka[j] = *reinterpret_cast<const float4*>(Ks + (tk + 16 * j) * LD + d);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    sc[i][j] += qa[i].x * ka[j].x + qa[i].y * ka[j].y + qa[i].z * ka[j].z + qa[i].w * ka[j].w;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int qr = 4 * tq + i, qpos = p0 + qr;
+            float tmax = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                float d = sc[i][j] * scale;
+                if (kt + tk + 16 * j > qpos || qr >= nq) d = -INFINITY;  // causal mask (CpuBackend.cs:547-553)
+                sc[i][j] = d;
+                tmax = fmaxf(tmax, d);
+            }
+#pragma unroll
+            for (int o2 = 1; o2 < 16; o2 <<= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o2));
+            const float mnew = fmaxf(m[i], tmax);
+            const float corr = (mnew == -INFINITY) ? 1.f : __expf(m[i] - mnew);
+            float psum = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float pv = (sc[i][j] == -INFINITY) ? 0.f : __expf(sc[i][j] - mnew);
+                Ps[qr * LP + tk + 16 * j] = pv;
+                psum += pv;
+            }
+#pragma unroll
+            for (int o2 = 1; o2 < 16; o2 <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o2);
+            l[i] = l[i] * corr + psum;
+            m[i] = mnew;
+#pragma unroll
+            for (int e = 0; e < DPT; e++) o[i][e] *= corr;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int j = 0; j < BK; j++) {
+            float pv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) pv[i] = Ps[(4 * tq + i) * LP + j];
+            float vv[DPT];
+#pragma unroll
+            for (int e = 0; e < DPT; e += 4) {
+                const float4 v4 = *reinterpret_cast<const float4*>(Vs + j * HD + tk * DPT + e);
+                vv[e] = v4.x;
+                if (e + 1 < DPT) vv[e + 1] = v4.y;
+                if (e + 2 < DPT) vv[e + 2] = v4.z;
+                if (e + 3 < DPT) vv[e + 3] = v4.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int e = 0; e < DPT; e++) o[i][e] += pv[i] * vv[e];
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int qr = 4 * tq + i;
+        if (qr >= nq) continue;
+        const float inv = 1.0f / l[i];
+        float* out = ctx_out + (size_t)(row0 + qr) * D + h * HD + tk * DPT;
+#pragma unroll
+        for (int e = 0; e < DPT; e++) out[e] = o[i][e] * inv;
+    }
+}
+
+// ---------------------------------------------------------------------------
 // LM head on selected rows (TiedOutputProjection.Forward, Layers.cs:80-86,
 // last row only): logits[m][v] = dot(xln[m], tok_emb[v]).  One warp per
 // vocab row, MR rows at a time, xln staged in shared memory.
