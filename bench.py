@@ -7,6 +7,11 @@ Workloads (synthetic seeded weights and prompts):
       generate (prefill + 512 sampled tokens).
   c3: Forge-98M fp32, 64 sequences split evenly over the GPUs, prompts of
       256 ids, 768 greedy tokens.  One step = one generate of the shard.
+  c4: forge-220m fp32, 16 sequences split over the GPUs, prompts of 1024 ids
+      (the full context), sampled at T 0.7, top-k 30: every new token slides
+      the window, so every step re-prefills all 1024 positions (tensor-core
+      bound).  One bench step = 16 new tokens of the 512 the workload names
+      (a bounded sample; each token costs the same full re-prefill).
 Metric: decode tokens/s, whole job (sum over GPUs), max over ranks of the
 device time.  N>1: one process per GPU, independent sequences, no data-path
 collective (weak scaling for c2, strong for c3).
@@ -30,6 +35,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 FORGE_98M = dict(vocab_size=16384, context_length=1024, d_model=768, n_layers=12, n_heads=12)
+FORGE_220M = dict(vocab_size=16384, context_length=1024, d_model=1024, n_layers=16, n_heads=16)
 WEIGHT_SEED = 1234
 
 WORKLOADS = {
@@ -39,7 +45,25 @@ WORKLOADS = {
     "c3": dict(name="Forge-98M fp32 bs64: prompts 256, 768 greedy tokens, sequences split over GPUs",
                model=FORGE_98M, seqs_total=64, seqs_per_gpu=None, prompt_len=256, new_tokens=768,
                temperature=0.0, top_k=0, penalty=1.0, ngram=0, scaling="strong"),
+    "c4": dict(name="forge-220m fp32 bs16: prompts 1024 (full context), sampled T 0.7 top-k 30; every token "
+                    "re-prefills the 1024-token window; 16 of the 512 tokens per bench step",
+               model=FORGE_220M, seqs_total=16, seqs_per_gpu=None, prompt_len=1024, new_tokens=16,
+               temperature=0.7, top_k=30, penalty=1.0, ngram=0, scaling="strong", bound="tensor"),
 }
+
+
+def model_name(m: dict) -> str:
+    name = "Forge-98M" if m == FORGE_98M else "forge-220m" if m == FORGE_220M else "custom"
+    return (f"{name} (V {m['vocab_size']}, ctx {m['context_length']}, D {m['d_model']}, L {m['n_layers']}, "
+            f"H {m['n_heads']})")
+
+
+def flops_per_sequence_step(m: dict, T: int) -> float:
+    """FLOPs of one full re-forward of a T-token window (the sliding-window
+    step): the block projections for every row, causal attention (scores
+    and context, T(T+1)/2 pairs each), and the head on the last row."""
+    D, L, V = m["d_model"], m["n_layers"], m["vocab_size"]
+    return 2.0 * T * L * 12 * D * D + 2.0 * L * T * (T + 1) * D + 2.0 * D * V
 
 
 def parse():
@@ -166,8 +190,9 @@ def cpu_reference_sample(wl: dict, seconds_target: float = 15.0, max_tokens: int
     dt = time.perf_counter() - t0
     return {"value": len(out) / dt, "unit": "tokens/s", "cores": O.get_threads(), "kind": "port",
             "sample": f"first {len(out)} of {wl['new_tokens']} tokens of sequence 0 (prompt {wl['prompt_len']}), "
-                      f"full re-forward per token as the reference CPU backend does; later tokens cost more "
-                      f"(window grows), so this over-states the full-run rate",
+                      f"full re-forward per token as the reference CPU backend does"
+                      + ("" if wl["prompt_len"] >= m["context_length"] else
+                         "; later tokens cost more (window grows), so this over-states the full-run rate"),
             "seconds": dt}
 
 
@@ -313,7 +338,25 @@ def main():
             peaks = json.load(f)
     except OSError:
         pass
-    peak = float(peaks.get("hbm_gbs", 6650.0))
+    if wl.get("bound") == "tensor":
+        # every step re-forwards each sequence's full window
+        flops_step = count * flops_per_sequence_step(m, m["context_length"])
+        roofline = {"bound": "tensor", "kernel": "k_gemm_tc (tcgen05 3xTF32 GEMM) + k_attn_prefill_rt",
+                    "achieved": flops_step / (step_ms / 1000.0) / 1e12,
+                    "peak": float(peaks.get("bf16_tflops", 1590.0)), "unit": "TFLOP/s",
+                    "peak_source": ("measured (MEASURED_PEAKS.json bf16_tflops; the GEMMs run TF32 with 3 MMAs per "
+                                    "product for fp32 parity, and the TF32 dense rate is half the bf16 rate)")
+                    if peaks else "fallback", "traffic": None, "step_ms": step_ms,
+                    "algorithmic_flops_per_step": flops_step}
+        roofline["frac"] = roofline["achieved"] / roofline["peak"]
+    else:
+        peak = float(peaks.get("hbm_gbs", 6650.0))
+        roofline = {"bound": "hbm",
+                    "kernel": "k_decode_mega (persistent decode kernel: cp.async.bulk weight stream, on-device "
+                              "sampler)" if persistent else "decode step (CUDA graph replay of the step kernels)",
+                    "achieved": achieved_gbs, "peak": peak, "unit": "GB/s", "frac": achieved_gbs / peak,
+                    "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
+                    "traffic": None, "step_ms": step_ms, "algorithmic_bytes_per_step": bytes_step}
 
     # ---- e2e: the public host-buffer call, copies inside the timed region ----
     if args.skip_e2e:
@@ -351,16 +394,12 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": wl["scaling"], "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init weights, uniform-random prompt ids)",
-            "config": {"workload": wl["name"], "model": "Forge-98M (V 16384, ctx 1024, D 768, L 12, H 12)",
+            "config": {"workload": wl["name"], "model": model_name(m),
                        "sequences_per_gpu": count, "prompt_len": plen, "new_tokens": new,
                        "parallelism": f"request-parallel x{world} (independent sequences, no collective)",
-                       "l2": "inputs larger than L2: every decode step streams 390 MB of weights"},
-            "roofline": {"bound": "hbm",
-                         "kernel": "k_decode_mega (persistent decode kernel: cp.async.bulk weight stream, on-device "
-                                   "sampler)" if persistent else "decode step (CUDA graph replay of the step kernels)",
-                         "achieved": achieved_gbs, "peak": peak, "unit": "GB/s", "frac": achieved_gbs / peak,
-                         "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
-                         "traffic": None, "step_ms": step_ms, "algorithmic_bytes_per_step": bytes_step},
+                       "l2": f"inputs larger than L2: every decode step streams {weight_bytes(m) / 1e6:.0f} MB "
+                             f"of weights"},
+            "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": int(st.get("kernel_launches", 0)),

@@ -228,6 +228,27 @@ def test_forge98m_vocabulary_persistent_and_graph_paths(pkg, O, monkeypatch):
             assert relerr(tf[0, k], O.forward_last(ocfg, params, toks[0, :40 + k])) <= TOL, (mode, k)
 
 
+def test_full_context_prompts_reprefill_every_step(pkg, O):
+    """The forge-220m bs16 pattern on a small model:
+    prompts fill the context, so every sampled token slides the window and
+    re-forwards it (Sampler.cs:93-94) -- the tensor-core GEMM and the
+    register-tiled attention prefill on every step."""
+    shape = (600, 64, 64, 2, 2)
+    ocfg = O.Config(*shape)
+    params = O.init_params(ocfg, 31)
+    rng = np.random.default_rng(12)
+    prompts = [rng.integers(0, shape[0], 64).astype(np.int32) for _ in range(3)]
+    seeds = [7, 8, 9]
+    be = pkg.B200Backend(pkg.ModelConfig(*shape), params, devices=[0], max_seqs=3)
+    with be:
+        got = be.generate_batch([p.tolist() for p in prompts], 20, 0.7, 30, seeds=seeds)
+        st = be.stats()
+    assert st["reprefills"] == 3 * 19
+    for i, p in enumerate(prompts):
+        want = O.generate(ocfg, params, p, 20, 0.7, 30, O.DotNetRandom(seeds[i]))
+        check_ids(O, ocfg, params, p, got[i], want)
+
+
 def test_generate_batch_ragged_and_long_prompts(pkg, O):
     shape = (300, 24, 32, 2, 2)
     ocfg, params, be = make(pkg, O, shape, 9, max_seqs=5)
