@@ -36,6 +36,11 @@ sys.path.insert(0, ROOT)
 
 FORGE_98M = dict(vocab_size=16384, context_length=1024, d_model=768, n_layers=12, n_heads=12)
 FORGE_220M = dict(vocab_size=16384, context_length=1024, d_model=1024, n_layers=16, n_heads=16)
+# DRAM bytes per decode step of the persistent kernel over the algorithmic
+# bytes at the same positions: 396.6 MB measured / 395.9 MB, ncu capture of
+# 15 C2 steps (profiles/k_decode_mega_c2.md).  KV bytes scale with T and the
+# weights are fixed, so the bench reports ratio x algorithmic bytes.
+MK_TRAFFIC_RATIO = 396.58 / 395.92
 WEIGHT_SEED = 1234
 
 WORKLOADS = {
@@ -356,7 +361,9 @@ def main():
                               "sampler)" if persistent else "decode step (CUDA graph replay of the step kernels)",
                     "achieved": achieved_gbs, "peak": peak, "unit": "GB/s", "frac": achieved_gbs / peak,
                     "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
-                    "traffic": None, "step_ms": step_ms, "algorithmic_bytes_per_step": bytes_step}
+                    "traffic": MK_TRAFFIC_RATIO * bytes_step if persistent and count == 1 else None,
+                    "traffic_unit": "bytes per decode step (ncu dram read+write, scaled to this workload's "
+                                    "positions)", "step_ms": step_ms, "algorithmic_bytes_per_step": bytes_step}
 
     # ---- e2e: the public host-buffer call, copies inside the timed region ----
     if args.skip_e2e:
