@@ -110,11 +110,14 @@ class B200Backend:
     params: the model's weights in Parameters.Names order (float32 arrays of
     the shapes `param_shapes(config)` gives), e.g. as Checkpoint.LoadCore
     read them (src/LLM.Core/Checkpoint/Checkpoint.cs:222-227).  The library
-    copies them; the caller keeps ownership.
+    copies them; the caller keeps ownership.  weight_dtype "bf16" stores
+    tok_emb and the projections rounded to bf16 (FB2_WEIGHTS_BF16).
     """
 
     def __init__(self, config: ModelConfig, params: Sequence[np.ndarray], devices: Iterable[int] | None = None,
-                 max_seqs: int = 1):
+                 max_seqs: int = 1, weight_dtype: str = "fp32"):
+        if weight_dtype not in ("fp32", "bf16"):
+            raise ArgumentError(N.FB2_INVALID_ARG, "weight_dtype must be 'fp32' or 'bf16'")
         self.config = config
         L = N.load()
         shapes = param_shapes(config)
@@ -127,7 +130,7 @@ class B200Backend:
                 raise ArgumentError(N.FB2_INVALID_ARG, f"parameter of shape {a.shape} does not match {s}")
             self._params.append(a)
         desc = N.ModelDesc(config.vocab_size, config.context_length, config.d_model, config.n_layers,
-                           config.n_heads, N.FB2_WEIGHTS_FP32)
+                           config.n_heads, N.FB2_WEIGHTS_BF16 if weight_dtype == "bf16" else N.FB2_WEIGHTS_FP32)
         ptrs = (C.c_void_p * len(self._params))(*[a.ctypes.data for a in self._params])
         devs = _i32(list(devices) if devices is not None else [0])
         self._model = C.c_void_p()

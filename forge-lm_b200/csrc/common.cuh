@@ -50,6 +50,28 @@ FB2_DEV float ld_cg(const float* p) { return __ldcg(p); }
 FB2_DEV float4 ld_cg4(const float4* p) { return __ldcg(p); }
 
 // Streaming read-only weight load: do not keep in L1.
+FB2_DEV uint2 ld_stream_u2(const uint2* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+FB2_DEV float4 ld_stream4(const float4* p);
+// Weight element types of the HBM-bound decode kernels: WF32 reads fp32
+// weights, WBF16 reads bf16 weights (4 per 8-byte load) and widens them
+// exactly to fp32.  load4(base, i) = elements 4i .. 4i+3.
+struct WF32 {
+    using T = float;
+    static FB2_DEV float4 load4(const T* base, size_t i) { return ld_stream4(reinterpret_cast<const float4*>(base) + i); }
+};
+struct WBF16 {
+    using T = unsigned short;  // bf16 bits
+    static FB2_DEV float4 load4(const T* base, size_t i) {
+        const uint2 u = ld_stream_u2(reinterpret_cast<const uint2*>(base) + i);
+        return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                           __uint_as_float(u.y & 0xFFFF0000u));
+    }
+};
+
 FB2_DEV float4 ld_stream4(const float4* p) {
     float4 v;
     asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"

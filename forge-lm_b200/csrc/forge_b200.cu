@@ -13,6 +13,7 @@
 
 #include <algorithm>
 #include <array>
+#include <unordered_map>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
@@ -129,6 +130,12 @@ struct DeviceModel {
     // (qkv, proj, fc, mlp proj) and their TMA descriptors
     bool tc_ok = false;
     float* tc_blob = nullptr;
+    // FB2_WEIGHTS_BF16: the projections and tok_emb are rounded to bf16 in
+    // `blob` (every path computes with the same values) and the HBM-bound
+    // decode kernels read bf16 copies: fp32 tensor -> its bf16 bits
+    bool bf16 = false;
+    unsigned short* blob16 = nullptr;
+    std::unordered_map<const float*, const unsigned short*> w16;
     std::vector<std::array<CUtensorMap, 8>> tc_maps;  // per layer: {hi, lo} x 4 matrices (W^T, 128-row boxes)
 };
 
@@ -170,6 +177,11 @@ static void configure_kernels(int dev) {
     setmax((const void*)k_gemv<4>, 227 * 1024);
     setmax((const void*)k_gemv<8>, 227 * 1024);
     setmax((const void*)k_gemv<16>, 227 * 1024);
+    setmax((const void*)k_gemv<1, WBF16>, 227 * 1024);
+    setmax((const void*)k_gemv<2, WBF16>, 227 * 1024);
+    setmax((const void*)k_gemv<4, WBF16>, 227 * 1024);
+    setmax((const void*)k_gemv<8, WBF16>, 227 * 1024);
+    setmax((const void*)k_gemv<16, WBF16>, 227 * 1024);
     setmax((const void*)k_attn_prefill<4>, 227 * 1024);
     setmax((const void*)k_attn_prefill<8>, 227 * 1024);
     setmax((const void*)k_attn_prefill<16>, 227 * 1024);
@@ -184,6 +196,11 @@ static void configure_kernels(int dev) {
     setmax((const void*)k_head<4>, 227 * 1024);
     setmax((const void*)k_head<8>, 227 * 1024);
     setmax((const void*)k_head<16>, 227 * 1024);
+    setmax((const void*)k_head<1, WBF16>, 227 * 1024);
+    setmax((const void*)k_head<2, WBF16>, 227 * 1024);
+    setmax((const void*)k_head<4, WBF16>, 227 * 1024);
+    setmax((const void*)k_head<8, WBF16>, 227 * 1024);
+    setmax((const void*)k_head<16, WBF16>, 227 * 1024);
     setmax((const void*)k_sample_step, 227 * 1024);
     setmax((const void*)k_gemm_tc<128>, 227 * 1024);
     setmax((const void*)k_gemm_tc_swab<64>, 227 * 1024);
@@ -224,6 +241,22 @@ static int mk_nstage(const fb2_model& m, int MR, int nW, int device) {
     int ns = 16;
     while (ns >= 4 && (long long)mk_smem(m, MR, nW, ns) > avail) ns--;
     return ns >= 4 ? ns : 0;
+}
+
+// ---- bf16 weights ---------------------------------------------------------------
+// Round to the nearest bf16 value (ties to even), kept as fp32.
+static float bf16_round_host(float x) {
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+    float r;
+    std::memcpy(&r, &u, 4);
+    return r;
+}
+// bf16 bits of values that are already bf16-representable fp32.
+__global__ void k_to_bf16_bits(const float* __restrict__ x, long long n, unsigned short* __restrict__ y) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        y[i] = (unsigned short)(__float_as_uint(x[i]) >> 16);
 }
 
 // ---- tensor-core GEMM support ----------------------------------------------
@@ -520,7 +553,13 @@ static void launch_gemv_mr(DeviceSession& s, int M, int K, int N, const float* A
     size_t need = (size_t)S * M * N;
     if (S > 1 && need > s.gemv_part_cap) fail(FB2_UNSUPPORTED, "split-K scratch too small");
     size_t smem = (size_t)MR * kchunk * 4 + (size_t)16 * MR * 64 * 4;
-    s.stats.kernel_launches++; k_gemv<MR><<<dim3(nblk, S), 256, smem, s.stream>>>(M, K, N, kchunk, A, W, s.d_gemv_part, s.d_tickets, e);
+    s.stats.kernel_launches++;
+    auto it = s.dm->w16.find(W);
+    if (it != s.dm->w16.end())
+        k_gemv<MR, WBF16><<<dim3(nblk, S), 256, smem, s.stream>>>(M, K, N, kchunk, A, it->second, s.d_gemv_part,
+                                                                  s.d_tickets, e);
+    else
+        k_gemv<MR><<<dim3(nblk, S), 256, smem, s.stream>>>(M, K, N, kchunk, A, W, s.d_gemv_part, s.d_tickets, e);
 }
 
 // y = A * W (+ epilogue) for M rows.
@@ -570,7 +609,8 @@ static bool launch_gemm_tc(cudaStream_t st, int sm_count, int M, int K, int N, c
 // selects the tensor-core GEMM when it applies.
 static void launch_linear(DeviceSession& s, int M, int K, int N, const float* A, const float* W, Epi e,
                           const CUtensorMap* bmaps) {
-    if (bmaps && s.d_ahi &&
+    // bf16 weights: decode batches stay on the bf16 gemv (half the bytes)
+    if (bmaps && s.d_ahi && !(s.dm->bf16 && M < kTcMinRows) &&
         launch_gemm_tc(s.stream, s.dm->sm_count, M, K, N, A, s.d_ahi, s.d_alo, bmaps, e, s.d_tc_err, s.d_tc_part,
                        s.tc_part_cap, &s.stats.kernel_launches))
         return;
@@ -687,7 +727,11 @@ static void launch_head(DeviceSession& s, int M, const float* xln, const int* ou
 #define HEAD_CASE(R)                                                                               \
     if (mm <= R) {                                                                                 \
         smem = (size_t)R * m.D * 4;                                                                \
-        s.stats.kernel_launches++; k_head<R><<<blocks, 256, smem, s.stream>>>(mm, m.D, m.V, x, s.dm->tok_emb, out, m.V);      \
+        s.stats.kernel_launches++;                                                                 \
+        if (s.dm->bf16)                                                                            \
+            k_head<R, WBF16><<<blocks, 256, smem, s.stream>>>(mm, m.D, m.V, x, s.dm->w16.at(s.dm->tok_emb), out, m.V); \
+        else                                                                                       \
+            k_head<R><<<blocks, 256, smem, s.stream>>>(mm, m.D, m.V, x, s.dm->tok_emb, out, m.V);  \
         continue;                                                                                  \
     }
         HEAD_CASE(1) HEAD_CASE(2) HEAD_CASE(4) HEAD_CASE(8) HEAD_CASE(16)
@@ -1388,7 +1432,8 @@ int32_t fb2_model_create(const fb2_model_desc* desc, const float* const* params,
         if (d.d_model % 4 != 0 || d.d_model > 2048) fail(FB2_UNSUPPORTED, "d_model must be a multiple of 4, <= 2048");
         if (sampler_smem_bytes(d.vocab_size) > 227 * 1024)
             fail(FB2_UNSUPPORTED, "vocabulary too large for the on-chip sampler");
-        if (d.weight_dtype != FB2_WEIGHTS_FP32) fail(FB2_UNSUPPORTED, "only fp32 weights in this build");
+        if (d.weight_dtype != FB2_WEIGHTS_FP32 && d.weight_dtype != FB2_WEIGHTS_BF16)
+            fail(FB2_INVALID_ARG, "weight_dtype must be FB2_WEIGHTS_FP32 or FB2_WEIGHTS_BF16");
         if (n_params != 4 + 12 * d.n_layers) fail(FB2_INVALID_ARG, "n_params must be 4 + 12*n_layers");
         for (int i = 0; i < n_params; i++)
             if (!params[i]) fail(FB2_INVALID_ARG, "parameter pointer is NULL");
@@ -1406,6 +1451,22 @@ int32_t fb2_model_create(const fb2_model_desc* desc, const float* const* params,
             m->V = d.vocab_size; m->ctx = d.context_length; m->D = d.d_model; m->L = d.n_layers;
             m->H = d.n_heads; m->hd = hd; m->F = 4 * d.d_model;
             std::vector<long long> numel = param_numels(d);
+            // bf16 weights: tok_emb and the four projections of every layer,
+            // rounded to nearest-even bf16 on the host before upload
+            const bool bf16 = d.weight_dtype == FB2_WEIGHTS_BF16;
+            std::vector<int> narrow_idx;
+            if (bf16) {
+                narrow_idx.push_back(0);
+                for (int l = 0; l < d.n_layers; l++)
+                    for (int j : {2, 4, 8, 10}) narrow_idx.push_back(2 + 12 * l + j);
+            }
+            std::vector<std::vector<float>> rounded(n_params);
+            std::vector<const float*> up(params, params + n_params);
+            for (int i : narrow_idx) {
+                rounded[i].resize((size_t)numel[i]);
+                for (long long k = 0; k < numel[i]; k++) rounded[i][k] = bf16_round_host(params[i][k]);
+                up[i] = rounded[i].data();
+            }
             std::vector<size_t> offs;
             size_t total = 0;
             for (long long k : numel) {
@@ -1426,8 +1487,23 @@ int32_t fb2_model_create(const fb2_model_desc* desc, const float* const* params,
                 m->devs.push_back(dm);
                 DeviceModel& D = m->devs.back();
                 for (int i = 0; i < n_params; i++) {
-                    CK(cudaMemcpy(D.blob + offs[i], params[i], (size_t)numel[i] * 4, cudaMemcpyHostToDevice));
+                    CK(cudaMemcpy(D.blob + offs[i], up[i], (size_t)numel[i] * 4, cudaMemcpyHostToDevice));
                     D.p.push_back(D.blob + offs[i]);
+                }
+                if (bf16) {
+                    D.bf16 = true;
+                    size_t n16 = 0;
+                    for (int i : narrow_idx) n16 += ((size_t)numel[i] + 127) / 128 * 128;
+                    D.blob16 = dalloc<unsigned short>(n16);
+                    size_t at = 0;
+                    for (int i : narrow_idx) {
+                        k_to_bf16_bits<<<(int)std::min<long long>(4096, (numel[i] + 255) / 256), 256>>>(D.p[i], numel[i],
+                                                                                                  D.blob16 + at);
+                        D.w16[D.p[i]] = D.blob16 + at;
+                        at += ((size_t)numel[i] + 127) / 128 * 128;
+                    }
+                    CK(cudaGetLastError());
+                    CK(cudaDeviceSynchronize());
                 }
                 D.tok_emb = D.p[0];
                 D.pos_emb = D.p[1];
@@ -1437,7 +1513,7 @@ int32_t fb2_model_create(const fb2_model_desc* desc, const float* const* params,
                 }
                 D.lnf_w = D.p[2 + 12 * d.n_layers];
                 D.lnf_b = D.p[3 + 12 * d.n_layers];
-                mk_setup(*m, D, params);
+                mk_setup(*m, D, up.data());
                 tc_setup(*m, D);
             }
         } catch (...) {
@@ -1447,6 +1523,7 @@ int32_t fb2_model_create(const fb2_model_desc* desc, const float* const* params,
                 dfree(dm.relaid);
                 dfree(dm.d_mk_layers);
                 dfree(dm.tc_blob);
+                dfree(dm.blob16);
             }
             delete m;
             throw;
@@ -1463,6 +1540,7 @@ void fb2_model_destroy(fb2_model* m) {
         dfree(dm.relaid);
         dfree(dm.d_mk_layers);
         dfree(dm.tc_blob);
+        dfree(dm.blob16);
     }
     delete m;
 }

@@ -179,9 +179,9 @@ FB2_DEV void epi_store4(const Epi& e, int m, int n, int N, float4 a) {
 // CTA of a column block (atomic ticket) sums the S partials in split order,
 // so the result is deterministic.
 // ---------------------------------------------------------------------------
-template <int MR>
+template <int MR, class WL = WF32>
 __global__ void __launch_bounds__(256) k_gemv(int M, int K, int N, int kchunk, const float* __restrict__ A,
-                                              const float* __restrict__ W, float* __restrict__ partial,
+                                              const typename WL::T* __restrict__ W, float* __restrict__ partial,
                                               unsigned int* __restrict__ tickets, Epi e) {
     extern __shared__ float smem[];
     float* As = smem;                     // [MR][kchunk]
@@ -203,15 +203,15 @@ __global__ void __launch_bounds__(256) k_gemv(int M, int K, int N, int kchunk, c
     for (int m = 0; m < MR; m++) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
     const int col = col0 + cq * 4;
     const bool col_ok = col < N;
-    const float4* Wp = reinterpret_cast<const float4*>(W + (size_t)k0 * N + col);
-    const size_t wstride = (size_t)N / 4 * 16;  // 16 k rows, in float4 units
+    const size_t w4 = ((size_t)k0 * N + col) / 4;  // this thread's first weight quad
+    const size_t n4 = (size_t)N / 4;               // quads per k row
     int kk = kl;
     constexpr int U = 4;
     for (; kk + 16 * (U - 1) < kn; kk += 16 * U) {
         float4 w[U];
 #pragma unroll
         for (int u = 0; u < U; u++)
-            w[u] = col_ok ? ld_stream4(Wp + (size_t)(kk + 16 * u) * (N / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            w[u] = col_ok ? WL::load4(W, w4 + (size_t)(kk + 16 * u) * n4) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int u = 0; u < U; u++) {
 #pragma unroll
@@ -224,9 +224,8 @@ __global__ void __launch_bounds__(256) k_gemv(int M, int K, int N, int kchunk, c
             }
         }
     }
-    (void)wstride;
     for (; kk < kn; kk += 16) {
-        float4 w = col_ok ? ld_stream4(Wp + (size_t)kk * (N / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 w = col_ok ? WL::load4(W, w4 + (size_t)kk * n4) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int m = 0; m < MR; m++) {
             float a = As[m * kchunk + kk];
@@ -696,9 +695,9 @@ __global__ void __launch_bounds__(256) k_attn_prefill_rt(const float* __restrict
 // last row only): logits[m][v] = dot(xln[m], tok_emb[v]).  One warp per
 // vocab row, MR rows at a time, xln staged in shared memory.
 // ---------------------------------------------------------------------------
-template <int MR>
+template <int MR, class WL = WF32>
 __global__ void __launch_bounds__(256) k_head(int M, int D, int V, const float* __restrict__ xln,
-                                              const float* __restrict__ E, float* __restrict__ logits,
+                                              const typename WL::T* __restrict__ E, float* __restrict__ logits,
                                               int logits_stride) {
     extern __shared__ float xs[];  // [MR][D]
     for (int i = threadIdx.x; i < MR * D; i += blockDim.x) {
@@ -709,12 +708,12 @@ __global__ void __launch_bounds__(256) k_head(int M, int D, int V, const float* 
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     for (int v = blockIdx.x * warps + (threadIdx.x >> 5); v < V; v += gridDim.x * warps) {
-        const float4* er = reinterpret_cast<const float4*>(E + (size_t)v * D);
+        const size_t e4 = (size_t)v * D / 4;
         float acc[MR];
 #pragma unroll
         for (int m = 0; m < MR; m++) acc[m] = 0.f;
         for (int i = lane; i < D / 4; i += 32) {
-            float4 w = ld_stream4(er + i);
+            float4 w = WL::load4(E, e4 + i);
 #pragma unroll
             for (int m = 0; m < MR; m++) {
                 float4 x = *reinterpret_cast<const float4*>(&xs[m * D + i * 4]);

@@ -49,6 +49,12 @@ typedef enum {
     FB2_NO_DEVICE = -6
 } fb2_status;
 
+/* FB2_WEIGHTS_BF16: the caller still passes fp32 arrays; the library rounds
+ * tok_emb and the four projection matrices of every layer to the nearest
+ * bf16 (ties to even) and computes with those values (fp32 accumulation,
+ * fp32 LayerNorm, softmax, biases and position table).  The HBM-bound decode
+ * kernels read 2-byte weights.  No reference counterpart: the reference
+ * stores fp32 (Parameters, GptModel.cs:14-18). */
 typedef enum { FB2_WEIGHTS_FP32 = 0, FB2_WEIGHTS_BF16 = 1 } fb2_weight_dtype;
 
 /* ModelConfig (src/LLM.Core/Model/ModelConfig.cs:8-26): MlpHidden = 4*d_model,

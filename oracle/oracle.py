@@ -154,6 +154,21 @@ def init_params(cfg: Config, seed: int) -> list[np.ndarray]:
     return params
 
 
+def round_bf16(cfg: Config, params) -> list[np.ndarray]:
+    """The weights a FB2_WEIGHTS_BF16 model computes with: tok_emb and each
+    layer's attn.qkv.w, attn.proj.w, mlp.fc.w, mlp.proj.w rounded to the
+    nearest bf16 (ties to even); everything else unchanged.  (The reference
+    keeps fp32; this is the oracle of the library's bf16 option.)"""
+    out = [np.array(p, np.float32, copy=True) for p in params]
+    idx = [0] + [2 + 12 * layer + j for layer in range(cfg.n_layers) for j in (2, 4, 8, 10)]
+    for i in idx:
+        u = out[i].view(np.uint32)
+        finite = (u & np.uint32(0x7F800000)) != np.uint32(0x7F800000)
+        r = (u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)
+        u[finite] = r[finite]
+    return out
+
+
 def _ptrs(params):
     for p in params:
         assert p.dtype == np.float32 and p.flags.c_contiguous

@@ -249,6 +249,42 @@ def test_full_context_prompts_reprefill_every_step(pkg, O):
         check_ids(O, ocfg, params, p, got[i], want)
 
 
+def test_bf16_weights(pkg, O, monkeypatch):
+    """FB2_WEIGHTS_BF16 (the Forge-98M bf16 config): the
+    library computes with tok_emb and the projections rounded to bf16.  Against
+    the oracle run on the same rounded weights the fp32 bar holds (logits
+    1e-3, ids exact or near-tie) on every path -- persistent kernel and graph
+    step, the bf16 gemv and head, prefill; against the fp32 model the stated
+    C5 tolerance is logits max-rel <= 2e-2."""
+    shape = (16384, 160, 128, 2, 2)
+    ocfg = O.Config(*shape)
+    params = O.init_params(ocfg, 41)
+    rparams = O.round_bf16(ocfg, params)
+    rng = np.random.default_rng(17)
+    toks = rng.integers(0, shape[0], (2, 60)).astype(np.int32)
+    prompts = [rng.integers(0, shape[0], L).astype(np.int32) for L in (20, 33, 47)]
+    for mode in ("persistent", "graph"):
+        if mode == "graph":
+            monkeypatch.setenv("FORGE_B200_DECODE", "graph")
+        be = pkg.B200Backend(pkg.ModelConfig(*shape), params, devices=[0], max_seqs=3, weight_dtype="bf16")
+        with be:
+            tf = be.teacher_forced_logits(toks, 40)
+            got1 = be.generate(prompts[0].tolist(), 40, 0.7, 30, pkg.DotNetRandom(3), repetition_penalty=1.1,
+                               no_repeat_ngram_size=4)
+            gotb = be.generate_batch([p.tolist() for p in prompts], 24, 0.0, 0)
+        for s_ in range(2):
+            for k in (0, 9, 20):
+                want = O.forward_last(ocfg, rparams, toks[s_, :40 + k])
+                assert relerr(tf[s_, k], want) <= TOL, (mode, s_, k)
+                full = O.forward_last(ocfg, params, toks[s_, :40 + k])
+                assert relerr(tf[s_, k], full) <= 2e-2, (mode, s_, k)
+        want1 = O.generate(ocfg, rparams, prompts[0], 40, 0.7, 30, O.DotNetRandom(3), repetition_penalty=1.1,
+                           no_repeat_ngram=4)
+        check_ids(O, ocfg, rparams, prompts[0], got1, want1)
+        for i, p in enumerate(prompts):
+            check_ids(O, ocfg, rparams, p, gotb[i], O.generate(ocfg, rparams, p, 24, 0.0, 0, O.DotNetRandom(1)))
+
+
 def test_generate_batch_ragged_and_long_prompts(pkg, O):
     shape = (300, 24, 32, 2, 2)
     ocfg, params, be = make(pkg, O, shape, 9, max_seqs=5)

@@ -176,3 +176,22 @@ def test_dotnet_random_restatements_agree(O, pkg):
         N.check(N.load().fb2_test_dotnet_random(seed, 200, C.c_void_p(c.ctypes.data)))
         assert np.array_equal(a, b) and np.array_equal(a, c), seed
         assert np.all((a >= 0) & (a < 1))
+
+
+def test_round_bf16_ties_to_even_and_scope(O):
+    """round_bf16: nearest-even bf16 of the projections and tok_emb only."""
+    cfg = O.Config(12, 6, 8, 1, 2)
+    params = O.init_params(cfg, 3)
+    r = O.round_bf16(cfg, params)
+    bits = [np.float32(1.0 + 2.0 ** -8), np.float32(1.0 + 3 * 2.0 ** -8), np.float32(-2.5 + 2.0 ** -9)]
+    want = [np.float32(1.0), np.float32(1.0 + 2 * 2.0 ** -7), np.float32(-2.5)]
+    p = [np.array(b, np.float32).reshape(1) for b in bits]
+    for b, w in zip(p, want):
+        q = O.round_bf16(O.Config(1, 1, 4, 1, 1), [b] + [np.zeros(1, np.float32)] * 15)[0]
+        assert q[0] == w
+    for i, (a, b) in enumerate(zip(params, r)):
+        narrowed = i == 0 or (i >= 2 and (i - 2) % 12 in (2, 4, 8, 10) and i < 2 + 12 * cfg.n_layers)
+        if narrowed:
+            assert np.all((b.view(np.uint32) & 0xFFFF) == 0) and np.max(np.abs(a - b)) <= np.max(np.abs(a)) * 2 ** -8
+        else:
+            assert np.array_equal(a, b)
