@@ -12,6 +12,10 @@ Workloads (synthetic seeded weights and prompts):
       the window, so every step re-prefills all 1024 positions (tensor-core
       bound).  One bench step = 16 new tokens of the 512 the workload names
       (a bounded sample; each token costs the same full re-prefill).
+  c5: Forge-98M with bf16 weights (FB2_WEIGHTS_BF16), 32 sequences per GPU
+      (256 on 8 GPUs), prompt lengths uniform in [64, 960], greedy decode
+      (the workload decodes every sequence to the 1024-token context; one
+      bench step = 64 new tokens of that, a bounded sample).  KV-bound.
 Metric: decode tokens/s, whole job (sum over GPUs), max over ranks of the
 device time.  N>1: one process per GPU, independent sequences, no data-path
 collective (weak scaling for c2, strong for c3).
@@ -50,6 +54,10 @@ WORKLOADS = {
     "c3": dict(name="Forge-98M fp32 bs64: prompts 256, 768 greedy tokens, sequences split over GPUs",
                model=FORGE_98M, seqs_total=64, seqs_per_gpu=None, prompt_len=256, new_tokens=768,
                temperature=0.0, top_k=0, penalty=1.0, ngram=0, scaling="strong"),
+    "c5": dict(name="Forge-98M bf16 weights, 32 sequences per GPU, prompts U[64, 960], greedy; 64 new tokens per "
+                    "bench step of the decode to the 1024-token context",
+               model=FORGE_98M, seqs_total=None, seqs_per_gpu=32, prompt_len=(64, 960), new_tokens=64,
+               temperature=0.0, top_k=0, penalty=1.0, ngram=0, scaling="weak", weight_dtype="bf16"),
     "c4": dict(name="forge-220m fp32 bs16: prompts 1024 (full context), sampled T 0.7 top-k 30; every token "
                     "re-prefills the 1024-token window; 16 of the 512 tokens per bench step",
                model=FORGE_220M, seqs_total=16, seqs_per_gpu=None, prompt_len=1024, new_tokens=16,
@@ -99,16 +107,24 @@ def shard(total: int, world: int, rank: int) -> tuple[int, int]:
     return first, per + (1 if rank < extra else 0)
 
 
-def prompts_for(first: int, count: int, plen: int, vocab: int) -> list[np.ndarray]:
-    """Uniform-random prompt ids, seed 42 + global sequence index."""
-    return [np.random.default_rng(42 + first + i).integers(0, vocab, plen).astype(np.int32) for i in range(count)]
+def prompts_for(first: int, count: int, plen, vocab: int) -> list[np.ndarray]:
+    """Uniform-random prompt ids, seed 42 + global sequence index; `plen` is a
+    length or a (lo, hi) range drawn per sequence from the same seed."""
+    out = []
+    for i in range(count):
+        g = np.random.default_rng(42 + first + i)
+        n = plen if isinstance(plen, int) else int(g.integers(plen[0], plen[1] + 1))
+        out.append(g.integers(0, vocab, n).astype(np.int32))
+    return out
 
 
-def weight_bytes(m: dict) -> float:
+def weight_bytes(m: dict, dtype: str = "fp32") -> float:
     """Bytes of every parameter one decode step streams once (shared by all
-    sequences of the step): block weights and biases, ln_f, the tied head."""
+    sequences of the step): block weights and biases, ln_f, the tied head.
+    bf16 narrows the projections and the head to 2 bytes."""
     D, L, V = m["d_model"], m["n_layers"], m["vocab_size"]
-    return 4.0 * (L * (12 * D * D + 13 * D) + 2 * D + V * D)
+    wide = 2.0 if dtype == "bf16" else 4.0
+    return wide * (L * 12 * D * D + V * D) + 4.0 * (L * 13 * D + 2 * D)
 
 
 def sequence_bytes(m: dict, T: int) -> float:
@@ -180,6 +196,8 @@ def cpu_reference_sample(wl: dict, seconds_target: float = 15.0, max_tokens: int
     m = wl["model"]
     cfg = O.Config(m["vocab_size"], m["context_length"], m["d_model"], m["n_layers"], m["n_heads"])
     params = O.init_params(cfg, WEIGHT_SEED)
+    if wl.get("weight_dtype") == "bf16":
+        params = O.round_bf16(cfg, params)
     prompt = prompts_for(0, 1, wl["prompt_len"], m["vocab_size"])[0]
     # calibrate: one token, then as many as fit the target time
     t0 = time.perf_counter()
@@ -194,9 +212,9 @@ def cpu_reference_sample(wl: dict, seconds_target: float = 15.0, max_tokens: int
                      repetition_penalty=wl["penalty"], no_repeat_ngram=wl["ngram"])
     dt = time.perf_counter() - t0
     return {"value": len(out) / dt, "unit": "tokens/s", "cores": O.get_threads(), "kind": "port",
-            "sample": f"first {len(out)} of {wl['new_tokens']} tokens of sequence 0 (prompt {wl['prompt_len']}), "
+            "sample": f"first {len(out)} of {wl['new_tokens']} tokens of sequence 0 (prompt {len(prompt)}), "
                       f"full re-forward per token as the reference CPU backend does"
-                      + ("" if wl["prompt_len"] >= m["context_length"] else
+                      + ("" if len(prompt) >= m["context_length"] else
                          "; later tokens cost more (window grows), so this over-states the full-run rate"),
             "seconds": dt}
 
@@ -250,7 +268,8 @@ def main():
     else:
         first, count = rank * wl["seqs_per_gpu"], wl["seqs_per_gpu"]
     params = pkg.init_params(cfg, WEIGHT_SEED)
-    be = pkg.B200Backend(cfg, params, devices=[local], max_seqs=max(count, 1))
+    wdt = wl.get("weight_dtype", "fp32")
+    be = pkg.B200Backend(cfg, params, devices=[local], max_seqs=max(count, 1), weight_dtype=wdt)
     del params
     # a real (non-legacy) stream: its handle is what the library launches on,
     # and the CUDA events below are recorded on the same stream
@@ -260,17 +279,18 @@ def main():
     be.set_stream(stream.cuda_stream)
     plen, new = wl["prompt_len"], wl["new_tokens"]
     prompts = prompts_for(first, count, plen, m["vocab_size"])
+    lens = [len(p) for p in prompts]
     seeds = [1 + first + i for i in range(count)]
     dev = torch.device("cuda", local)
     d_prompts = torch.from_numpy(np.concatenate(prompts)).to(dev)
-    d_lens = torch.full((count,), plen, dtype=torch.int32, device=dev)
+    d_lens = torch.tensor(lens, dtype=torch.int32, device=dev)
     d_out = torch.zeros((count, new), dtype=torch.int32, device=dev)
     d_cnt = torch.zeros((count,), dtype=torch.int32, device=dev)
     gen_kw = dict(max_new_tokens=new, temperature=wl["temperature"], top_k=wl["top_k"],
                   repetition_penalty=wl["penalty"], no_repeat_ngram_size=wl["ngram"])
 
     def step_device():
-        be.generate_device(d_prompts.data_ptr(), d_lens.data_ptr(), [plen] * count, out_tokens_ptr=d_out.data_ptr(),
+        be.generate_device(d_prompts.data_ptr(), d_lens.data_ptr(), lens, out_tokens_ptr=d_out.data_ptr(),
                            out_counts_ptr=d_cnt.data_ptr(), seeds=seeds, **gen_kw)
 
     def step_host():
@@ -330,12 +350,12 @@ def main():
     be.reset_stats()
     t_long = timed(step_device)
     persistent = be.stats()["persistent_steps"] > 0
-    t_short = timed(lambda: be.generate_device(d_prompts.data_ptr(), d_lens.data_ptr(), [plen] * count,
+    t_short = timed(lambda: be.generate_device(d_prompts.data_ptr(), d_lens.data_ptr(), lens,
                                                out_tokens_ptr=d_out.data_ptr(), out_counts_ptr=d_cnt.data_ptr(),
                                                seeds=seeds, **short_kw))
     step_ms = (t_long - t_short) / max(new - 1, 1)
-    Ts = [plen + n for n in range(1, new)]
-    bytes_step = weight_bytes(m) + count * float(np.mean([sequence_bytes(m, min(T, m["context_length"])) for T in Ts]))
+    bytes_step = weight_bytes(m, wdt) + float(np.mean(
+        [sum(sequence_bytes(m, min(L0 + n, m["context_length"])) for L0 in lens) for n in range(1, new)]))
     achieved_gbs = bytes_step / (step_ms / 1000.0) / 1e9
     peaks = {}
     try:
@@ -385,7 +405,7 @@ def main():
         dist.all_reduce(t)
         e2e_tokens = int(t.item())
     e2e = {"value": e2e_tokens / (e2e_ms / 1000.0), "unit": "tokens/s",
-           "h2d_bytes_per_step": int(count * plen * 4 + count * 4), "d2h_bytes_per_step": int(count * new * 4 + count * 4)}
+           "h2d_bytes_per_step": int(sum(lens) * 4 + count * 4), "d2h_bytes_per_step": int(count * new * 4 + count * 4)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -402,9 +422,10 @@ def main():
             "higher_is_better": True, "scaling": wl["scaling"], "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init weights, uniform-random prompt ids)",
             "config": {"workload": wl["name"], "model": model_name(m),
-                       "sequences_per_gpu": count, "prompt_len": plen, "new_tokens": new,
+                       "sequences_per_gpu": count, "prompt_len": plen if isinstance(plen, int) else list(plen),
+                       "new_tokens": new, "weights": wdt,
                        "parallelism": f"request-parallel x{world} (independent sequences, no collective)",
-                       "l2": f"inputs larger than L2: every decode step streams {weight_bytes(m) / 1e6:.0f} MB "
+                       "l2": f"inputs larger than L2: every decode step streams {weight_bytes(m, wdt) / 1e6:.0f} MB "
                              f"of weights"},
             "roofline": roofline,
             "cpu_baseline": cpu,
