@@ -22,11 +22,12 @@ from typing import Callable, Iterable, Sequence
 import numpy as np
 
 from . import _native as N
-from ._native import ArgumentError, NativeError
+from ._native import ArgumentError, InvalidDataError, NativeError
 from .dotnet_random import DotNetRandom
 
 __all__ = ["ModelConfig", "B200Backend", "Sampler", "DotNetRandom", "ArgumentError", "NativeError",
-           "param_names", "param_shapes", "init_params", "device_count", "library_path"]
+           "InvalidDataError", "param_names", "param_shapes", "init_params", "device_count", "library_path",
+           "read_forgemodel_header", "write_forgemodel"]
 
 
 def library_path() -> str:
@@ -99,6 +100,40 @@ def _i32(a) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=np.int32)
 
 
+def _dtype_code(weight_dtype: str) -> int:
+    if weight_dtype not in ("fp32", "bf16"):
+        raise ArgumentError(N.FB2_INVALID_ARG, "weight_dtype must be 'fp32' or 'bf16'")
+    return N.FB2_WEIGHTS_BF16 if weight_dtype == "bf16" else N.FB2_WEIGHTS_FP32
+
+
+def read_forgemodel_header(path: str) -> tuple[ModelConfig, str]:
+    """Validate a FORGEMODEL1 checkpoint (every rule of Checkpoint.LoadCore,
+    Checkpoint.cs:174-264, checksum included) and return its configuration
+    and ModelName.  No device needed."""
+    desc = N.ModelDesc()
+    name = C.create_string_buffer(4096)
+    N.check(N.load().fb2_forgemodel_read_header(str(path).encode(), C.byref(desc), name, len(name)))
+    return (ModelConfig(desc.vocab_size, desc.context_length, desc.d_model, desc.n_layers, desc.n_heads),
+            name.value.decode("utf-8"))
+
+
+def write_forgemodel(path: str, cfg: ModelConfig, params: Sequence[np.ndarray], model_name: str) -> None:
+    """Write a FORGEMODEL1 model checkpoint (Checkpoint.SaveTraining's layout,
+    Checkpoint.cs:63-119, 143-166, with no optimizer state)."""
+    shapes = param_shapes(cfg)
+    if len(params) != len(shapes):
+        raise ArgumentError(N.FB2_INVALID_ARG, f"expected {len(shapes)} parameter tensors, got {len(params)}")
+    arrs = [np.ascontiguousarray(p, dtype=np.float32) for p in params]
+    for a, s in zip(arrs, shapes):
+        if a.size != int(np.prod(s)):
+            raise ArgumentError(N.FB2_INVALID_ARG, f"parameter of shape {a.shape} does not match {s}")
+    desc = N.ModelDesc(cfg.vocab_size, cfg.context_length, cfg.d_model, cfg.n_layers, cfg.n_heads,
+                       N.FB2_WEIGHTS_FP32)
+    ptrs = (C.c_void_p * len(arrs))(*[a.ctypes.data for a in arrs])
+    N.check(N.load().fb2_forgemodel_write(str(path).encode(), C.byref(desc), model_name.encode("utf-8"), ptrs,
+                                          len(arrs)))
+
+
 def _ptr(a: np.ndarray):
     return C.c_void_p(a.ctypes.data) if a is not None and a.size else None
 
@@ -130,13 +165,36 @@ class B200Backend:
                 raise ArgumentError(N.FB2_INVALID_ARG, f"parameter of shape {a.shape} does not match {s}")
             self._params.append(a)
         desc = N.ModelDesc(config.vocab_size, config.context_length, config.d_model, config.n_layers,
-                           config.n_heads, N.FB2_WEIGHTS_BF16 if weight_dtype == "bf16" else N.FB2_WEIGHTS_FP32)
+                           config.n_heads, _dtype_code(weight_dtype))
         ptrs = (C.c_void_p * len(self._params))(*[a.ctypes.data for a in self._params])
         devs = _i32(list(devices) if devices is not None else [0])
         self._model = C.c_void_p()
         N.check(L.fb2_model_create(C.byref(desc), ptrs, len(self._params), _ptr(devs), len(devs),
                                    C.byref(self._model)))
         self._params = None  # the device copies are authoritative now
+        self._open_session(devs, max_seqs)
+
+    @classmethod
+    def from_forgemodel(cls, path: str, devices: Iterable[int] | None = None, max_seqs: int = 1,
+                        weight_dtype: str = "fp32") -> "B200Backend":
+        """Checkpoint.Load (src/LLM.Core/Checkpoint/Checkpoint.cs:121-122)
+        straight to the devices: the library validates the FORGEMODEL1 file
+        (header rules, registry names, payload size, SHA-256) and uploads it;
+        InvalidDataError where the reference throws InvalidDataException."""
+        self = cls.__new__(cls)
+        L = N.load()
+        devs = _i32(list(devices) if devices is not None else [0])
+        desc = N.ModelDesc()
+        self._model = C.c_void_p()
+        N.check(L.fb2_model_load_forgemodel(str(path).encode(), _dtype_code(weight_dtype), _ptr(devs), len(devs),
+                                            C.byref(desc), C.byref(self._model)))
+        self.config = ModelConfig(desc.vocab_size, desc.context_length, desc.d_model, desc.n_layers, desc.n_heads)
+        self._params = None
+        self._open_session(devs, max_seqs)
+        return self
+
+    def _open_session(self, devs: np.ndarray, max_seqs: int) -> None:
+        L = N.load()
         self.max_seqs = int(max_seqs)
         self._session = C.c_void_p()
         try:

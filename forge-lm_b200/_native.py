@@ -18,6 +18,7 @@ FB2_CUDA_ERROR = -3
 FB2_TIMEOUT = -4
 FB2_UNSUPPORTED = -5
 FB2_NO_DEVICE = -6
+FB2_INVALID_DATA = -7
 
 FB2_WEIGHTS_FP32 = 0
 FB2_WEIGHTS_BF16 = 1
@@ -32,9 +33,10 @@ EXPORTED = [
     "fb2_session_create", "fb2_session_destroy", "fb2_session_seed", "fb2_session_set_stream",
     "fb2_generate", "fb2_generate_device", "fb2_forward_last_logits", "fb2_teacher_forced_logits",
     "fb2_sample_logits", "fb2_forward_last_logits_noalloc", "fb2_init_params", "fb2_stats", "fb2_stats_reset",
+    "fb2_forgemodel_read_header", "fb2_model_load_forgemodel", "fb2_forgemodel_write",
 ]
 TEST_EXPORTED = ["fb2_test_expf", "fb2_test_expf_hash", "fb2_test_dotnet_random", "fb2_test_mk_trace",
-                 "fb2_test_gemm_tc"]
+                 "fb2_test_gemm_tc", "fb2_test_sha256"]
 
 
 class ModelDesc(C.Structure):
@@ -67,6 +69,11 @@ class NativeError(RuntimeError):
 
 class ArgumentError(ValueError, NativeError):
     """INVALID_ARG: the reference throws ArgumentException / ArgumentOutOfRangeException."""
+
+
+class InvalidDataError(NativeError):
+    """INVALID_DATA: a checkpoint the reference rejects with InvalidDataException
+    (Checkpoint.cs:174-264)."""
 
 
 def load(path: str | None = None):
@@ -104,6 +111,10 @@ def load(path: str | None = None):
     L.fb2_test_dotnet_random.argtypes = [i32, i32, vp]
     L.fb2_test_mk_trace.argtypes = [vp, vp, i64, C.POINTER(i32), C.POINTER(i32)]
     L.fb2_test_gemm_tc.argtypes = [i32, i32, i32, vp, vp, vp]
+    L.fb2_test_sha256.argtypes = [vp, i64, vp]
+    L.fb2_forgemodel_read_header.argtypes = [C.c_char_p, C.POINTER(ModelDesc), C.c_char_p, i32]
+    L.fb2_model_load_forgemodel.argtypes = [C.c_char_p, i32, i32p, i32, C.POINTER(ModelDesc), C.POINTER(vp)]
+    L.fb2_forgemodel_write.argtypes = [C.c_char_p, C.POINTER(ModelDesc), C.c_char_p, C.POINTER(vp), i32]
     for name in EXPORTED + TEST_EXPORTED:
         fn = getattr(L, name)
         if fn.restype is C.c_int:  # default
@@ -118,4 +129,6 @@ def check(status: int) -> None:
     msg = (load().fb2_last_error() or b"").decode(errors="replace")
     if status == FB2_INVALID_ARG:
         raise ArgumentError(status, msg)
+    if status == FB2_INVALID_DATA:
+        raise InvalidDataError(status, msg)
     raise NativeError(status, msg)

@@ -15,6 +15,7 @@
 #include <array>
 #include <unordered_map>
 #include <atomic>
+#include <cctype>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -30,6 +31,7 @@
 #include "sampler.cuh"
 #include "decode_mega.cuh"
 #include "gemm_tc.cuh"
+#include "forgemodel.hpp"
 
 #include <cudaTypedefs.h>
 
@@ -66,6 +68,9 @@ int32_t guarded(F&& f) {
     } catch (const Fb2Error& e) {
         g_last_error = e.msg;
         return e.status;
+    } catch (const fb2::fm::InvalidData& e) {
+        g_last_error = e.what();
+        return FB2_INVALID_DATA;
     } catch (const std::bad_alloc&) {
         g_last_error = "host out of memory";
         return FB2_OUT_OF_MEMORY;
@@ -2089,6 +2094,97 @@ int32_t fb2_forward_last_logits_noalloc(fb2_model* m, int32_t device_slot, int32
 // Copies the persistent kernel's per-phase %globaltimer stamps of its last
 // traced launch (FORGE_B200_MK_TRACE=<steps> at session creation) into out:
 // [CTAs][steps][64] uint64; *n_ctas / *n_steps receive the shape.
+// ---- FORGEMODEL1 ---------------------------------------------------------------
+static fb2_model_desc fm_desc(const fb2::fm::Header& h) {
+    fb2_model_desc d{};
+    d.vocab_size = h.vocab;
+    d.context_length = h.ctx;
+    d.d_model = h.d_model;
+    d.n_layers = h.n_layers;
+    d.n_heads = h.n_heads;
+    d.weight_dtype = FB2_WEIGHTS_FP32;
+    return d;
+}
+
+int32_t fb2_forgemodel_read_header(const char* path, fb2_model_desc* out_desc, char* name, int32_t name_capacity) {
+    return guarded([&] {
+        if (!path || !out_desc) fail(FB2_INVALID_ARG, "NULL argument");
+        const fb2::fm::File f = fb2::fm::read_file(path);
+        *out_desc = fm_desc(f.hdr);
+        if (name && name_capacity > 0) {
+            const size_t n = std::min(f.hdr.name.size(), (size_t)name_capacity - 1);
+            std::memcpy(name, f.hdr.name.data(), n);
+            name[n] = 0;
+        }
+    });
+}
+
+int32_t fb2_model_load_forgemodel(const char* path, int32_t weight_dtype, const int32_t* devices, int32_t n_devices,
+                                  fb2_model_desc* out_desc, fb2_model** out) {
+    return guarded([&] {
+        if (!path || !out) fail(FB2_INVALID_ARG, "NULL argument");
+        *out = nullptr;
+        fb2::fm::File f = fb2::fm::read_file(path);
+        fb2_model_desc d = fm_desc(f.hdr);
+        d.weight_dtype = weight_dtype;
+        const std::vector<long long> numel = param_numels(d);
+        // the weights are 4-byte aligned only if the header length is; copy otherwise
+        std::vector<float> aligned;
+        const unsigned char* base = f.bytes.data() + f.weights_at;
+        const float* w = reinterpret_cast<const float*>(base);
+        if (reinterpret_cast<uintptr_t>(base) % alignof(float)) {
+            long long total = 0;
+            for (long long k : numel) total += k;
+            aligned.resize((size_t)total);
+            std::memcpy(aligned.data(), base, (size_t)total * 4);
+            w = aligned.data();
+        }
+        std::vector<const float*> ptrs;
+        for (long long k : numel) {
+            ptrs.push_back(w);
+            w += k;
+        }
+        const int32_t st = fb2_model_create(&d, ptrs.data(), (int32_t)ptrs.size(), devices, n_devices, out);
+        if (st != FB2_OK) fail(st, g_last_error);
+        if (out_desc) *out_desc = d;
+    });
+}
+
+int32_t fb2_forgemodel_write(const char* path, const fb2_model_desc* desc, const char* model_name,
+                             const float* const* params, int32_t n_params) {
+    return guarded([&] {
+        if (!path || !desc || !params) fail(FB2_INVALID_ARG, "NULL argument");
+        const fb2_model_desc& d = *desc;
+        if (d.vocab_size <= 0 || d.context_length <= 0 || d.d_model <= 0 || d.n_layers <= 0 || d.n_heads <= 0 ||
+            d.d_model % d.n_heads)
+            fail(FB2_INVALID_ARG, "invalid model configuration");
+        if (n_params != 4 + 12 * d.n_layers) fail(FB2_INVALID_ARG, "n_params must be 4 + 12*n_layers");
+        for (int i = 0; i < n_params; i++)
+            if (!params[i]) fail(FB2_INVALID_ARG, "parameter pointer is NULL");
+        fb2::fm::Header h;
+        h.vocab = d.vocab_size;
+        h.ctx = d.context_length;
+        h.d_model = d.d_model;
+        h.n_layers = d.n_layers;
+        h.n_heads = d.n_heads;
+        h.name = model_name ? model_name : "";
+        bool blank = true;
+        for (char c : h.name)
+            if (!std::isspace((unsigned char)c)) blank = false;
+        if (blank) fail(FB2_INVALID_ARG, "a checkpoint needs a model name");
+        fb2::fm::write_file(path, h, params, n_params);
+    });
+}
+
+int32_t fb2_test_sha256(const void* data, int64_t n, uint8_t* out32) {
+    return guarded([&] {
+        if ((!data && n) || n < 0 || !out32) fail(FB2_INVALID_ARG, "bad arguments");
+        fb2::fm::Sha256 h;
+        h.update(data, (size_t)n);
+        h.finish(out32);
+    });
+}
+
 int32_t fb2_test_gemm_tc(int32_t M, int32_t N, int32_t K, const float* A, const float* W, float* out) {
     return guarded([&] {
         if (!A || !W || !out) fail(FB2_INVALID_ARG, "NULL argument");

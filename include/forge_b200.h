@@ -46,7 +46,8 @@ typedef enum {
     FB2_CUDA_ERROR = -3,
     FB2_TIMEOUT = -4,      /* a bounded device wait gave up; the context stays usable */
     FB2_UNSUPPORTED = -5,  /* shape or option this build does not handle */
-    FB2_NO_DEVICE = -6
+    FB2_NO_DEVICE = -6,
+    FB2_INVALID_DATA = -7  /* a checkpoint file breaks the FORGEMODEL1 rules (InvalidDataException) */
 } fb2_status;
 
 /* FB2_WEIGHTS_BF16: the caller still passes fp32 arrays; the library rounds
@@ -230,6 +231,32 @@ int32_t fb2_init_params(const fb2_model_desc* desc, int32_t seed, float* const* 
 /* ---- statistics -------------------------------------------------------------- */
 int32_t fb2_stats(fb2_session* s, fb2_stats_t* out);
 int32_t fb2_stats_reset(fb2_session* s);
+
+/* ---- FORGEMODEL1 checkpoints (src/LLM.Core/Checkpoint/Checkpoint.cs) ----------
+ * File: "FORGEMODEL1", int32 LE header length, UTF-8 JSON header, fp32 LE
+ * parameters in registry order (+ Adam moments when the header says so),
+ * SHA-256 of everything before the 32-byte trailer.  Every rule
+ * Checkpoint.LoadCore (Checkpoint.cs:174-264) enforces returns
+ * FB2_INVALID_DATA with its message; the checksum is verified before any
+ * weight is used. */
+
+/* Validates the whole file and returns its model configuration (weight_dtype
+ * FB2_WEIGHTS_FP32) and ModelName (NUL-terminated, truncated to
+ * name_capacity - 1 bytes; name may be NULL).  No device needed.  Replaces
+ * Checkpoint.LoadWithMetadata's header half (Checkpoint.cs:124-125). */
+int32_t fb2_forgemodel_read_header(const char* path, fb2_model_desc* out_desc, char* name, int32_t name_capacity);
+
+/* Checkpoint.Load (Checkpoint.cs:121-122) straight into device memory: the
+ * validated file's weights go to fb2_model_create (weight_dtype as there).
+ * out_desc (may be NULL) receives the configuration. */
+int32_t fb2_model_load_forgemodel(const char* path, int32_t weight_dtype, const int32_t* devices, int32_t n_devices,
+                                  fb2_model_desc* out_desc, fb2_model** out);
+
+/* Writes params (registry order, fp32) as a FORGEMODEL1 model checkpoint in
+ * the layout Checkpoint.SaveTraining writes (Checkpoint.cs:63-119, 143-166),
+ * with a Training header that records no optimizer state. */
+int32_t fb2_forgemodel_write(const char* path, const fb2_model_desc* desc, const char* model_name,
+                             const float* const* params, int32_t n_params);
 
 #ifdef __cplusplus
 }

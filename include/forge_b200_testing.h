@@ -34,6 +34,9 @@ struct fb2_session;
 int32_t fb2_test_mk_trace(struct fb2_session* s, uint64_t* out, int64_t capacity, int32_t* n_ctas,
                           int32_t* n_steps);
 
+/* SHA-256 of n bytes (the checkpoint trailer's hash; host only). */
+int32_t fb2_test_sha256(const void* data, int64_t n, uint8_t* out32);
+
 /* out[M][N] = A[M][K] * W[K][N] through the tensor-core 3xTF32 GEMM on the
  * current device (host arrays; M, N, K > 0, N and K multiples of 4).
  * FB2_UNSUPPORTED when the tensor-core path is unavailable. */

@@ -285,6 +285,23 @@ def test_bf16_weights(pkg, O, monkeypatch):
             check_ids(O, ocfg, rparams, p, gotb[i], O.generate(ocfg, rparams, p, 24, 0.0, 0, O.DotNetRandom(1)))
 
 
+def test_forgemodel_checkpoint_round_trip(pkg, O, tmp_path):
+    """CheckpointTests.cs:31-60 on the device: a model loaded from its
+    FORGEMODEL1 file gives bitwise the logits of the in-memory model."""
+    shape = (300, 24, 32, 2, 2)
+    cfg = pkg.ModelConfig(*shape)
+    params = O.init_params(O.Config(*shape), 42)
+    path = tmp_path / "forge-test.forgemodel"
+    pkg.write_forgemodel(path, cfg, params, "Forge-Test")
+    toks = np.random.default_rng(2).integers(0, shape[0], (2, 20)).astype(np.int32)
+    with pkg.B200Backend(cfg, params, devices=[0], max_seqs=2) as a:
+        want = a.forward_last_batch([t.tolist() for t in toks])
+    with pkg.B200Backend.from_forgemodel(path, devices=[0], max_seqs=2) as b:
+        assert b.config.d_model == shape[2]
+        got = b.forward_last_batch([t.tolist() for t in toks])
+    assert np.array_equal(np.asarray(got).view(np.uint32), np.asarray(want).view(np.uint32))
+
+
 def test_generate_batch_ragged_and_long_prompts(pkg, O):
     shape = (300, 24, 32, 2, 2)
     ocfg, params, be = make(pkg, O, shape, 9, max_seqs=5)
