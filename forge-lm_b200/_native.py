@@ -53,7 +53,7 @@ class Stats(C.Structure):
     _fields_ = [("tokens_generated", C.c_int64), ("decode_steps", C.c_int64), ("prefill_rows", C.c_int64),
                 ("reprefills", C.c_int64), ("prefill_ms", C.c_double), ("decode_ms", C.c_double),
                 ("sample_ms", C.c_double), ("kernel_launches", C.c_int64), ("device_count", C.c_int32),
-                ("reserved", C.c_int32), ("persistent_steps", C.c_int64)]
+                ("reserved", C.c_int32), ("persistent_steps", C.c_int64), ("reused_prefix_rows", C.c_int64)]
 
 
 TOKEN_CB = C.CFUNCTYPE(C.c_int32, C.c_void_p, C.c_int32, C.c_int32, C.c_int32)

@@ -398,6 +398,11 @@ struct DeviceSession {
 
     // per-slot state
     int *d_len = nullptr, *d_count = nullptr, *d_done = nullptr, *d_hist = nullptr;
+    // tokens whose K/V the slot's cache holds at positions 0.. (the window of
+    // the last host-path generate, when it never slid); empty = unknown.  A
+    // later generate whose prompt starts with them prefills only the rest
+    // (a chat turn resubmits the whole history, Program.cs:736-765).
+    std::vector<std::vector<int>> kv_tokens;
     int hist_cap = 0;
     float* d_kv = nullptr;
     long long kv_slot_stride = 0, kv_layer_stride = 0, v_offset = 0;
@@ -938,15 +943,21 @@ static void run_prefill_chunk(DeviceSession& s, const ChunkPlan& c, const int* d
 }
 
 // Builds prefill chunk tables for slots `order` with window lengths `wl`
-// (slot-local indices), appending to `tab` and `plans`.
+// (slot-local indices), appending to `tab` and `plans`.  `start` (optional):
+// per slot the first position to compute; the cache already holds K/V of
+// the positions before it.
 static void plan_prefill(const DeviceSession& s, const std::vector<int>& order, const std::vector<int>& wl,
-                         std::vector<int>& tab, std::vector<ChunkPlan>& plans) {
+                         std::vector<int>& tab, std::vector<ChunkPlan>& plans, const std::vector<int>* start = nullptr) {
+    auto st = [&](int sl) { return start ? (*start)[sl] : 0; };
     size_t i = 0;
     while (i < order.size()) {
         size_t j = i;
         int rows = 0;
-        while (j < order.size() && j - i < (size_t)kMaxChunkSlots && (rows + wl[order[j]] <= s.row_cap || j == i))
-            rows += wl[order[j++]];
+        while (j < order.size() && j - i < (size_t)kMaxChunkSlots &&
+               (rows + wl[order[j]] - st(order[j]) <= s.row_cap || j == i)) {
+            rows += wl[order[j]] - st(order[j]);
+            j++;
+        }
         if (rows > s.row_cap) fail(FB2_UNSUPPORTED, "window longer than the session's row capacity");
         ChunkPlan c{};
         c.rows = rows;
@@ -957,21 +968,21 @@ static void plan_prefill(const DeviceSession& s, const std::vector<int>& order, 
         std::vector<int> last, slot;
         int r = 0;
         for (size_t k = i; k < j; k++) {
-            int sl = order[k], w = wl[sl];
-            for (int p = 0; p < w; p++) {
+            const int sl = order[k], w = wl[sl], a = st(sl);
+            for (int p = a; p < w; p++) {
                 seq.push_back(sl);
                 pos.push_back(p);
             }
-            for (int p0 = 0; p0 < w; p0 += 64) {
+            for (int p0 = a; p0 < w; p0 += 64) {
                 int cnt = std::min(64, w - p0);
-                q.push_back(r + p0);
+                q.push_back(r + (p0 - a));
                 q.push_back(cnt);
                 q.push_back(sl);
                 q.push_back(p0);
             }
-            last.push_back(r + w - 1);
+            last.push_back(r + (w - a) - 1);
             slot.push_back(sl);
-            r += w;
+            r += w - a;
         }
         tab.insert(tab.end(), seq.begin(), seq.end());
         tab.insert(tab.end(), pos.begin(), pos.end());
@@ -1159,11 +1170,26 @@ static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
     for (int i = 0; i < n; i++) order[i] = i;
     std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return slide_at[a] < slide_at[b]; });
 
+    // cached prefixes: a slot whose cache holds the K/V of this prompt's first
+    // tokens (the previous turn of a chat) computes only the new positions
+    std::vector<int> start(n, 0);
+    if (!job.device_io && (int)s.kv_tokens.size() >= n)
+        for (int i = 0; i < n; i++) {
+            const std::vector<int>& kv = s.kv_tokens[i];
+            if (kv.empty() || plen[i] > ctx) continue;
+            const int* p = job.prompt_tokens + poff[i];
+            int c = 0;
+            while (c < (int)kv.size() && c < plen[i] && kv[c] == p[c]) c++;
+            start[i] = std::min(c, plen[i] - 1);  // at least one row yields the logits
+            s.stats.reused_prefix_rows += start[i];
+        }
+    for (auto& kv : s.kv_tokens) kv.clear();  // rewritten below for the host path
+
     std::vector<int> tab;
     std::vector<ChunkPlan> init_plans, slide_plans_all;
     std::vector<int> all(n);
     for (int i = 0; i < n; i++) all[i] = i;
-    plan_prefill(s, all, wl0, tab, init_plans);
+    plan_prefill(s, all, wl0, tab, init_plans, &start);
     // sliding re-prefill: every window is ctx rows; plan chunks over prefixes
     // of `order` (the set that slides only grows with the step).
     std::vector<int> wctx(n, ctx);
@@ -1332,6 +1358,17 @@ static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
         s.stats.tokens_generated += counts[i];
         if (job.rng_mode == FB2_RNG_SESSION && sampled)
             for (int k = 0; k < counts[i]; k++) s.rngs[i].next_double();
+    }
+    // the cache now holds the K/V of the prompt and of every generated token
+    // but the last (never fed), at positions 0.. when the window never slid
+    if ((int)s.kv_tokens.size() < n) s.kv_tokens.resize(n);
+    for (int i = 0; i < n; i++) {
+        const int fed = plen[i] + std::max(counts[i] - 1, 0);
+        if (plen[i] == 0 || fed > ctx) continue;
+        std::vector<int>& kv = s.kv_tokens[i];
+        kv.assign(job.prompt_tokens + poff[i], job.prompt_tokens + poff[i] + plen[i]);
+        if (max_new > 0)
+            kv.insert(kv.end(), job.out_tokens + (size_t)i * max_new, job.out_tokens + (size_t)i * max_new + std::max(counts[i] - 1, 0));
     }
 }
 
@@ -1746,6 +1783,12 @@ int32_t fb2_generate(fb2_session* S, int32_t n_seqs, const int32_t* prompt_token
     });
 }
 
+// The slots' caches are about to be overwritten outside the generate path.
+static void forget_cached_prefixes(fb2_session* S) {
+    for (auto d : S->ds)
+        for (auto& kv : d->kv_tokens) kv.clear();
+}
+
 int32_t fb2_generate_device(fb2_session* S, int32_t n_seqs, const int32_t* device_prompt_tokens,
                             const int32_t* device_prompt_lens, const int32_t* host_prompt_lens, const fb2_sampling* sp,
                             int32_t rng_mode, const int32_t* seeds, const double* device_uniforms,
@@ -1809,6 +1852,7 @@ int32_t fb2_forward_last_logits(fb2_session* S, int32_t n_seqs, const int32_t* t
     return guarded([&] {
         if (!S || !tokens || !lens || !out_logits) fail(FB2_INVALID_ARG, "NULL argument");
         if (n_seqs <= 0 || n_seqs > S->max_seqs) fail(FB2_INVALID_ARG, "n_seqs out of range");
+        forget_cached_prefixes(S);
         const fb2_model& m = *S->model;
         long long total = 0;
         for (int i = 0; i < n_seqs; i++) {
@@ -1859,6 +1903,7 @@ int32_t fb2_teacher_forced_logits(fb2_session* S, int32_t n_seqs, const int32_t*
         const fb2_model& m = *S->model;
         if (n_seqs <= 0 || n_seqs > S->max_seqs) fail(FB2_INVALID_ARG, "n_seqs out of range");
         if (prompt_len < 1 || len < prompt_len || len > m.ctx) fail(FB2_INVALID_ARG, "need 1 <= prompt_len <= len <= ctx");
+        forget_cached_prefixes(S);
         for (long long i = 0; i < (long long)n_seqs * len; i++)
             if (tokens[i] < 0 || tokens[i] >= m.V) fail(FB2_INVALID_ARG, "Token id out of range.");
         const int steps = len - prompt_len + 1;
@@ -1993,6 +2038,7 @@ int32_t fb2_stats(fb2_session* S, fb2_stats_t* out) {
             t.sample_ms += s->stats.sample_ms;
             t.kernel_launches += s->stats.kernel_launches;
             t.persistent_steps += s->stats.persistent_steps;
+            t.reused_prefix_rows += s->stats.reused_prefix_rows;
         }
         t.device_count = (int)S->ds.size();
         *out = t;

@@ -111,6 +111,7 @@ typedef struct {
     int32_t device_count;
     int32_t reserved;
     int64_t persistent_steps;   /* decode steps run inside the persistent decode kernel */
+    int64_t reused_prefix_rows; /* prompt positions whose K/V a previous generate left in the cache */
 } fb2_stats_t;
 
 /* ---- library ------------------------------------------------------------- */

@@ -302,6 +302,34 @@ def test_forgemodel_checkpoint_round_trip(pkg, O, tmp_path):
     assert np.array_equal(np.asarray(got).view(np.uint32), np.asarray(want).view(np.uint32))
 
 
+def test_chat_turns_reuse_the_cached_prefix(pkg, O):
+    """Chat (Program.cs:736-765) resubmits the whole history each turn: the
+    second turn prefills only the positions the first turn did not leave in
+    the cache, and its ids are those of a fresh generate.  A prompt that
+    departs from the history reuses only the common prefix."""
+    shape = (2256, 96, 128, 2, 4)
+    ocfg, params, be = make(pkg, O, shape, 5)
+    rng = np.random.default_rng(4)
+    p1 = rng.integers(0, shape[0], 20).astype(np.int32).tolist()
+    with be:
+        g1 = be.generate(p1, 12, 0.0, 0, None)
+        u2 = rng.integers(0, shape[0], 7).astype(np.int32).tolist()
+        p2 = p1 + list(g1) + u2
+        be.reset_stats()
+        g2 = be.generate(p2, 12, 0.0, 0, None)
+        st = be.stats()
+        assert st["reused_prefix_rows"] == len(p1) + len(g1) - 1
+        assert st["prefill_rows"] == len(p2) - st["reused_prefix_rows"]
+        check_ids(O, ocfg, params, np.array(p2), g2, O.generate(ocfg, params, np.array(p2), 12, 0.0, 0,
+                                                                 O.DotNetRandom(1)))
+        p3 = p2[:10] + [(p2[10] + 1) % shape[0]] + p2[11:]  # an edit at position 10
+        be.reset_stats()
+        g3 = be.generate(p3, 8, 0.7, 30, pkg.DotNetRandom(9))
+        assert be.stats()["reused_prefix_rows"] == 10
+        check_ids(O, ocfg, params, np.array(p3), g3, O.generate(ocfg, params, np.array(p3), 8, 0.7, 30,
+                                                                 O.DotNetRandom(9)))
+
+
 def test_generate_batch_ragged_and_long_prompts(pkg, O):
     shape = (300, 24, 32, 2, 2)
     ocfg, params, be = make(pkg, O, shape, 9, max_seqs=5)
