@@ -325,6 +325,40 @@ FB2_DEV void radix_pick(const uint32_t* hist, int kk, int& bin, int& above_out) 
     if (bin < 0) bin = 0;
 }
 
+// The k-th largest of vals[0..n) (ties counted, as "fewer than k strictly
+// larger"), by the consumer threads: an exact 4-pass radix select on the
+// order-preserving keys.  hist = 256 words, st = 3 ints of shared scratch;
+// every consumer thread returns the value.  k in [1, n].
+__device__ __noinline__ float cons_kth_largest(const float* vals, int n, int k, uint32_t* hist, int* st) {
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        st[0] = 0;  // prefix
+        st[1] = 0;  // mask
+        st[2] = k;  // rank still to find within the prefix
+    }
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        hist[tid] = 0u;
+        cons_sync();
+        const uint32_t prefix = (uint32_t)st[0], mask = (uint32_t)st[1];
+        for (int i = tid; i < n; i += MK_CONS) {
+            const uint32_t key = float_key(vals[i]);
+            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        cons_sync();
+        if ((tid >> 5) == 0) {
+            int bin, above;
+            radix_pick(hist, st[2], bin, above);
+            if (tid == 0) {
+                st[0] = (int)(prefix | ((uint32_t)bin << shift));
+                st[1] = (int)(mask | (255u << shift));
+                st[2] -= above;
+            }
+        }
+        cons_sync();
+    }
+    return key_float((uint32_t)st[0]);
+}
+
 FB2_DEV void wait_full(uint64_t* full, uint32_t it, int nstage, int* err, volatile int* abort_flag) {
     uint64_t* b = &full[it % nstage];
     const uint32_t par = (it / nstage) & 1u;
@@ -419,7 +453,7 @@ __device__ __noinline__ void mk_layernorm(const float* src, float* dst, int D, c
 
 // Shared-memory bytes the kernel needs besides the ring.
 inline size_t mk_aux_bytes(int MR, int D, int F, int H, int ctx, int slice_max, int maxc, int nstage) {
-    size_t floats = (size_t)MR * F + 2 * (size_t)MR * D + (size_t)MR * 256 + (size_t)MR * slice_max + 512 + 512;
+    size_t floats = (size_t)MR * F + 2 * (size_t)MR * D + (size_t)MR * 256 + (size_t)MR * slice_max + 512 + 512 + 2048;
     size_t ints = 2048 + (size_t)MR * ctx;
     size_t wts = 2 * (size_t)MR * H * maxc;
     return 2 * (size_t)nstage * 8 + floats * 4 + ints * 4 + MK_SURV_MAX * 8 + wts * 4;
@@ -533,7 +567,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     float* slice = red + MR * 256;                             // [MR][slice_max]
     float* scr = slice + MR * a.slice_max;                     // [512]
     float* uacc = scr + 512;                                   // [8][64] attention unit: per-warp p.V
-    int* iscr = reinterpret_cast<int*>(uacc + 512);            // [2048]
+    float* hstage = uacc + 512;                                // [2][4][256] sampler: slices' top 4 (value, id)
+    int* iscr = reinterpret_cast<int*>(hstage + 2048);         // [2048]
     int* win = iscr + 2048;                                    // [MR][ctx]
     float* surv_v = reinterpret_cast<float*>(win + MR * a.ctx);  // [MK_SURV_MAX]
     int* surv_i = reinterpret_cast<int*>(surv_v + MK_SURV_MAX);  // [MK_SURV_MAX]
@@ -1263,8 +1298,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         MK_TRACE(30);
         // ---- finalize: every CTA computes the same token for each row ----------
         for (int m = 0; m < MR; m++) {
-            float* tops = act;                                  // [nW][4] slices' largest values
-            int* topi = reinterpret_cast<int*>(act + 4 * nW);    // [nW][4] their vocabulary ids
+            float* tops = hstage;                                    // [nW][4] slices' largest values
+            int* topi = reinterpret_cast<int*>(hstage + 4 * 256);  // [nW][4] their vocabulary ids
             if (tid < nW) {  // nW <= 256: one slice header per thread
                 const unsigned long long* hp = a.cand_hdr + ((size_t)m * nW + tid) * 9;
                 unsigned long long w[9];
@@ -1280,6 +1315,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
             }
             if (cons_sync_or(s_abort)) return;
             fence_acq_rel();
+            if (m == 0) MK_TRACE(57);
             if (!sampled) {
                 // one candidate (the slice's first argmax) per slice
                 float bv = -INFINITY;
@@ -1320,19 +1356,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
             } else {
                 // lower bound of the row's k-th largest: the k-th largest of the
                 // slices' top values (a subset of the row)
-                float tl = INFINITY;
-                for (int i = tid; i < 4 * nW; i += MK_CONS) {
-                    const float v = tops[i];
-                    int rank = 0;
-                    for (int j = 0; j < 4 * nW; j++) rank += tops[j] > v;
-                    if (rank < sp.top_k) tl = fminf(tl, v);
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) tl = fminf(tl, __shfl_xor_sync(0xffffffffu, tl, o));
-                if (lane == 0) scr[256 + warp] = tl;
-                cons_sync();
-                float tlo = INFINITY;
-                for (int w8 = 0; w8 < 8; w8++) tlo = fminf(tlo, scr[256 + w8]);
+                const int ntops = 4 * nW;
+                const float tlo = cons_kth_largest(tops, ntops, min(sp.top_k, ntops), reinterpret_cast<uint32_t*>(scr),
+                                                   misc + 24);
+                if (m == 0) MK_TRACE(58);
                 // stage every candidate >= the bound: from the header when the
                 // slice's 4th largest is below the bound (then every such entry
                 // is among its top 4), else from the slice's list
@@ -1349,8 +1376,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                         for (int q4 = 0; q4 < 4; q4++) q += topi[tid * 4 + q4] >= 0 && !(tops[tid * 4 + q4] < tlo);
                     }
                 }
+                // when no slice needed its list, every entry >= the bound is
+                // among the tops, so the bound is the row's exact k-th largest
+                const int any_list = cons_sync_or(from_list ? 1 : 0);
                 int Q;
                 const int off = cons_excl_scan(q, misc + 16, Q);
+                if (m == 0) MK_TRACE(59);
                 if (Q <= MK_SURV_MAX && tid < nW) {
                     int o = off;
                     if (from_list) {
@@ -1399,14 +1430,18 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 }
                 if (Q <= MK_SURV_MAX) {
                     // exact threshold: smallest staged value with < k larger ones
+                    if (m == 0) MK_TRACE(60);
                     float thr = INFINITY, mx = -INFINITY;
                     for (int i = tid; i < Q; i += MK_CONS) {
                         const float v = surv_v[i];
                         mx = fmaxf(mx, v);
-                        int rank = 0;
-                        for (int j = 0; j < Q; j++) rank += surv_v[j] > v;
-                        if (rank < sp.top_k) thr = fminf(thr, v);
+                        if (any_list) {
+                            int rank = 0;
+                            for (int j = 0; j < Q; j++) rank += surv_v[j] > v;
+                            if (rank < sp.top_k) thr = fminf(thr, v);
+                        }
                     }
+                    if (!any_list) thr = tlo;
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) {
                         thr = fminf(thr, __shfl_xor_sync(0xffffffffu, thr, o));
@@ -1423,6 +1458,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                         M = fmaxf(M, scr[264 + w8]);
                     }
                     // exponentials of the survivors in parallel (Sampler.cs:57),
+                    if (m == 0) MK_TRACE(61);
                     // zero for the entries below the threshold
                     for (int i = tid; i < Q; i += MK_CONS) {
                         const float v = surv_v[i];
@@ -1448,6 +1484,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                         rtok[m] = pick;
                     }
                     cons_sync();
+                    if (m == 0) MK_TRACE(62);
                 } else {
                     // more candidates above the bound than shared memory stages
                     // (massive ties): radix-select the threshold over memory,
