@@ -50,6 +50,12 @@ FB2_DEV float ld_cg(const float* p) { return __ldcg(p); }
 FB2_DEV float4 ld_cg4(const float4* p) { return __ldcg(p); }
 
 // Streaming read-only weight load: do not keep in L1.
+// Programmatic dependent launch: the kernels of a decode step are launched
+// with programmatic stream serialization, so a kernel's launch and prologue
+// overlap its predecessor; every kernel waits here for the predecessor grid
+// to complete before touching global memory (a no-op without the attribute).
+FB2_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 FB2_DEV uint2 ld_stream_u2(const uint2* p) {
     uint2 v;
     asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));

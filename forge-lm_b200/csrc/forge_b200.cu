@@ -60,6 +60,25 @@ void ck(cudaError_t e, const char* what) {
 }
 #define CK(x) ck((x), #x)
 
+// Launch with programmatic stream serialization (the kernel itself waits in
+// pdl_wait before touching global memory), so consecutive kernels of a step
+// overlap launch and prologue; inside a stream capture this becomes a
+// programmatic edge of the graph.
+template <class... KArgs, class... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ck(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), "cudaLaunchKernelEx");
+}
+
 template <class F>
 int32_t guarded(F&& f) {
     try {
@@ -260,6 +279,7 @@ static float bf16_round_host(float x) {
 }
 // bf16 bits of values that are already bf16-representable fp32.
 __global__ void k_to_bf16_bits(const float* __restrict__ x, long long n, unsigned short* __restrict__ y) {
+    pdl_wait();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         y[i] = (unsigned short)(__float_as_uint(x[i]) >> 16);
 }
@@ -293,11 +313,11 @@ static bool tc_encode(CUtensorMap* map, const float* base, uint64_t inner, uint6
 static void launch_split_tf32(cudaStream_t st, const float* x, size_t n, float* hi, float* lo) {
     const size_t n4 = n / 4;
     const int blocks = (int)std::min<size_t>(4096, (n4 + 255) / 256);
-    k_split_tf32<<<std::max(blocks, 1), 256, 0, st>>>(reinterpret_cast<const float4*>(x), n4,
+    launch_pdl(k_split_tf32, std::max(blocks, 1), 256, 0, st, reinterpret_cast<const float4*>(x), n4,
                                                       reinterpret_cast<float4*>(hi), reinterpret_cast<float4*>(lo));
 }
 static void launch_split_tf32_transpose(cudaStream_t st, const float* W, int K, int N, float* hiT, float* loT) {
-    k_split_tf32_transpose<<<dim3(ceil_div(N, 32), ceil_div(K, 32)), dim3(32, 8), 0, st>>>(W, K, N, hiT, loT);
+    launch_pdl(k_split_tf32_transpose, dim3(ceil_div(N, 32), ceil_div(K, 32)), dim3(32, 8), 0, st, W, K, N, hiT, loT);
 }
 // TF32 hi/lo copies of every projection, transposed to W^T [N][K], and their
 // descriptors (boxes of 32 K x 128 N rows).  FORGE_B200_GEMM=simt leaves the
@@ -545,7 +565,7 @@ static void launch_layernorm(DeviceSession& s, int rows, const float* x, const f
     int per = ceil_div(D, 32);
     dim3 grid(ceil_div(rows, 8)), block(256);
 #define LN_CASE(P) \
-    if (per <= P) { s.stats.kernel_launches++; k_layernorm<P><<<grid, block, 0, s.stream>>>(rows, D, x, w, b, y, row_map); return; }
+    if (per <= P) { s.stats.kernel_launches++; launch_pdl(k_layernorm<P>, grid, block, 0, s.stream, rows, D, x, w, b, y, row_map); return; }
     LN_CASE(1) LN_CASE(2) LN_CASE(4) LN_CASE(8) LN_CASE(16) LN_CASE(24) LN_CASE(32) LN_CASE(48) LN_CASE(64)
 #undef LN_CASE
     fail(FB2_UNSUPPORTED, "d_model too large for the LayerNorm kernel");
@@ -566,10 +586,10 @@ static void launch_gemv_mr(DeviceSession& s, int M, int K, int N, const float* A
     s.stats.kernel_launches++;
     auto it = s.dm->w16.find(W);
     if (it != s.dm->w16.end())
-        k_gemv<MR, WBF16><<<dim3(nblk, S), 256, smem, s.stream>>>(M, K, N, kchunk, A, it->second, s.d_gemv_part,
+        launch_pdl(k_gemv<MR, WBF16>, dim3(nblk, S), 256, smem, s.stream, M, K, N, kchunk, A, it->second, s.d_gemv_part,
                                                                   s.d_tickets, e);
     else
-        k_gemv<MR><<<dim3(nblk, S), 256, smem, s.stream>>>(M, K, N, kchunk, A, W, s.d_gemv_part, s.d_tickets, e);
+        launch_pdl(k_gemv<MR>, dim3(nblk, S), 256, smem, s.stream, M, K, N, kchunk, A, W, s.d_gemv_part, s.d_tickets, e);
 }
 
 // y = A * W (+ epilogue) for M rows.
@@ -593,7 +613,7 @@ static bool launch_gemm_tc(cudaStream_t st, int sm_count, int M, int K, int N, c
         if (!tc_encode(&maps.a_hi, ahi, K, M, TC_BM) || !tc_encode(&maps.a_lo, alo, K, M, TC_BM))
             fail(FB2_CUDA_ERROR, "cuTensorMapEncodeTiled failed for a GEMM operand");
         (*launches)++;
-        k_gemm_tc<128><<<dim3(ceil_div(N, 128), ceil_div(M, TC_BM)), 128, TcCfg<128>::SMEM, st>>>(maps, M, N, K, e, err);
+        launch_pdl(k_gemm_tc<128>, dim3(ceil_div(N, 128), ceil_div(M, TC_BM)), 128, TcCfg<128>::SMEM, st, maps, M, N, K, e, err);
         return true;
     }
     const int bnb = M <= 64 ? 64 : 128;
@@ -605,12 +625,12 @@ static bool launch_gemm_tc(cudaStream_t st, int sm_count, int M, int K, int N, c
     if ((size_t)S * M * N > part_cap) S = 1;
     dim3 grid(ceil_div(N, 128), ceil_div(M, bnb), S);
     (*launches)++;
-    if (bnb == 64) k_gemm_tc_swab<64><<<grid, 128, TcSwabCfg<64>::SMEM, st>>>(maps, M, N, K, e, err, part);
-    else k_gemm_tc_swab<128><<<grid, 128, TcSwabCfg<128>::SMEM, st>>>(maps, M, N, K, e, err, part);
+    if (bnb == 64) launch_pdl(k_gemm_tc_swab<64>, grid, 128, TcSwabCfg<64>::SMEM, st, maps, M, N, K, e, err, part);
+    else launch_pdl(k_gemm_tc_swab<128>, grid, 128, TcSwabCfg<128>::SMEM, st, maps, M, N, K, e, err, part);
     if (S > 1) {
         const size_t n4 = (size_t)M * N / 4;
         (*launches)++;
-        k_splitk_reduce<<<(int)std::min<size_t>((n4 + 255) / 256, 4 * (size_t)sm_count), 256, 0, st>>>(part, S, M, N, e);
+        launch_pdl(k_splitk_reduce, (int)std::min<size_t>((n4 + 255) / 256, 4 * (size_t)sm_count), 256, 0, st, part, S, M, N, e);
     }
     return true;
 }
@@ -657,10 +677,10 @@ static void launch_linear(DeviceSession& s, int M, int K, int N, const float* A,
     }
     if (M <= 1024) {
         dim3 grid(ceil_div(N, 128), ceil_div(M, 64));
-        s.stats.kernel_launches++; k_gemm_tiled<64><<<grid, 256, 0, s.stream>>>(M, K, N, A, W, e);
+        s.stats.kernel_launches++; launch_pdl(k_gemm_tiled<64>, grid, 256, 0, s.stream, M, K, N, A, W, e);
     } else {
         dim3 grid(ceil_div(N, 128), ceil_div(M, 128));
-        s.stats.kernel_launches++; k_gemm_tiled<128><<<grid, 256, 0, s.stream>>>(M, K, N, A, W, e);
+        s.stats.kernel_launches++; launch_pdl(k_gemm_tiled<128>, grid, 256, 0, s.stream, M, K, N, A, W, e);
     }
 }
 
@@ -678,9 +698,9 @@ static void launch_attn_decode_hd(DeviceSession& s, int M, int layer, Rows R) {
     const fb2_model& m = *s.model;
     float scale = 1.0f / sqrtf((float)m.hd);  // Layers.cs:174
     const float* kvl = s.d_kv + (size_t)layer * s.kv_layer_stride;
-    s.stats.kernel_launches++; k_attn_decode_partial<HD><<<dim3(M, m.H, s.attn_nsplit), 128, 0, s.stream>>>(
+    s.stats.kernel_launches++; launch_pdl(k_attn_decode_partial<HD>, dim3(M, m.H, s.attn_nsplit), 128, 0, s.stream, 
         s.d_q, kvl, s.kv_slot_stride, s.v_offset, m.H, m.ctx, scale, R, s.d_attn_part, s.attn_nsplit);
-    s.stats.kernel_launches++; k_attn_decode_combine<HD><<<dim3(M, m.H), 64, 0, s.stream>>>(s.d_attn_part, m.H, s.attn_nsplit, R, s.d_att);
+    s.stats.kernel_launches++; launch_pdl(k_attn_decode_combine<HD>, dim3(M, m.H), 64, 0, s.stream, s.d_attn_part, m.H, s.attn_nsplit, R, s.d_att);
 }
 
 static void launch_attn_decode(DeviceSession& s, int M, int layer, Rows R) {
@@ -703,12 +723,12 @@ static void launch_attn_prefill_hd(DeviceSession& s, int nblk, const int4* qblk,
     if constexpr (HD == 32 || HD == 64 || HD == 128) {
         const size_t smem = (size_t)(64 * (HD + 4) * 2 + 64 * HD + 64 * 68) * 4;
         s.stats.kernel_launches++;
-        k_attn_prefill_rt<HD><<<dim3(nblk, m.H), 256, smem, s.stream>>>(s.d_q, kvl, s.kv_slot_stride, s.v_offset, m.H,
+        launch_pdl(k_attn_prefill_rt<HD>, dim3(nblk, m.H), 256, smem, s.stream, s.d_q, kvl, s.kv_slot_stride, s.v_offset, m.H,
                                                                         m.ctx, scale, qblk, s.d_att);
         return;
     }
     size_t smem = (size_t)(64 * (HD + 1) * 2 + 64 * HD + 64 * 65) * 4;
-    s.stats.kernel_launches++; k_attn_prefill<HD><<<dim3(nblk, m.H), 256, smem, s.stream>>>(s.d_q, kvl, s.kv_slot_stride, s.v_offset, m.H,
+    s.stats.kernel_launches++; launch_pdl(k_attn_prefill<HD>, dim3(nblk, m.H), 256, smem, s.stream, s.d_q, kvl, s.kv_slot_stride, s.v_offset, m.H,
                                                                  m.ctx, scale, qblk, s.d_att);
 }
 
@@ -739,9 +759,9 @@ static void launch_head(DeviceSession& s, int M, const float* xln, const int* ou
         smem = (size_t)R * m.D * 4;                                                                \
         s.stats.kernel_launches++;                                                                 \
         if (s.dm->bf16)                                                                            \
-            k_head<R, WBF16><<<blocks, 256, smem, s.stream>>>(mm, m.D, m.V, x, s.dm->w16.at(s.dm->tok_emb), out, m.V); \
+            launch_pdl(k_head<R, WBF16>, blocks, 256, smem, s.stream, mm, m.D, m.V, x, s.dm->w16.at(s.dm->tok_emb), out, m.V); \
         else                                                                                       \
-            k_head<R><<<blocks, 256, smem, s.stream>>>(mm, m.D, m.V, x, s.dm->tok_emb, out, m.V);  \
+            launch_pdl(k_head<R>, blocks, 256, smem, s.stream, mm, m.D, m.V, x, s.dm->tok_emb, out, m.V);  \
         continue;                                                                                  \
     }
         HEAD_CASE(1) HEAD_CASE(2) HEAD_CASE(4) HEAD_CASE(8) HEAD_CASE(16)
@@ -779,10 +799,10 @@ static void run_layers(DeviceSession& s, int M, Rows R, bool decode, int nqblk, 
 // One KV-cached decode step for slots 0..n-1 (graph-captured).
 static void enqueue_decode_step(DeviceSession& s, int n) {
     const fb2_model& m = *s.model;
-    s.stats.kernel_launches++; k_step_prepare<<<ceil_div(n, 128), 128, 0, s.stream>>>(n, s.d_len, s.d_done, m.ctx, s.d_row_seq, s.d_row_pos,
+    s.stats.kernel_launches++; launch_pdl(k_step_prepare, ceil_div(n, 128), 128, 0, s.stream, n, s.d_len, s.d_done, m.ctx, s.d_row_seq, s.d_row_pos,
                                                           s.d_row_hidx, s.d_row_active);
     Rows R{s.d_row_seq, s.d_row_pos, s.d_row_hidx, s.d_row_active};
-    s.stats.kernel_launches++; k_embed<<<n, 128, 0, s.stream>>>(n, R, s.d_hist, s.hist_cap, s.dm->tok_emb, s.dm->pos_emb, m.D, m.V, s.d_x);
+    s.stats.kernel_launches++; launch_pdl(k_embed, n, 128, 0, s.stream, n, R, s.d_hist, s.hist_cap, s.dm->tok_emb, s.dm->pos_emb, m.D, m.V, s.d_x);
     run_layers(s, n, R, true, 0, nullptr);
     launch_layernorm(s, n, s.d_x, s.dm->lnf_w, s.dm->lnf_b, s.d_lnf, nullptr);
     launch_head(s, n, s.d_lnf, nullptr, s.d_logits);
@@ -904,6 +924,7 @@ struct PrefillTables {
 };
 
 __global__ void k_gather_logits_rows(int n, const int* out_slot, const float* src, float* dst, int V) {
+    pdl_wait();
     // src rows are chunk-compact; dst rows are session slots
     int r = blockIdx.y;
     if (r >= n) return;
@@ -913,6 +934,7 @@ __global__ void k_gather_logits_rows(int n, const int* out_slot, const float* sr
 }
 
 __global__ void k_prefill_hidx(int rows, const int* row_seq, const int* row_pos, const int* len, int ctx, int* hidx) {
+    pdl_wait();
     int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) return;
     int L = len[row_seq[r]];
@@ -927,17 +949,17 @@ static void run_prefill_chunk(DeviceSession& s, const ChunkPlan& c, const int* d
     const int4* qblk = reinterpret_cast<const int4*>(d_tab_base + c.qblk_off);
     const int* last_row = d_tab_base + c.slot_off;
     const int* out_slot = last_row + c.nslots;
-    s.stats.kernel_launches++; k_prefill_hidx<<<ceil_div(c.rows, 256), 256, 0, s.stream>>>(c.rows, row_seq, row_pos, s.d_len, m.ctx,
+    s.stats.kernel_launches++; launch_pdl(k_prefill_hidx, ceil_div(c.rows, 256), 256, 0, s.stream, c.rows, row_seq, row_pos, s.d_len, m.ctx,
                                                                s.d_row_hidx);
     Rows R{row_seq, row_pos, s.d_row_hidx, s.d_ones};
-    s.stats.kernel_launches++; k_embed<<<c.rows, 128, 0, s.stream>>>(c.rows, R, s.d_hist, s.hist_cap, s.dm->tok_emb, s.dm->pos_emb, m.D, m.V,
+    s.stats.kernel_launches++; launch_pdl(k_embed, c.rows, 128, 0, s.stream, c.rows, R, s.d_hist, s.hist_cap, s.dm->tok_emb, s.dm->pos_emb, m.D, m.V,
                                           s.d_x);
     run_layers(s, c.rows, R, false, c.nqblk, qblk);
     launch_layernorm(s, c.nslots, s.d_x, s.dm->lnf_w, s.dm->lnf_b, s.d_lnf, last_row);
     // head into the chunk-compact area after the slots' logits, then scatter
     float* tmp = s.d_logits + (size_t)s.nslots * m.V;
     launch_head(s, c.nslots, s.d_lnf, nullptr, tmp);
-    s.stats.kernel_launches++; k_gather_logits_rows<<<dim3(std::min(ceil_div(m.V, 256), 64), c.nslots), 256, 0, s.stream>>>(c.nslots, out_slot,
+    s.stats.kernel_launches++; launch_pdl(k_gather_logits_rows, dim3(std::min(ceil_div(m.V, 256), 64), c.nslots), 256, 0, s.stream, c.nslots, out_slot,
                                                                                               tmp, s.d_logits, m.V);
     s.stats.prefill_rows += c.rows;
 }
@@ -1063,6 +1085,7 @@ static void upload_tables(DeviceSession& s, const std::vector<int>& tab, const s
 __global__ void k_init_slots(int n, const int* __restrict__ plens_eff, const int* __restrict__ poff,
                              const int* __restrict__ ptok, int* hist, int hist_stride, int* len, int* count, int* done,
                              int max_new) {
+    pdl_wait();
     int sidx = blockIdx.x;
     if (sidx >= n) return;
     int w = plens_eff[sidx];
@@ -1079,6 +1102,7 @@ __global__ void k_init_slots(int n, const int* __restrict__ plens_eff, const int
 // on the device; keeps the last min(len, ctx) tokens of each prompt.
 __global__ void k_init_slots_device(int n, const int* __restrict__ plens, const int* __restrict__ ptok, int ctx,
                                     int* hist, int hist_stride, int* len, int* count, int* done, int max_new) {
+    pdl_wait();
     int sidx = blockIdx.x;
     if (sidx >= n) return;
     long long off = 0;
@@ -1095,6 +1119,7 @@ __global__ void k_init_slots_device(int n, const int* __restrict__ plens, const 
 }
 
 __global__ void k_copy_counts(int n, const int* count, int* out) {
+    pdl_wait();
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) out[i] = count[i];
 }
@@ -1247,17 +1272,17 @@ static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
 
     int* d_out = job.device_io ? job.out_tokens : s.d_out;
     if (job.device_io) {
-        s.stats.kernel_launches++; k_init_slots_device<<<n, 256, 0, s.stream>>>(n, job.dev_prompt_lens, job.dev_prompt_tokens, ctx, s.d_hist,
+        s.stats.kernel_launches++; launch_pdl(k_init_slots_device, n, 256, 0, s.stream, n, job.dev_prompt_lens, job.dev_prompt_tokens, ctx, s.d_hist,
                                                      s.hist_cap, s.d_len, s.d_count, s.d_done, max_new);
     } else {
-        s.stats.kernel_launches++; k_init_slots<<<n, 256, 0, s.stream>>>(n, s.d_tab + pl_off, s.d_tab + poff_off, s.d_tab + ptok_off, s.d_hist,
+        s.stats.kernel_launches++; launch_pdl(k_init_slots, n, 256, 0, s.stream, n, s.d_tab + pl_off, s.d_tab + poff_off, s.d_tab + ptok_off, s.d_hist,
                                               s.hist_cap, s.d_len, s.d_count, s.d_done, max_new);
     }
     CK(cudaGetLastError());
     SampleParams P = to_params(sp);
     size_t ssmem = sampler_smem_bytes(m.V);
     auto sample_all = [&]() {
-        s.stats.kernel_launches++; k_sample_step<<<n, kSampleThreads, ssmem, s.stream>>>(n, s.d_logits, m.V, ctx, s.d_hist, s.hist_cap, s.d_len,
+        s.stats.kernel_launches++; launch_pdl(k_sample_step, n, kSampleThreads, ssmem, s.stream, n, s.d_logits, m.V, ctx, s.d_hist, s.hist_cap, s.d_len,
                                                               s.d_count, s.d_done, d_uni, max_new, P, d_out, max_new);
     };
     std::vector<int> h_tok, h_cnt, prev_cnt(n, 0);
@@ -1340,7 +1365,7 @@ static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
     CK(cudaGetLastError());
     CK(cudaEventRecord(s.ev1, s.stream));
     if (job.device_io) {
-        s.stats.kernel_launches++; k_copy_counts<<<ceil_div(n, 128), 128, 0, s.stream>>>(n, s.d_count, job.out_counts);
+        s.stats.kernel_launches++; launch_pdl(k_copy_counts, ceil_div(n, 128), 128, 0, s.stream, n, s.d_count, job.out_counts);
         CK(cudaGetLastError());
         return;
     }
@@ -1415,6 +1440,7 @@ NoallocLayout noalloc_layout(const fb2_model& m) {
 // 0..n-1, one query block, last row n-1 written to output row 0; tickets
 // cleared (the array keeps the previous call's contents).
 __global__ void k_noalloc_tables(int n, int* ints, unsigned int* tickets) {
+    pdl_wait();
     int* row_seq = ints;
     int* row_pos = ints + kNoallocMaxRows;
     int* hidx = ints + 2 * kNoallocMaxRows;
@@ -1827,6 +1853,7 @@ int32_t fb2_generate_device(fb2_session* S, int32_t n_seqs, const int32_t* devic
 }
 
 __global__ void k_bump_len(int n, int* len) {
+    pdl_wait();
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) len[i] += 1;
 }
@@ -1840,7 +1867,7 @@ static void load_histories(DeviceSession& s, int n, const int* tokens_host, int 
     int poff_off = (int)tab.size();
     for (int i = 0; i < n; i++) tab.push_back(i * seq_len);
     upload_tables(s, tab, nullptr);
-    s.stats.kernel_launches++; k_init_slots<<<n, 256, 0, s.stream>>>(n, s.d_tab + pl_off, s.d_tab + poff_off, s.d_tab, s.d_hist, s.hist_cap,
+    s.stats.kernel_launches++; launch_pdl(k_init_slots, n, 256, 0, s.stream, n, s.d_tab + pl_off, s.d_tab + poff_off, s.d_tab, s.d_hist, s.hist_cap,
                                           s.d_len, s.d_count, s.d_done, 1);
     std::vector<int> lens(n, len0);
     CK(cudaMemcpyAsync(s.d_len, lens.data(), n * 4, cudaMemcpyHostToDevice, s.stream));
@@ -1885,7 +1912,7 @@ int32_t fb2_forward_last_logits(fb2_session* S, int32_t n_seqs, const int32_t* t
             for (int i = 0; i < n; i++) { tab.push_back(acc); acc += wl[i]; }
             toff += cnt;
             upload_tables(s, tab, nullptr);
-            s.stats.kernel_launches++; k_init_slots<<<n, 256, 0, s.stream>>>(n, s.d_tab + pl_off, s.d_tab + poff_off, s.d_tab + ptok_off,
+            s.stats.kernel_launches++; launch_pdl(k_init_slots, n, 256, 0, s.stream, n, s.d_tab + pl_off, s.d_tab + poff_off, s.d_tab + ptok_off,
                                                   s.d_hist, s.hist_cap, s.d_len, s.d_count, s.d_done, 1);
             for (const ChunkPlan& c : plans) run_prefill_chunk(s, c, s.d_tab);
             CK(cudaGetLastError());
@@ -1928,7 +1955,7 @@ int32_t fb2_teacher_forced_logits(fb2_session* S, int32_t n_seqs, const int32_t*
             const bool mk = mk_eligible(s, n, greedy);
             for (int st = 0; st < steps; st++) {
                 if (st > 0) {
-                    s.stats.kernel_launches++; k_bump_len<<<ceil_div(n, 128), 128, 0, s.stream>>>(n, s.d_len);
+                    s.stats.kernel_launches++; launch_pdl(k_bump_len, ceil_div(n, 128), 128, 0, s.stream, n, s.d_len);
                     if (mk) run_mega(s, n, 1, to_params(greedy), nullptr, nullptr, 1, false);
                     else run_decode_step(s, n);
                 }
@@ -1976,7 +2003,7 @@ int32_t fb2_sample_logits(fb2_session* S, int32_t n, const float* logits, const 
         float* d_l = dalloc<float>((size_t)n * m.V);
         try {
             CK(cudaMemcpyAsync(d_l, logits, (size_t)n * m.V * 4, cudaMemcpyHostToDevice, s.stream));
-            s.stats.kernel_launches++; k_sample_rows<<<n, kSampleThreads, sampler_smem_bytes(m.V), s.stream>>>(
+            s.stats.kernel_launches++; launch_pdl(k_sample_rows, n, kSampleThreads, sampler_smem_bytes(m.V), s.stream, 
                 n, d_l, m.V, s.d_tab, s.d_tab + off_off, s.d_tab + len_off, s.d_uni, to_params(*sp), s.d_tab + ids_off);
             CK(cudaGetLastError());
             CK(cudaMemcpyAsync(out_ids, s.d_tab + ids_off, n * 4, cudaMemcpyDeviceToHost, s.stream));
@@ -2119,15 +2146,15 @@ int32_t fb2_forward_last_logits_noalloc(fb2_model* m, int32_t device_slot, int32
         s.d_hist = const_cast<int*>(device_tokens);
         s.hist_cap = n_tokens;
         s.d_logits = device_logits;
-        k_noalloc_tables<<<1, 256, 0, s.stream>>>(n_tokens, ints, s.d_tickets);
+        launch_pdl(k_noalloc_tables, 1, 256, 0, s.stream, n_tokens, ints, s.d_tickets);
         // the prefill chunk of run_prefill_chunk, for this single window
         const int* row_seq = ints;                    // slot 0 for every row
         const int* row_pos = ints + kNoallocMaxRows;  // positions 0..n-1
         const int4* qblk = reinterpret_cast<const int4*>(ints + 4 * kNoallocMaxRows);
         const int* last_row = ints + 4 * kNoallocMaxRows + 4;
-        k_prefill_hidx<<<1, 256, 0, s.stream>>>(n_tokens, row_seq, row_pos, s.d_len, view.ctx, s.d_row_hidx);
+        launch_pdl(k_prefill_hidx, 1, 256, 0, s.stream, n_tokens, row_seq, row_pos, s.d_len, view.ctx, s.d_row_hidx);
         Rows R{row_seq, row_pos, s.d_row_hidx, s.d_ones};
-        k_embed<<<n_tokens, 128, 0, s.stream>>>(n_tokens, R, s.d_hist, s.hist_cap, dm.tok_emb, dm.pos_emb, view.D,
+        launch_pdl(k_embed, n_tokens, 128, 0, s.stream, n_tokens, R, s.d_hist, s.hist_cap, dm.tok_emb, dm.pos_emb, view.D,
                                                 view.V, s.d_x);
         run_layers(s, n_tokens, R, false, 1, qblk);
         launch_layernorm(s, 1, s.d_x, dm.lnf_w, dm.lnf_b, s.d_lnf, last_row);

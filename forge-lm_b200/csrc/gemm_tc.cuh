@@ -158,6 +158,7 @@ FB2_DEV void tf32_split(float x, float& hi, float& lo) {
 // W [K][N] -> W^T halves hiT, loT [N][K] (32 x 32 tiles through shared memory).
 __global__ void k_split_tf32_transpose(const float* __restrict__ W, int K, int N, float* __restrict__ hiT,
                                        float* __restrict__ loT) {
+    pdl_wait();
     __shared__ float t[32][33];
     const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
     for (int r = threadIdx.y; r < 32; r += blockDim.y) {
@@ -178,6 +179,7 @@ __global__ void k_split_tf32_transpose(const float* __restrict__ W, int K, int N
 
 // x -> (hi, lo) TF32 halves.
 __global__ void k_split_tf32(const float4* __restrict__ x, size_t n4, float4* __restrict__ hi, float4* __restrict__ lo) {
+    pdl_wait();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
         const float4 v = x[i];
         float4 h, l;
@@ -224,6 +226,7 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(const __grid_constant__ TcMa
     __syncthreads();
     tc::fence_after();
     const uint32_t tmem = tmem_base;
+    pdl_wait();  // barriers and tensor memory set up; global memory from here on
 
     if (warp == 0 && lane == 0) {
         // ---- producer ----
@@ -366,6 +369,7 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc_swab(const __grid_constant__
     __syncthreads();
     tc::fence_after();
     const uint32_t tmem = tmem_base;
+    pdl_wait();  // barriers and tensor memory set up; global memory from here on
 
     if (warp == 0 && lane == 0) {
         for (int i = 0; i < nk; i++) {
@@ -449,6 +453,7 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc_swab(const __grid_constant__
 
 // y[m][n..n+3] = epilogue(sum over z = 0..S-1 of partial[z][m][n..n+3]).
 __global__ void k_splitk_reduce(const float* __restrict__ partial, int S, int M, int N, Epi e) {
+    pdl_wait();
     const int n4 = N / 4;
     const size_t total = (size_t)M * n4;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {

@@ -29,6 +29,7 @@ struct Rows {
 // the host instead (Sampler.cs:93-94), so it is inactive here.
 __global__ void k_step_prepare(int n, const int* __restrict__ len, const int* __restrict__ done, int ctx,
                                int* row_seq, int* row_pos, int* row_hidx, int* row_active) {
+    pdl_wait();
     int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= n) return;
     int L = len[r];
@@ -43,6 +44,7 @@ __global__ void k_step_prepare(int n, const int* __restrict__ len, const int* __
 __global__ void k_embed(int rows, Rows R, const int* __restrict__ hist, int hist_stride,
                         const float* __restrict__ tok_emb, const float* __restrict__ pos_emb, int D, int V,
                         float* __restrict__ x) {
+    pdl_wait();
     int r = blockIdx.x;
     if (r >= rows) return;
     int s = R.seq[r];
@@ -65,6 +67,7 @@ __global__ void k_embed(int rows, Rows R, const int* __restrict__ hist, int hist
 template <int PER_LANE>
 __global__ void k_layernorm(int rows, int D, const float* __restrict__ x, const float* __restrict__ w,
                             const float* __restrict__ b, float* __restrict__ y, const int* __restrict__ row_map) {
+    pdl_wait();
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
     if (warp >= rows) return;
@@ -183,6 +186,7 @@ template <int MR, class WL = WF32>
 __global__ void __launch_bounds__(256) k_gemv(int M, int K, int N, int kchunk, const float* __restrict__ A,
                                               const typename WL::T* __restrict__ W, float* __restrict__ partial,
                                               unsigned int* __restrict__ tickets, Epi e) {
+    pdl_wait();
     extern __shared__ float smem[];
     float* As = smem;                     // [MR][kchunk]
     float* red = smem + MR * kchunk;      // [16][MR][64]
@@ -289,6 +293,7 @@ __global__ void __launch_bounds__(256) k_gemv(int M, int K, int N, int kchunk, c
 template <int BM>
 __global__ void __launch_bounds__(256) k_gemm_tiled(int M, int K, int N, const float* __restrict__ A,
                                                     const float* __restrict__ W, Epi e) {
+    pdl_wait();
     constexpr int BN = 128, BK = 16, TM = BM / 16;
     __shared__ __align__(16) float As[BK][BM + 4];
     __shared__ __align__(16) float Bs[BK][BN + 4];
@@ -366,6 +371,7 @@ template <int HD>
 __global__ void __launch_bounds__(128) k_attn_decode_partial(const float* __restrict__ q, const float* __restrict__ kv_layer,
                                                              long long kv_slot_stride, long long v_offset, int H, int ctx,
                                                              float scale, Rows R, float* __restrict__ part, int nsplit) {
+    pdl_wait();
     constexpr int LPK = HD / 4;        // lanes per key
     constexpr int KPW = 32 / LPK;      // keys per warp iteration
     const int r = blockIdx.x, h = blockIdx.y, sp = blockIdx.z;
@@ -439,6 +445,7 @@ __global__ void __launch_bounds__(128) k_attn_decode_partial(const float* __rest
 template <int HD>
 __global__ void k_attn_decode_combine(const float* __restrict__ part, int H, int nsplit, Rows R,
                                       float* __restrict__ ctx_out) {
+    pdl_wait();
     const int r = blockIdx.x, h = blockIdx.y;
     const int D = H * HD;
     float* o = ctx_out + (size_t)r * D + h * HD;
@@ -472,6 +479,7 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const float* __restrict__ 
                                                       long long kv_slot_stride, long long v_offset, int H, int ctx,
                                                       float scale, const int4* __restrict__ qblk,
                                                       float* __restrict__ ctx_out) {
+    pdl_wait();
     constexpr int BQ = 64, BK = 64, DPT = (HD + 3) / 4;  // dims per thread
     extern __shared__ float sm[];
     float* Qs = sm;                          // [BQ][HD+1]
@@ -568,6 +576,7 @@ __global__ void __launch_bounds__(256) k_attn_prefill_rt(const float* __restrict
                                                          long long kv_slot_stride, long long v_offset, int H, int ctx,
                                                          float scale, const int4* __restrict__ qblk,
                                                          float* __restrict__ ctx_out) {
+    pdl_wait();
     constexpr int BQ = 64, BK = 64, LD = HD + 4, LP = BK + 4, DPT = HD / 16;
     static_assert(HD % 16 == 0 && HD <= 128, "head dim");
     extern __shared__ __align__(16) float sm[];
@@ -699,6 +708,7 @@ template <int MR, class WL = WF32>
 __global__ void __launch_bounds__(256) k_head(int M, int D, int V, const float* __restrict__ xln,
                                               const typename WL::T* __restrict__ E, float* __restrict__ logits,
                                               int logits_stride) {
+    pdl_wait();
     extern __shared__ float xs[];  // [MR][D]
     for (int i = threadIdx.x; i < MR * D; i += blockDim.x) {
         int m = i / D;

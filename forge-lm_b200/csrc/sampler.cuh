@@ -305,6 +305,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample_step(
     int n, const float* __restrict__ logits, int V, int ctx, int* __restrict__ hist, int hist_stride,
     int* __restrict__ len, int* __restrict__ count, int* __restrict__ done, const double* __restrict__ uniforms,
     int uni_stride, SampleParams sp, int* __restrict__ out_tokens, int out_stride) {
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int s = blockIdx.x;
     if (s >= n) return;
@@ -332,6 +333,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample_rows(int n, const flo
                                                                 const int* __restrict__ win_len,
                                                                 const double* __restrict__ uniforms, SampleParams sp,
                                                                 int* __restrict__ out_ids) {
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int r = blockIdx.x;
     if (r >= n) return;
@@ -342,6 +344,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample_rows(int n, const flo
 
 // Test hook: device expf_libm over an array (compared with the host libm).
 __global__ void k_expf_libm(const float* __restrict__ x, float* __restrict__ y, long long n) {
+    pdl_wait();
     long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = expf_libm(x[i]);
 }
@@ -349,6 +352,7 @@ __global__ void k_expf_libm(const float* __restrict__ x, float* __restrict__ y, 
 // Test hook: exhaustive range check.  For each chunk of 2^20 consecutive
 // float bit patterns starting at lo_bits, a 64-bit hash of the outputs.
 __global__ void k_expf_libm_hash(uint32_t lo_bits, int nchunks, unsigned long long* __restrict__ hashes) {
+    pdl_wait();
     const int chunk = blockIdx.x;
     if (chunk >= nchunks) return;
     unsigned long long h = 0;
