@@ -330,6 +330,30 @@ def test_chat_turns_reuse_the_cached_prefix(pkg, O):
                                                                  O.DotNetRandom(9)))
 
 
+def test_in_process_sharding_over_two_devices(pkg, O):
+    """One model on two GPUs (fb2_model_create with a devices list): the
+    sequences of a batch split over the devices' sessions, one host thread
+    per device, no collective; ids and logits as on one device."""
+    if pkg.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    shape = (2256, 96, 128, 2, 4)
+    ocfg = O.Config(*shape)
+    params = O.init_params(ocfg, 5)
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, shape[0], L).astype(np.int32) for L in (9, 30, 17, 44, 5)]
+    seeds = [11, 12, 13, 14, 15]
+    with pkg.B200Backend(pkg.ModelConfig(*shape), params, devices=[0, 1], max_seqs=5) as be:
+        assert be.stats()["device_count"] == 2
+        got = be.generate_batch([p.tolist() for p in prompts], 16, 0.7, 30, seeds=seeds, repetition_penalty=1.1,
+                                no_repeat_ngram_size=3)
+        lg = be.forward_last_batch([p.tolist() for p in prompts])
+    for i, p in enumerate(prompts):
+        want = O.generate(ocfg, params, p, 16, 0.7, 30, O.DotNetRandom(seeds[i]), repetition_penalty=1.1,
+                          no_repeat_ngram=3)
+        check_ids(O, ocfg, params, p, got[i], want)
+        assert relerr(lg[i], O.forward_last(ocfg, params, p)) <= TOL
+
+
 def test_generate_batch_ragged_and_long_prompts(pkg, O):
     shape = (300, 24, 32, 2, 2)
     ocfg, params, be = make(pkg, O, shape, 9, max_seqs=5)
