@@ -27,7 +27,7 @@ from .dotnet_random import DotNetRandom
 
 __all__ = ["ModelConfig", "B200Backend", "Sampler", "DotNetRandom", "ArgumentError", "NativeError",
            "InvalidDataError", "param_names", "param_shapes", "init_params", "device_count", "library_path",
-           "read_forgemodel_header", "write_forgemodel"]
+           "read_forgemodel_header", "write_forgemodel", "BpeTokenizer"]
 
 
 def library_path() -> str:
@@ -405,3 +405,69 @@ class Sampler:
             raise ArgumentError(N.FB2_INVALID_ARG, "Temperature must be finite.")
         u = [rng.next_double()] if temperature > 0 else None
         return int(model.sample_logits(lg, [[]], temperature, top_k, u)[0])
+
+
+class BpeTokenizer:
+    """The byte-level BPE tokenizer (src/LLM.Core/Tokenizer/BpeTokenizer.cs)
+    in the library: load (BpeTokenizer.Load's checks; InvalidDataError where
+    it throws InvalidDataException), Encode, EncodeDocument, Decode, and a
+    UTF-8 stream decoder for tokens printed as they are generated."""
+
+    def __init__(self, path: str):
+        self._t = C.c_void_p()
+        N.check(N.load().fb2_tokenizer_load(str(path).encode(), C.byref(self._t)))
+        vs, eos = C.c_int32(), C.c_int32()
+        N.check(N.load().fb2_tokenizer_info(self._t, C.byref(vs), C.byref(eos)))
+        self.vocab_size, self.eos_token_id = vs.value, eos.value
+
+    def close(self) -> None:
+        if getattr(self, "_t", None):
+            N.load().fb2_tokenizer_destroy(self._t)
+            self._t = None
+
+    def __del__(self):
+        self.close()
+
+    def encode(self, data: str | bytes) -> list[int]:
+        b = data.encode("utf-8") if isinstance(data, str) else bytes(data)
+        buf = np.frombuffer(b, np.uint8) if b else np.zeros(1, np.uint8)
+        out = np.empty(max(len(b), 1), np.int32)
+        n = C.c_int64()
+        N.check(N.load().fb2_tokenizer_encode(self._t, buf.ctypes.data, len(b), out.ctypes.data, out.size,
+                                              C.byref(n)))
+        return out[:n.value].tolist()
+
+    def encode_document(self, data: str | bytes) -> list[int]:
+        """EncodeDocument (BpeTokenizer.cs:244-251): the text, then EOS."""
+        return self.encode(data) + [self.eos_token_id]
+
+    def decode_bytes(self, ids: Sequence[int]) -> bytes:
+        a = _i32(list(ids)) if len(ids) else np.zeros(1, np.int32)
+        n = C.c_int64()
+        L = N.load()
+        st = L.fb2_tokenizer_decode(self._t, a.ctypes.data, len(ids), None, 0, C.byref(n))
+        if st != N.FB2_OK and n.value == 0:
+            N.check(st)
+        out = np.empty(max(n.value, 1), np.uint8)
+        N.check(L.fb2_tokenizer_decode(self._t, a.ctypes.data, len(ids), out.ctypes.data, out.size, C.byref(n)))
+        return out[:n.value].tobytes()
+
+    def decode(self, ids: Sequence[int]) -> str:
+        """Decode (BpeTokenizer.cs:320-339): UTF-8 with replacement characters."""
+        return self.decode_bytes(ids).decode("utf-8", errors="replace")
+
+    def stream_decoder(self):
+        """Utf8StreamDecoder (BpeTokenizer.cs:57-78): keeps incomplete UTF-8
+        sequences until later tokens complete them."""
+        import codecs
+        dec = codecs.getincrementaldecoder("utf-8")("replace")
+        tok = self
+
+        class _Stream:
+            def decode_token(self, token_id: int) -> str:
+                return dec.decode(tok.decode_bytes([token_id]))
+
+            def flush(self) -> str:
+                return dec.decode(b"", final=True)
+
+        return _Stream()

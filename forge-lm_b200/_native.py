@@ -34,6 +34,8 @@ EXPORTED = [
     "fb2_generate", "fb2_generate_device", "fb2_forward_last_logits", "fb2_teacher_forced_logits",
     "fb2_sample_logits", "fb2_forward_last_logits_noalloc", "fb2_init_params", "fb2_stats", "fb2_stats_reset",
     "fb2_forgemodel_read_header", "fb2_model_load_forgemodel", "fb2_forgemodel_write",
+    "fb2_tokenizer_load", "fb2_tokenizer_destroy", "fb2_tokenizer_info", "fb2_tokenizer_encode",
+    "fb2_tokenizer_decode",
 ]
 TEST_EXPORTED = ["fb2_test_expf", "fb2_test_expf_hash", "fb2_test_dotnet_random", "fb2_test_mk_trace",
                  "fb2_test_gemm_tc", "fb2_test_sha256"]
@@ -115,6 +117,12 @@ def load(path: str | None = None):
     L.fb2_forgemodel_read_header.argtypes = [C.c_char_p, C.POINTER(ModelDesc), C.c_char_p, i32]
     L.fb2_model_load_forgemodel.argtypes = [C.c_char_p, i32, i32p, i32, C.POINTER(ModelDesc), C.POINTER(vp)]
     L.fb2_forgemodel_write.argtypes = [C.c_char_p, C.POINTER(ModelDesc), C.c_char_p, C.POINTER(vp), i32]
+    L.fb2_tokenizer_load.argtypes = [C.c_char_p, C.POINTER(vp)]
+    L.fb2_tokenizer_destroy.argtypes = [vp]
+    L.fb2_tokenizer_destroy.restype = None
+    L.fb2_tokenizer_info.argtypes = [vp, C.POINTER(i32), C.POINTER(i32)]
+    L.fb2_tokenizer_encode.argtypes = [vp, vp, i64, vp, i64, C.POINTER(i64)]
+    L.fb2_tokenizer_decode.argtypes = [vp, vp, i64, vp, i64, C.POINTER(i64)]
     for name in EXPORTED + TEST_EXPORTED:
         fn = getattr(L, name)
         if fn.restype is C.c_int:  # default

@@ -32,6 +32,7 @@
 #include "decode_mega.cuh"
 #include "gemm_tc.cuh"
 #include "forgemodel.hpp"
+#include "tokenizer.hpp"
 
 #include <cudaTypedefs.h>
 
@@ -2246,6 +2247,63 @@ int32_t fb2_forgemodel_write(const char* path, const fb2_model_desc* desc, const
             if (!std::isspace((unsigned char)c)) blank = false;
         if (blank) fail(FB2_INVALID_ARG, "a checkpoint needs a model name");
         fb2::fm::write_file(path, h, params, n_params);
+    });
+}
+
+// ---- tokenizer ------------------------------------------------------------------
+struct fb2_tokenizer {
+    fb2::tok::Bpe bpe;
+};
+
+int32_t fb2_tokenizer_load(const char* path, fb2_tokenizer** out) {
+    return guarded([&] {
+        if (!path || !out) fail(FB2_INVALID_ARG, "NULL argument");
+        *out = nullptr;
+        auto t = std::make_unique<fb2_tokenizer>();
+        t->bpe = fb2::tok::Bpe::load(path);
+        *out = t.release();
+    });
+}
+
+void fb2_tokenizer_destroy(fb2_tokenizer* t) { delete t; }
+
+int32_t fb2_tokenizer_info(const fb2_tokenizer* t, int32_t* vocab_size, int32_t* eos_id) {
+    return guarded([&] {
+        if (!t) fail(FB2_INVALID_ARG, "NULL argument");
+        if (vocab_size) *vocab_size = (int32_t)t->bpe.vocab.size();
+        if (eos_id) *eos_id = t->bpe.eos;
+    });
+}
+
+int32_t fb2_tokenizer_encode(const fb2_tokenizer* t, const uint8_t* bytes, int64_t n_bytes, int32_t* ids,
+                             int64_t capacity, int64_t* n_ids) {
+    return guarded([&] {
+        if (!t || !n_ids || (n_bytes > 0 && !bytes) || n_bytes < 0) fail(FB2_INVALID_ARG, "bad arguments");
+        const std::vector<int32_t> v = t->bpe.encode(bytes, (size_t)n_bytes);
+        *n_ids = (int64_t)v.size();
+        if ((int64_t)v.size() > capacity || (!ids && !v.empty())) fail(FB2_INVALID_ARG, "ids buffer too small");
+        if (!v.empty()) std::memcpy(ids, v.data(), v.size() * sizeof(int32_t));
+    });
+}
+
+int32_t fb2_tokenizer_decode(const fb2_tokenizer* t, const int32_t* ids, int64_t n_ids, uint8_t* bytes,
+                             int64_t capacity, int64_t* n_bytes) {
+    return guarded([&] {
+        if (!t || !n_bytes || (n_ids > 0 && !ids) || n_ids < 0) fail(FB2_INVALID_ARG, "bad arguments");
+        int64_t total = 0;
+        for (int64_t i = 0; i < n_ids; i++) {
+            if (ids[i] < 0 || ids[i] >= (int32_t)t->bpe.vocab.size())
+                fail(FB2_INVALID_ARG, "token id " + std::to_string(ids[i]) + " is outside the vocabulary");
+            total += (int64_t)t->bpe.vocab[(size_t)ids[i]].size();
+        }
+        *n_bytes = total;
+        if (total > capacity || (!bytes && total)) fail(FB2_INVALID_ARG, "bytes buffer too small");
+        int64_t at = 0;
+        for (int64_t i = 0; i < n_ids; i++) {
+            const std::vector<uint8_t>& b = t->bpe.vocab[(size_t)ids[i]];
+            if (!b.empty()) std::memcpy(bytes + at, b.data(), b.size());
+            at += (int64_t)b.size();
+        }
     });
 }
 

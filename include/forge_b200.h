@@ -259,6 +259,27 @@ int32_t fb2_model_load_forgemodel(const char* path, int32_t weight_dtype, const 
 int32_t fb2_forgemodel_write(const char* path, const fb2_model_desc* desc, const char* model_name,
                              const float* const* params, int32_t n_params);
 
+/* ---- Byte-level BPE tokenizer (src/LLM.Core/Tokenizer/BpeTokenizer.cs) --------
+ * Host only (no device).  fb2_tokenizer_load reads the JSON BpeTokenizer.Save
+ * writes and applies BpeTokenizer.Load's checks (BpeTokenizer.cs:353-389):
+ * FB2_INVALID_DATA where it throws InvalidDataException. */
+typedef struct fb2_tokenizer fb2_tokenizer;
+int32_t fb2_tokenizer_load(const char* path, fb2_tokenizer** out);
+void fb2_tokenizer_destroy(fb2_tokenizer* t);
+/* VocabSize (bytes + merges + EOS) and EosTokenId. */
+int32_t fb2_tokenizer_info(const fb2_tokenizer* t, int32_t* vocab_size, int32_t* eos_id);
+/* BpeTokenizer.Encode(ReadOnlySpan<byte>) (BpeTokenizer.cs:259-318): *n_ids
+ * receives the count; FB2_INVALID_ARG when it exceeds capacity (ids then
+ * untouched). */
+int32_t fb2_tokenizer_encode(const fb2_tokenizer* t, const uint8_t* bytes, int64_t n_bytes, int32_t* ids,
+                             int64_t capacity, int64_t* n_ids);
+/* The bytes BpeTokenizer.Decode concatenates before its UTF-8 conversion
+ * (BpeTokenizer.cs:320-339; the EOS token adds none).  An id outside the
+ * vocabulary is FB2_INVALID_ARG (ArgumentOutOfRangeException); *n_bytes as
+ * in fb2_tokenizer_encode. */
+int32_t fb2_tokenizer_decode(const fb2_tokenizer* t, const int32_t* ids, int64_t n_ids, uint8_t* bytes,
+                             int64_t capacity, int64_t* n_bytes);
+
 #ifdef __cplusplus
 }
 #endif
