@@ -614,7 +614,8 @@ static bool launch_gemm_tc(cudaStream_t st, int sm_count, int M, int K, int N, c
         if (!tc_encode(&maps.a_hi, ahi, K, M, TC_BM) || !tc_encode(&maps.a_lo, alo, K, M, TC_BM))
             fail(FB2_CUDA_ERROR, "cuTensorMapEncodeTiled failed for a GEMM operand");
         (*launches)++;
-        launch_pdl(k_gemm_tc<128>, dim3(ceil_div(N, 128), ceil_div(M, TC_BM)), 128, TcCfg<128>::SMEM, st, maps, M, N, K, e, err);
+        const int tiles = ceil_div(N, 128) * ceil_div(M, TC_BM);
+        launch_pdl(k_gemm_tc<128>, std::min(tiles, sm_count), TCP_THREADS, TcCfg<128>::SMEM, st, maps, M, N, K, e, err);
         return true;
     }
     const int bnb = M <= 64 ? 64 : 128;

@@ -38,7 +38,7 @@ namespace fb2 {
 constexpr int TC_BM = 128, TC_BK = 32;
 constexpr int TC_TILE_A = TC_BM * TC_BK * 4;  // 16 KB: 128 rows x 32 fp32
 
-// Tile shape of the prefill GEMM (one CTA per 128 x BN output tile).
+// Tile shape and ring of the prefill GEMM.
 template <int BN>
 struct TcCfg {
     static constexpr int TILE_B = BN * TC_BK * 4;
@@ -192,19 +192,29 @@ __global__ void k_split_tf32(const float4* __restrict__ x, size_t n4, float4* __
     }
 }
 
-// gridDim = (ceil(N/BN), ceil(M/128)).
+// Persistent, warp-specialized: one CTA per SM walks the 128 x BN output
+// tiles t = blockIdx.x, += gridDim.x (row-major over N, so neighbouring CTAs
+// share A rows in L2).  Warp 0 lane 0 feeds the smem ring with TMA for tile
+// after tile; warp 1 lane 0 issues the MMAs into one of two TMEM
+// accumulators (2 x BN columns), so warps 2-5 can drain tile i (tcgen05.ld
+// of their TMEM lane quarter, the fused epilogue) while tile i+1 accumulates.
+// Barriers: full/empty per ring stage; tfull[a] (MMA commit: accumulator a
+// holds a finished tile) and tempty[a] (the 4 epilogue warps drained it).
+constexpr int TCP_THREADS = 192;
+
 template <int BN>
-__global__ void __launch_bounds__(128, 1) k_gemm_tc(const __grid_constant__ TcMaps maps, int M, int N, int K, Epi e,
-                                                    int* err) {
+__global__ void __launch_bounds__(TCP_THREADS, 1) k_gemm_tc(const __grid_constant__ TcMaps maps, int M, int N, int K,
+                                                            Epi e, int* err) {
     using Cfg = TcCfg<BN>;
     constexpr int STAGES = Cfg::STAGES, STAGE = Cfg::STAGE, TILE_B = Cfg::TILE_B;
+    constexpr uint32_t TCOLS = 2 * BN;  // two accumulators
     extern __shared__ unsigned char tc_smem_raw[];
-    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], accb;
+    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2], drain;
     __shared__ uint32_t tmem_base;
     __shared__ volatile int s_abort;
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int m0 = blockIdx.y * TC_BM, n0 = blockIdx.x * BN;
+    const int tiles_n = (N + BN - 1) / BN, tiles_m = (M + TC_BM - 1) / TC_BM, ntiles = tiles_n * tiles_m;
     const int nk = (K + TC_BK - 1) / TC_BK;
 
     if (tid == 0) {
@@ -213,12 +223,16 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(const __grid_constant__ TcMa
             tc::bar_init(&full[i], 1);
             tc::bar_init(&empty[i], 1);
         }
-        tc::bar_init(&accb, 1);
+        for (int i = 0; i < 2; i++) {
+            tc::bar_init(&tfull[i], 1);
+            tc::bar_init(&tempty[i], 4);
+        }
+        tc::bar_init(&drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc::smem_addr(&tmem_base)),
-                     "r"((uint32_t)Cfg::TMEM_COLS)
+                     "r"(TCOLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -229,91 +243,105 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(const __grid_constant__ TcMa
     pdl_wait();  // barriers and tensor memory set up; global memory from here on
 
     if (warp == 0 && lane == 0) {
-        // ---- producer ----
-        for (int i = 0; i < nk; i++) {
-            const int st = i % STAGES;
-            if (i >= STAGES && !tc::bar_wait(&empty[st], ((i / STAGES) - 1) & 1, &s_abort)) break;
-            unsigned char* sb = sm + (size_t)st * STAGE;
-            tc::bar_expect_tx(&full[st], STAGE);
-            const int k0 = i * TC_BK;
-            tc::tma_load_2d(sb, &maps.a_hi, k0, m0, &full[st]);
-            tc::tma_load_2d(sb + TC_TILE_A, &maps.a_lo, k0, m0, &full[st]);
-            tc::tma_load_2d(sb + 2 * TC_TILE_A, &maps.b_hi, k0, n0, &full[st]);
-            tc::tma_load_2d(sb + 2 * TC_TILE_A + TILE_B, &maps.b_lo, k0, n0, &full[st]);
+        // ---- TMA producer ----
+        uint32_t it = 0;
+        for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x) {
+            const int m0 = (t / tiles_n) * TC_BM, n0 = (t % tiles_n) * BN;
+            for (int kb = 0; kb < nk; kb++, it++) {
+                const int st = it % STAGES;
+                if (it >= (uint32_t)STAGES && !tc::bar_wait(&empty[st], ((it / STAGES) - 1) & 1, &s_abort)) break;
+                unsigned char* sb = sm + (size_t)st * STAGE;
+                tc::bar_expect_tx(&full[st], STAGE);
+                const int k0 = kb * TC_BK;
+                tc::tma_load_2d(sb, &maps.a_hi, k0, m0, &full[st]);
+                tc::tma_load_2d(sb + TC_TILE_A, &maps.a_lo, k0, m0, &full[st]);
+                tc::tma_load_2d(sb + 2 * TC_TILE_A, &maps.b_hi, k0, n0, &full[st]);
+                tc::tma_load_2d(sb + 2 * TC_TILE_A + TILE_B, &maps.b_lo, k0, n0, &full[st]);
+            }
         }
+        // copies still landing (after an abort): wait for each stage's latest fill
+        if (s_abort)
+            for (uint32_t j = it > (uint32_t)STAGES ? it - STAGES : 0; j < it; j++) {
+                const unsigned long long t0 = tc::now_ns();
+                while (!tc::bar_try(&full[j % STAGES], (j / STAGES) & 1) && tc::now_ns() - t0 < kTcTimeoutNs / 4) {
+                }
+            }
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer ----
         constexpr uint32_t idesc = tc::idesc_tf32(TC_BM, BN);
-        for (int i = 0; i < nk; i++) {
-            const int st = i % STAGES;
-            if (!tc::bar_wait(&full[st], (i / STAGES) & 1, &s_abort)) break;
+        uint32_t it = 0, local = 0;
+        for (int t = blockIdx.x; t < ntiles && !s_abort; t += gridDim.x, local++) {
+            const uint32_t acc = local & 1;
+            if (local >= 2 && !tc::bar_wait(&tempty[acc], ((local / 2) - 1) & 1, &s_abort)) break;
             tc::fence_after();
-            const uint32_t sa = tc::smem_addr(sm + (size_t)st * STAGE);
-            const uint32_t a_hi = sa, a_lo = sa + TC_TILE_A, b_hi = sa + 2 * TC_TILE_A, b_lo = b_hi + TILE_B;
+            const uint32_t d = tmem + acc * BN;
+            bool ok = true;
+            for (int kb = 0; kb < nk; kb++, it++) {
+                const int st = it % STAGES;
+                if (!tc::bar_wait(&full[st], (it / STAGES) & 1, &s_abort)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after();
+                const uint32_t sa = tc::smem_addr(sm + (size_t)st * STAGE);
+                const uint32_t a_hi = sa, a_lo = sa + TC_TILE_A, b_hi = sa + 2 * TC_TILE_A, b_lo = b_hi + TILE_B;
 #pragma unroll
-            for (int ks = 0; ks < TC_BK / 8; ks++) {
-                // K-major rows of 128 B, 8-row swizzle atoms 1024 B apart;
-                // a k-step (8 TF32) is 32 B along the rows
-                const uint64_t dah = tc::sw128_desc(a_hi + ks * 32, 16, 1024);
-                const uint64_t dal = tc::sw128_desc(a_lo + ks * 32, 16, 1024);
-                const uint64_t dbh = tc::sw128_desc(b_hi + ks * 32, 16, 1024);
-                const uint64_t dbl = tc::sw128_desc(b_lo + ks * 32, 16, 1024);
-                tc::mma_tf32(tmem, dah, dbh, idesc, (i | ks) != 0);
-                tc::mma_tf32(tmem, dah, dbl, idesc, 1u);
-                tc::mma_tf32(tmem, dal, dbh, idesc, 1u);
+                for (int ks = 0; ks < TC_BK / 8; ks++) {
+                    const uint64_t dah = tc::sw128_desc(a_hi + ks * 32, 16, 1024);
+                    const uint64_t dal = tc::sw128_desc(a_lo + ks * 32, 16, 1024);
+                    const uint64_t dbh = tc::sw128_desc(b_hi + ks * 32, 16, 1024);
+                    const uint64_t dbl = tc::sw128_desc(b_lo + ks * 32, 16, 1024);
+                    tc::mma_tf32(d, dah, dbh, idesc, (kb | ks) != 0);
+                    tc::mma_tf32(d, dah, dbl, idesc, 1u);
+                    tc::mma_tf32(d, dal, dbh, idesc, 1u);
+                }
+                tc::mma_commit(&empty[st]);
             }
-            tc::mma_commit(&empty[st]);
+            if (!ok) break;
+            tc::mma_commit(&tfull[acc]);
         }
-        tc::mma_commit(&accb);  // fires once every MMA issued above has completed
-    }
-    __syncwarp();
-
-    // ---- epilogue: thread (warp w, lane i) owns accumulator row 32w + i ----
-    // The issuer always commits `accb`, after an abort too, so this wait
-    // (bounded, not cut short by the abort flag) also drains the MMAs in
-    // flight before the accumulator is freed.
-    bool ok = tc::bar_try(&accb, 0);
-    if (!ok) {
+        // every MMA issued above completes before the accumulators are freed
+        tc::mma_commit(&drain);
         const unsigned long long t0 = tc::now_ns();
-        while (!(ok = tc::bar_try(&accb, 0)) && tc::now_ns() - t0 < kTcTimeoutNs) {
+        while (!tc::bar_try(&drain, 0) && tc::now_ns() - t0 < kTcTimeoutNs) {
         }
-        if (!ok) s_abort = 1;
-    }
-    __syncwarp();
-    tc::fence_after();
-    const int row = m0 + warp * 32 + lane;
-    if (ok && !s_abort && nk > 0) {
+    } else if (warp >= 2) {
+        // ---- epilogue: TMEM lane quarter q = warp % 4 (rows 32q .. 32q+31 of the tile) ----
+        const int q = warp & 3;
+        uint32_t local = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, local++) {
+            // warp-uniform decisions: tcgen05.ld below needs the whole warp
+            if (__any_sync(0xffffffffu, s_abort != 0)) break;
+            const uint32_t acc = local & 1;
+            const bool ok = tc::bar_wait(&tfull[acc], (local / 2) & 1, &s_abort);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc::fence_after();
+            const int m0 = (t / tiles_n) * TC_BM, n0 = (t % tiles_n) * BN;
+            const int row = m0 + q * 32 + lane;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-            float v[16];
-            tc::tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
-            if (row < M) {
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                float v[16];
+                tc::tmem_ld16(tmem + acc * BN + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+                if (row < M) {
 #pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const int n = n0 + c0 + 4 * q;
-                    if (n >= N) continue;
-                    epi_store4(e, row, n, N, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+                    for (int k4 = 0; k4 < 4; k4++) {
+                        const int n = n0 + c0 + 4 * k4;
+                        if (n < N) epi_store4(e, row, n, N, make_float4(v[4 * k4], v[4 * k4 + 1], v[4 * k4 + 2], v[4 * k4 + 3]));
+                    }
                 }
             }
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_addr(&tempty[acc])) : "memory");
         }
     }
-    if (s_abort && tid == 0) {
-        atomicExch(err, TC_ERR_TIMEOUT);
-        // copies the issuer never consumed may still be landing: wait for
-        // every stage's latest fill (bounded) before the CTA's memory goes
-        for (int st = 0; st < STAGES && st < nk; st++) {
-            const int last = st + ((nk - 1 - st) / STAGES) * STAGES;  // last k block using stage st
-            const unsigned long long t0 = tc::now_ns();
-            while (!tc::bar_try(&full[st], (last / STAGES) & 1) && tc::now_ns() - t0 < kTcTimeoutNs / 4) {
-            }
-        }
-    }
+    __syncwarp();
+    if (s_abort && tid == 0) atomicExch(err, TC_ERR_TIMEOUT);
     tc::fence_before();
     __syncthreads();
     if (warp == 0) {
         tc::fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)Cfg::TMEM_COLS)
-                     : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
     }
 }
 
