@@ -162,6 +162,9 @@ struct DeviceModel {
     unsigned short* blob16 = nullptr;
     std::unordered_map<const float*, const unsigned short*> w16;
     std::vector<std::array<CUtensorMap, 8>> tc_maps;  // per layer: {hi, lo} x 4 matrices (W^T, 128-row boxes)
+    // the tied head: tok_emb [V][D] is already W^T of logits = x * tok_emb^T
+    CUtensorMap tc_head_maps[2];
+    float* tc_head_blob = nullptr;  // tok_emb hi, lo halves, then V zeros (the head has no bias)
 };
 
 struct fb2_model {
@@ -347,6 +350,15 @@ static void tc_setup(const fb2_model& m, DeviceModel& dm) {
                 return;
             at += 2 * n;
         }
+    }
+    {
+        const size_t nv = (size_t)m.V * D;
+        dm.tc_head_blob = dalloc<float>(2 * nv + (size_t)m.V);
+        launch_split_tf32(0, dm.tok_emb, nv, dm.tc_head_blob, dm.tc_head_blob + nv);
+        CK(cudaMemset(dm.tc_head_blob + 2 * nv, 0, (size_t)m.V * 4));
+        if (!tc_encode(&dm.tc_head_maps[0], dm.tc_head_blob, D, m.V, 128) ||
+            !tc_encode(&dm.tc_head_maps[1], dm.tc_head_blob + nv, D, m.V, 128))
+            return;
     }
     CK(cudaDeviceSynchronize());
     dm.tc_ok = true;
@@ -750,6 +762,13 @@ static void launch_head(DeviceSession& s, int M, const float* xln, const int* ou
                         float* logits_base) {
     (void)out_slot_host_unused;
     const fb2_model& m = *s.model;
+    // batches of rows: one pass over tok_emb on the tensor cores
+    if (M > kMaxGemvRows && s.dm->tc_ok && !s.dm->bf16 && s.d_ahi) {
+        Epi e = make_epi(EPI_BIAS, s.dm->tc_head_blob + 2 * (size_t)m.V * m.D, nullptr, logits_base);
+        if (launch_gemm_tc(s.stream, s.dm->sm_count, M, m.D, m.V, xln, s.d_ahi, s.d_alo, s.dm->tc_head_maps, e,
+                           s.d_tc_err, s.d_tc_part, s.tc_part_cap, &s.stats.kernel_launches))
+            return;
+    }
     int blocks = std::min(ceil_div(m.V, 8), 8 * s.dm->sm_count);
     for (int m0 = 0; m0 < M; m0 += kMaxGemvRows) {
         int mm = std::min(kMaxGemvRows, M - m0);
@@ -1593,6 +1612,7 @@ int32_t fb2_model_create(const fb2_model_desc* desc, const float* const* params,
                 dfree(dm.relaid);
                 dfree(dm.d_mk_layers);
                 dfree(dm.tc_blob);
+                dfree(dm.tc_head_blob);
                 dfree(dm.blob16);
             }
             delete m;
@@ -1610,6 +1630,7 @@ void fb2_model_destroy(fb2_model* m) {
         dfree(dm.relaid);
         dfree(dm.d_mk_layers);
         dfree(dm.tc_blob);
+        dfree(dm.tc_head_blob);
         dfree(dm.blob16);
     }
     delete m;

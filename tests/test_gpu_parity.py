@@ -354,6 +354,22 @@ def test_in_process_sharding_over_two_devices(pkg, O):
         assert relerr(lg[i], O.forward_last(ocfg, params, p)) <= TOL
 
 
+def test_batched_head_and_decode_24_sequences(pkg, O):
+    """More than 16 rows reach the head: the tied head runs as one
+    tensor-core pass over tok_emb (prefill slots and decode batch), the
+    projections as the swapped-operand GEMM."""
+    shape = (2256, 64, 128, 2, 4)
+    ocfg, params, be = make(pkg, O, shape, 8, max_seqs=24)
+    rng = np.random.default_rng(31)
+    prompts = [rng.integers(0, shape[0], int(rng.integers(1, 50))).astype(np.int32) for _ in range(24)]
+    with be:
+        lg = be.forward_last_batch([p.tolist() for p in prompts])
+        got = be.generate_batch([p.tolist() for p in prompts], 10, 0.0, 0)
+    for i, p in enumerate(prompts):
+        assert relerr(lg[i], O.forward_last(ocfg, params, p)) <= TOL, i
+        check_ids(O, ocfg, params, p, got[i], O.generate(ocfg, params, p, 10, 0.0, 0, O.DotNetRandom(1)))
+
+
 def test_generate_batch_ragged_and_long_prompts(pkg, O):
     shape = (300, 24, 32, 2, 2)
     ocfg, params, be = make(pkg, O, shape, 9, max_seqs=5)
