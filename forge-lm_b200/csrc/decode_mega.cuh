@@ -122,6 +122,20 @@ FB2_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+// The same copy with an L2 cache policy (createpolicy).
+FB2_DEV void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+// L2 policy that evicts these lines before any others.
+FB2_DEV uint64_t l2_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
 FB2_DEV void cons_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 // Barrier of the 256 consumer threads that also ORs `pred` over them.
 FB2_DEV int cons_sync_or(int pred) {
@@ -340,9 +354,17 @@ __device__ __noinline__ float cons_kth_largest(const float* vals, int n, int k, 
         hist[tid] = 0u;
         cons_sync();
         const uint32_t prefix = (uint32_t)st[0], mask = (uint32_t)st[1];
-        for (int i = tid; i < n; i += MK_CONS) {
-            const uint32_t key = float_key(vals[i]);
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        // one shared atomic per distinct bin per warp: the leading passes put
+        // most keys in one bin, where per-lane atomics would serialize
+        for (int base = 0; base < n; base += MK_CONS) {
+            const int i = base + tid;
+            int bin = -1;
+            if (i < n) {
+                const uint32_t key = float_key(vals[i]);
+                if ((key & mask) == prefix) bin = (int)((key >> shift) & 255u);
+            }
+            const unsigned peers = __match_any_sync(0xffffffffu, bin);
+            if (bin >= 0 && (int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
         }
         cons_sync();
         if ((tid >> 5) == 0) {
@@ -584,6 +606,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     int* cnts = iscr + 512;                              // [256]
 
     __shared__ int s_slot[MK_MAX_ROWS], s_pos0[MK_MAX_ROWS], s_tok[MK_MAX_ROWS], s_cnt0[MK_MAX_ROWS];
+    __shared__ double s_ud[MK_MAX_ROWS];  // this step's uniform draw per row
     __shared__ int s_len0[MK_MAX_ROWS], s_dead[MK_MAX_ROWS], s_dummy[MK_MAX_ROWS], s_ubase[MK_MAX_ROWS + 1];
     __shared__ volatile int s_abort;
 
@@ -628,7 +651,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         if (tid != MK_CONS) return;
         uint32_t it = 0;
         bool ok = true;
-        auto issue = [&](const void* src, uint32_t bytes) {
+        // Weights and the head's embedding rows are read once per step (391 MB
+        // for Forge-98M, beyond L2): they go through L2 evict-first, so the
+        // kernel's code, the small per-layer parameters, the exchange words
+        // and the sequence's K/V (normal priority) stay resident across steps.
+        const uint64_t stream_policy = l2_evict_first();
+        auto issue = [&](const void* src, uint32_t bytes, bool streamed) {
             if (!ok) return;
             const int st = it % a.nstage;
             if (it >= (uint32_t)a.nstage) {
@@ -646,7 +674,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 }
             }
             mbar_expect_tx(&full[st], bytes);
-            bulk_g2s(ring + (size_t)st * MK_STAGE, src, bytes, &full[st]);
+            if (streamed) bulk_g2s_hint(ring + (size_t)st * MK_STAGE, src, bytes, &full[st], stream_policy);
+            else bulk_g2s(ring + (size_t)st * MK_STAGE, src, bytes, &full[st]);
             it++;
         };
         auto issue_strip = [&](const float* Wt, int K, int N) {
@@ -655,7 +684,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
             const int R = strip_rows(w, K);
             if (R == 0) return;
             const float* base = Wt + (size_t)K * n0;
-            for (int r0 = 0; r0 < K && ok; r0 += R) issue(base + (size_t)r0 * w, (uint32_t)(min(R, K - r0) * w * 4));
+            for (int r0 = 0; r0 < K && ok; r0 += R) issue(base + (size_t)r0 * w, (uint32_t)(min(R, K - r0) * w * 4), true);
         };
         for (int s = 0; s < a.nsteps && ok; s++) {
             const unsigned int gs = a.gstep0 + s;
@@ -689,8 +718,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                         const int nk = min(KC, old - c * KC);
                         const float* kb = a.kv + (size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
                                           ((size_t)h * a.ctx + c * KC) * hd;
-                        issue(kb, (uint32_t)(nk * hd * 4));
-                        issue(kb + a.v_offset, (uint32_t)(nk * hd * 4));
+                        issue(kb, (uint32_t)(nk * hd * 4), false);
+                        issue(kb + a.v_offset, (uint32_t)(nk * hd * 4), false);
                     }
                     ubase += nu;
                 }
@@ -701,7 +730,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
             const int v0 = (int)(((long long)cta * V) / nW), v1 = (int)(((long long)(cta + 1) * V) / nW);
             const int Rh = max(1, MK_STAGE / (D * 4));
             for (int r0 = v0; r0 < v1 && ok; r0 += Rh)
-                issue(a.tok_emb + (size_t)r0 * D, (uint32_t)(min(Rh, v1 - r0) * D * 4));
+                issue(a.tok_emb + (size_t)r0 * D, (uint32_t)(min(Rh, v1 - r0) * D * 4), true);
         }
         // wait (bounded) for copies still landing in this CTA's ring
         for (uint32_t j = (it > (uint32_t)a.nstage ? it - a.nstage : 0); j < it; j++) {
@@ -1092,6 +1121,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
             if (cons_sync_or(s_abort)) return;
         }
         MK_TRACE(25);
+        // this step's uniform for row tid, loaded before the head (a cold
+        // global load) and parked in shared memory before the sampler
+        double ud_next = 0.0;
+        if (sampled && tid < MR)
+            ud_next = a.uniforms[(size_t)s_slot[tid] * a.uni_stride + min(s_cnt0[tid] + s, max(sp.max_new - 1, 0))];
         mk_layernorm<MR>(xres, act, D, lnf, scr + 384);
         const int v0 = (int)(((long long)cta * V) / nW), v1 = (int)(((long long)(cta + 1) * V) / nW);
         const int nsl = v1 - v0;
@@ -1283,6 +1317,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         MK_TRACE(28);
         // publish: release every plain write of this step (K/V cache, logits,
         // candidates), then per (row, slice) the tagged count and local k-th
+        if (tid < MR) s_ud[tid] = ud_next;
         __threadfence();
         cons_sync();
         if (tid < MR) {
@@ -1466,8 +1501,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     }
                     cons_sync();
                     if (tid == 0) {
-                        const double ud =
-                            a.uniforms[(size_t)s_slot[m] * a.uni_stride + min(s_cnt0[m] + s, max(sp.max_new - 1, 0))];
+                        const double ud = s_ud[m];
                         float sum = 0.0f;  // index order (Sampler.cs:54-59)
                         for (int i = 0; i < Q; i++) sum += surv_v[i];
                         const float uu = (float)ud * sum;  // Sampler.cs:61
@@ -1547,8 +1581,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     }
                     cons_sync();
                     if (tid == 0) {
-                        const double ud =
-                            a.uniforms[(size_t)s_slot[m] * a.uni_stride + min(s_cnt0[m] + s, max(sp.max_new - 1, 0))];
+                        const double ud = s_ud[m];
                         float sum = 0.0f;
                         int pick = V - 1;
                         if (S <= MK_SURV_MAX) {

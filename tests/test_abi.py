@@ -107,6 +107,29 @@ def test_expf_fixup_table_matches_host_libm(O):
     assert n == len(in_range) and np.array_equal(np.sort(bad), in_range)
 
 
+def test_expf_fixup_midpoint_bound():
+    """Every listed input with a normal result has exp(x) within
+    FB2_EXPF_FIXUP_MAX_GAP ulp of a rounding midpoint: the device skips the
+    table for inputs farther than twice that, so the bound must cover all."""
+    path = os.path.join(ROOT, "forge-lm_b200", "csrc", "generated", "expf_fixups.inc")
+    txt = open(path).read()
+    gap = float(txt.split("#define FB2_EXPF_FIXUP_MAX_GAP")[1].split()[0])
+    assert 0.0 < gap < 0.01  # the host expf is within about half an ulp
+    body = txt[txt.index("kExpfFixupData[] = {"):txt.index("};")]
+    words = np.array([int(w.rstrip("u"), 16) for w in body.replace(",", " ").split() if w.startswith("0x")], np.uint64)
+    x = words[0::2].astype(np.uint32).view(np.float32).astype(np.float64)
+    e = np.exp(x)
+    r = e.astype(np.float32)
+    normal = (r >= np.float32(1.17549435e-38)) & (r < np.finfo(np.float32).max)
+    rd, en = r[normal].astype(np.float64), e[normal]
+    up = np.nextafter(r[normal], np.float32(np.inf)).astype(np.float64) - rd
+    dn = rd - np.nextafter(r[normal], np.float32(0)).astype(np.float64)
+    g = np.minimum((rd + 0.5 * up - en) / up, (en - (rd - 0.5 * dn)) / dn)
+    # numpy's exp and the C runtime's exp may differ by a few double ulps,
+    # about 1e-8 float ulps here; the device compares against twice the bound
+    assert len(g) > 1000 and g.max() <= gap + 1e-7
+
+
 def test_library_init_params_equal_oracle(pkg, O):
     """fb2_init_params reproduces GptModel's seeded init bit for bit (the
     same restatement the oracle makes)."""
