@@ -1,0 +1,268 @@
+// attn_tc.cuh — causal prefill attention on the tensor cores (sm_100a),
+// head_dim 64.
+//
+// The same computation as k_attn_prefill_rt (softmax(q k^T * scale, causal)
+// v per head, CpuBackend.cs:540-575: scale, mask, softmax, weighted sum),
+// with both products on the 5th-generation tensor cores in TF32 and the
+// 3xTF32 compensation of gemm_tc.cuh (x = hi + lo, hi*hi + hi*lo + lo*hi).
+//
+// One CTA of 128 threads per (query block of <= 128 rows, head); thread t
+// owns query row t, which is also TMEM lane t (warp w reads lanes 32w..).
+// Per 64-key tile of the cache:
+//   1. the tile's K and V (prefetched into registers during the previous
+//      tile) are split into TF32 halves and written as K-major, 128-byte
+//      swizzled operands: K [64 keys][64 dims], V^T [64 dims][64 keys];
+//   2. thread 0 issues S = Q K^T (M128 N64, 8 k-steps x 3 MMAs) into TMEM
+//      columns 0..63 and commits to an mbarrier;
+//   3. every thread loads its score row (tcgen05.ld), applies scale and the
+//      causal mask, and updates its running max m and sum l (online softmax);
+//      p = exp(s - m) goes back to shared memory as P's TF32 halves;
+//   4. thread 0 issues O_tile = P V (M128 N64, V^T as the K-major operand)
+//      into TMEM columns 64..127; every thread folds its row into registers:
+//      o = o * alpha + O_tile.
+// Rows past the block and keys past the last query are zero operands (the
+// cache beyond them may hold anything); masked scores are -inf.
+// Every mbarrier wait is bounded (kTcTimeoutNs); on expiry the CTA records
+// TC_ERR_TIMEOUT, drains its MMAs (bounded), frees TMEM and returns.
+#pragma once
+#include "gemm_tc.cuh"
+
+namespace fb2 {
+
+constexpr int ATC_THREADS = 128;
+constexpr int ATC_BQ = 128, ATC_BK = 64, ATC_HD = 64;
+constexpr int ATC_QB = ATC_BQ * ATC_HD * 4;   // one TF32 half of Q (or P): 32 KB
+constexpr int ATC_KB = ATC_BK * ATC_HD * 4;   // one TF32 half of K (or V^T): 16 KB
+constexpr int ATC_SMEM = 4 * ATC_QB + 4 * ATC_KB + 1024;  // Q, P, K, V^T halves + alignment slack
+constexpr uint32_t ATC_TMEM_COLS = 128;       // S: columns 0..63, O tile: 64..127
+
+namespace atc {
+// Byte offset of fp32 element (row, col) in a K-major operand of `rows` rows
+// and 64 columns, stored as two 128-byte-wide blocks (columns 0..31, 32..63),
+// each rows x 128 B with the 128-byte swizzle (16-byte chunk c of row r at
+// c ^ (r % 8)) that the tensor cores' SWIZZLE_128B descriptor reads.
+FB2_DEV uint32_t swz(int row, int col, int rows) {
+    const int blk = col >> 5, c = col & 31;
+    return (uint32_t)(blk * rows * 128 + row * 128 + ((((c >> 2) ^ (row & 7)) << 4) | ((c & 3) << 2)));
+}
+// Descriptor of k-step kk (8 TF32 columns) of such an operand at `base`.
+FB2_DEV uint64_t kdesc(uint32_t base, int kk, int rows) {
+    return tc::sw128_desc(base + (uint32_t)((kk >> 2) * rows * 128 + (kk & 3) * 32), 16, 1024);
+}
+FB2_DEV void st_shared_v4(uint32_t addr, float4 v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+FB2_DEV void st_shared_f32(uint32_t addr, float v) { asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory"); }
+FB2_DEV void split4(float4 v, float4& hi, float4& lo) {
+    tf32_split(v.x, hi.x, lo.x);
+    tf32_split(v.y, hi.y, lo.y);
+    tf32_split(v.z, hi.z, lo.z);
+    tf32_split(v.w, hi.w, lo.w);
+}
+// Shared memory written by the threads -> visible to the tensor cores.
+FB2_DEV void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// 3 x 8 MMAs of one M128 N64 K64 product (A, B: K-major TF32 halves).
+FB2_DEV void mma_3x(uint32_t d, uint32_t a_hi, uint32_t a_lo, int a_rows, uint32_t b_hi, uint32_t b_lo, int b_rows) {
+    constexpr uint32_t idesc = tc::idesc_tf32(ATC_BQ, 64);
+#pragma unroll
+    for (int kk = 0; kk < ATC_HD / 8; kk++) {
+        const uint64_t ah = kdesc(a_hi, kk, a_rows), al = kdesc(a_lo, kk, a_rows);
+        const uint64_t bh = kdesc(b_hi, kk, b_rows), bl = kdesc(b_lo, kk, b_rows);
+        tc::mma_tf32(d, ah, bh, idesc, kk != 0);
+        tc::mma_tf32(d, ah, bl, idesc, 1u);
+        tc::mma_tf32(d, al, bh, idesc, 1u);
+    }
+}
+}  // namespace atc
+
+// qblk[b] = {first row, count (<= 128), sequence slot, first position}; the
+// block's rows are that sequence's consecutive positions.
+__global__ void __launch_bounds__(ATC_THREADS, 1)
+    k_attn_prefill_tc(const float* __restrict__ q, const float* __restrict__ kv_layer, long long kv_slot_stride,
+                      long long v_offset, int H, int ctx, float scale, const int4* __restrict__ qblk,
+                      float* __restrict__ ctx_out, int* err) {
+    extern __shared__ unsigned char atc_smem_raw[];
+    __shared__ __align__(8) uint64_t mbar, drain;
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int s_abort;
+    unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(atc_smem_raw) + 1023) & ~(uintptr_t)1023);
+    const uint32_t Qh = tc::smem_addr(sm), Ql = Qh + ATC_QB, Ph = Ql + ATC_QB, Pl = Ph + ATC_QB;
+    const uint32_t Kh = Pl + ATC_QB, Kl = Kh + ATC_KB, Vh = Kl + ATC_KB, Vl = Vh + ATC_KB;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (tid == 0) {
+        s_abort = 0;
+        tc::bar_init(&mbar, 1);
+        tc::bar_init(&drain, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc::smem_addr(&tmem_base)),
+                     "r"(ATC_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = tmem_base;
+    const uint32_t t_lane = tmem + ((uint32_t)(32 * warp) << 16);  // this warp's TMEM lane quarter
+    pdl_wait();  // barriers and tensor memory set up; global memory from here on
+
+    const int4 blk = qblk[blockIdx.x];
+    const int h = blockIdx.y;
+    const int row0 = blk.x, nq = blk.y, seq = blk.z, p0 = blk.w;
+    const int D = H * ATC_HD;
+    // Q block -> TF32 halves (16 threads per row: coalesced loads)
+    for (int i = tid; i < ATC_BQ * 16; i += ATC_THREADS) {
+        const int r = i >> 4, c4 = i & 15;
+        const float4 v = r < nq ? __ldg(reinterpret_cast<const float4*>(q + (size_t)(row0 + r) * D + h * ATC_HD) + c4)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 hi, lo;
+        atc::split4(v, hi, lo);
+        const uint32_t o = atc::swz(r, 4 * c4, ATC_BQ);
+        atc::st_shared_v4(Qh + o, hi);
+        atc::st_shared_v4(Ql + o, lo);
+    }
+    const float* Kb = kv_layer + (size_t)seq * kv_slot_stride + (size_t)h * ctx * ATC_HD;
+    const float* Vb = Kb + v_offset;
+    const int last_key = p0 + nq - 1, ntiles = last_key / ATC_BK + 1;
+    // tile prefetch: K as 8 float4 per thread (16 threads per key row); V as
+    // 8 float4 per thread with a warp's lanes on 32 consecutive keys (the
+    // transposed stores below are then conflict-free)
+    const int vkey = 32 * (warp & 1) + lane, vd0 = 32 * (warp >> 1);
+    float4 kr[8], vr[8];
+    auto load_tile = [&](int kt) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int i = tid + ATC_THREADS * j, key = kt + (i >> 4), c4 = i & 15;
+            kr[j] = key <= last_key ? __ldcg(reinterpret_cast<const float4*>(Kb + (size_t)key * ATC_HD) + c4)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            const int vk = kt + vkey;
+            vr[j] = vk <= last_key ? __ldcg(reinterpret_cast<const float4*>(Vb + (size_t)vk * ATC_HD + vd0) + j)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    load_tile(0);
+
+    const int r = tid, qpos = p0 + r;
+    float o[ATC_HD];
+#pragma unroll
+    for (int d = 0; d < ATC_HD; d++) o[d] = 0.f;
+    float m = -INFINITY, l = 0.f;
+    uint32_t phase = 0;
+    for (int t = 0; t < ntiles; t++) {
+        const int kt = t * ATC_BK;
+        // 1. this tile's K, V^T halves
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int i = tid + ATC_THREADS * j, key = i >> 4, c4 = i & 15;
+            float4 hi, lo;
+            atc::split4(kr[j], hi, lo);
+            const uint32_t ko = atc::swz(key, 4 * c4, ATC_BK);
+            atc::st_shared_v4(Kh + ko, hi);
+            atc::st_shared_v4(Kl + ko, lo);
+            float4 vh, vl;
+            atc::split4(vr[j], vh, vl);
+            const int d = vd0 + 4 * j;
+            atc::st_shared_f32(Vh + atc::swz(d, vkey, ATC_HD), vh.x);
+            atc::st_shared_f32(Vl + atc::swz(d, vkey, ATC_HD), vl.x);
+            atc::st_shared_f32(Vh + atc::swz(d + 1, vkey, ATC_HD), vh.y);
+            atc::st_shared_f32(Vl + atc::swz(d + 1, vkey, ATC_HD), vl.y);
+            atc::st_shared_f32(Vh + atc::swz(d + 2, vkey, ATC_HD), vh.z);
+            atc::st_shared_f32(Vl + atc::swz(d + 2, vkey, ATC_HD), vl.z);
+            atc::st_shared_f32(Vh + atc::swz(d + 3, vkey, ATC_HD), vh.w);
+            atc::st_shared_f32(Vl + atc::swz(d + 3, vkey, ATC_HD), vl.w);
+        }
+        // 2. the next tile's loads are in flight during this tile's MMAs
+        if (t + 1 < ntiles) load_tile(kt + ATC_BK);
+        // 3. S = Q K^T
+        atc::fence_async_shared();
+        tc::fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc::fence_after();
+            atc::mma_3x(tmem, Qh, Ql, ATC_BQ, Kh, Kl, ATC_BK);
+            tc::mma_commit(&mbar);
+        }
+        bool ok = tc::bar_wait(&mbar, phase, &s_abort);
+        phase ^= 1u;
+        if (!__syncthreads_and(ok)) break;
+        tc::fence_after();
+        float s[ATC_BK];
+#pragma unroll
+        for (int c = 0; c < ATC_BK / 16; c++) tc::tmem_ld16(t_lane + 16 * c, s + 16 * c);
+        // online softmax of row r over this tile (causal mask: key > position)
+        float tmax = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < ATC_BK; j++) {
+            const float v = kt + j > qpos ? -INFINITY : s[j] * scale;
+            s[j] = v;
+            tmax = fmaxf(tmax, v);
+        }
+        const float mnew = fmaxf(m, tmax);
+        const float alpha = mnew == -INFINITY ? 1.f : __expf(m - mnew);
+        float psum = 0.f;
+#pragma unroll
+        for (int j = 0; j < ATC_BK; j++) {
+            const float p = s[j] == -INFINITY ? 0.f : __expf(s[j] - mnew);
+            s[j] = p;
+            psum += p;
+        }
+        l = l * alpha + psum;
+        m = mnew;
+#pragma unroll
+        for (int c4 = 0; c4 < ATC_BK / 4; c4++) {
+            float4 hi, lo;
+            atc::split4(make_float4(s[4 * c4], s[4 * c4 + 1], s[4 * c4 + 2], s[4 * c4 + 3]), hi, lo);
+            const uint32_t po = atc::swz(r, 4 * c4, ATC_BQ);
+            atc::st_shared_v4(Ph + po, hi);
+            atc::st_shared_v4(Pl + po, lo);
+        }
+        // 4. O_tile = P V
+        atc::fence_async_shared();
+        tc::fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc::fence_after();
+            atc::mma_3x(tmem + 64, Ph, Pl, ATC_BQ, Vh, Vl, ATC_HD);
+            tc::mma_commit(&mbar);
+        }
+        ok = tc::bar_wait(&mbar, phase, &s_abort);
+        phase ^= 1u;
+        if (!__syncthreads_and(ok)) break;
+        tc::fence_after();
+#pragma unroll
+        for (int c = 0; c < ATC_HD / 16; c++) {
+            float ot[16];
+            tc::tmem_ld16(t_lane + 64 + 16 * c, ot);
+#pragma unroll
+            for (int i = 0; i < 16; i++) o[16 * c + i] = o[16 * c + i] * alpha + ot[i];
+        }
+        tc::fence_before();  // TMEM reads done before the next tile's MMAs (behind its barrier)
+    }
+    if (!s_abort && r < nq) {
+        const float inv = 1.0f / l;
+        float4* out = reinterpret_cast<float4*>(ctx_out + (size_t)(row0 + r) * D + h * ATC_HD);
+#pragma unroll
+        for (int d4 = 0; d4 < ATC_HD / 4; d4++)
+            out[d4] = make_float4(o[4 * d4] * inv, o[4 * d4 + 1] * inv, o[4 * d4 + 2] * inv, o[4 * d4 + 3] * inv);
+    }
+    if (s_abort && tid == 0) {
+        atomicExch(err, TC_ERR_TIMEOUT);
+        // every MMA issued completes before tensor memory is freed
+        tc::mma_commit(&drain);
+        const unsigned long long t0 = tc::now_ns();
+        while (!tc::bar_try(&drain, 0) && tc::now_ns() - t0 < kTcTimeoutNs) {
+        }
+    }
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ATC_TMEM_COLS) : "memory");
+    }
+}
+
+}  // namespace fb2

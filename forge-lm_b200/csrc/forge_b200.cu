@@ -31,6 +31,7 @@
 #include "sampler.cuh"
 #include "decode_mega.cuh"
 #include "gemm_tc.cuh"
+#include "attn_tc.cuh"
 #include "forgemodel.hpp"
 #include "tokenizer.hpp"
 
@@ -154,6 +155,9 @@ struct DeviceModel {
     // tensor-core GEMM: TF32 hi/lo halves of the four projections per layer
     // (qkv, proj, fc, mlp proj) and their TMA descriptors
     bool tc_ok = false;
+    // prefill attention on the tensor cores (head_dim 64; FORGE_B200_ATTN=simt
+    // keeps the SIMT kernel)
+    bool attn_tc = false;
     float* tc_blob = nullptr;
     // FB2_WEIGHTS_BF16: the projections and tok_emb are rounded to bf16 in
     // `blob` (every path computes with the same values) and the HBM-bound
@@ -219,6 +223,7 @@ static void configure_kernels(int dev) {
     setmax((const void*)k_attn_prefill_rt<32>, 227 * 1024);
     setmax((const void*)k_attn_prefill_rt<64>, 227 * 1024);
     setmax((const void*)k_attn_prefill_rt<128>, 227 * 1024);
+    setmax((const void*)k_attn_prefill_tc, 227 * 1024);
     setmax((const void*)k_head<1>, 227 * 1024);
     setmax((const void*)k_head<2>, 227 * 1024);
     setmax((const void*)k_head<4>, 227 * 1024);
@@ -362,6 +367,8 @@ static void tc_setup(const fb2_model& m, DeviceModel& dm) {
     }
     CK(cudaDeviceSynchronize());
     dm.tc_ok = true;
+    const char* aenv = getenv("FORGE_B200_ATTN");
+    dm.attn_tc = m.hd == ATC_HD && !(aenv && std::string(aenv) == "simt");
 }
 
 // Re-lays every projection W[K][N] as consecutive column strips [K][w_c],
@@ -418,7 +425,8 @@ static void mk_setup(const fb2_model& m, DeviceModel& dm, const float* const* pa
 struct ChunkPlan {
     int row_off;      // first entry in the row table
     int rows;         // rows in this chunk
-    int qblk_off, nqblk;
+    int qblk_off, nqblk;    // query blocks of <= 64 rows (SIMT attention)
+    int qblk2_off, nqblk2;  // query blocks of <= 128 rows (tensor-core attention)
     int slot_off, nslots;  // entries in last_row / out_slot tables
 };
 
@@ -746,7 +754,26 @@ static void launch_attn_prefill_hd(DeviceSession& s, int nblk, const int4* qblk,
                                                                  m.ctx, scale, qblk, s.d_att);
 }
 
-static void launch_attn_prefill(DeviceSession& s, int nblk, const int4* qblk, int layer) {
+// Query blocks of the prefill attention: <= 64 rows for the SIMT kernels,
+// <= 128 rows (may be null) for the tensor-core kernel.
+struct QBlocks {
+    int n;
+    const int4* b;
+    int n2;
+    const int4* b2;
+};
+
+static void launch_attn_prefill(DeviceSession& s, QBlocks qb, int layer) {
+    const fb2_model& m = *s.model;
+    if (s.dm->attn_tc && s.dm->tc_ok && s.d_tc_err && qb.b2 && qb.n2 > 0) {
+        const float* kvl = s.d_kv + (size_t)layer * s.kv_layer_stride;
+        s.stats.kernel_launches++;
+        launch_pdl(k_attn_prefill_tc, dim3(qb.n2, m.H), ATC_THREADS, (size_t)ATC_SMEM, s.stream, s.d_q, kvl,
+                   s.kv_slot_stride, s.v_offset, m.H, m.ctx, 1.0f / sqrtf((float)m.hd), qb.b2, s.d_att, s.d_tc_err);
+        return;
+    }
+    const int nblk = qb.n;
+    const int4* qblk = qb.b;
     switch (s.model->hd) {
     case 4: launch_attn_prefill_hd<4>(s, nblk, qblk, layer); break;
     case 8: launch_attn_prefill_hd<8>(s, nblk, qblk, layer); break;
@@ -793,7 +820,7 @@ static void launch_head(DeviceSession& s, int M, const float* xln, const int* ou
 // All transformer blocks (TransformerBlock.Forward, Layers.cs:384-392) over
 // rows 0..M-1 of d_x.  decode: single-row attention over the cache;
 // otherwise causal prefill attention over the query blocks.
-static void run_layers(DeviceSession& s, int M, Rows R, bool decode, int nqblk, const int4* qblk) {
+static void run_layers(DeviceSession& s, int M, Rows R, bool decode, QBlocks qb) {
     const fb2_model& m = *s.model;
     for (int l = 0; l < m.L; l++) {
         const LayerW& w = s.dm->layers[l];
@@ -809,7 +836,7 @@ static void run_layers(DeviceSession& s, int M, Rows R, bool decode, int nqblk, 
         const CUtensorMap* tcm = s.dm->tc_ok ? s.dm->tc_maps[l].data() : nullptr;
         launch_linear(s, M, m.D, 3 * m.D, s.d_ln, w.qkv_w, eq, tcm);
         if (decode) launch_attn_decode(s, M, l, R);
-        else launch_attn_prefill(s, nqblk, qblk, l);
+        else launch_attn_prefill(s, qb, l);
         launch_linear(s, M, m.D, m.D, s.d_att, w.proj_w, make_epi(EPI_RESID, w.proj_b, s.d_x, s.d_x2), tcm ? tcm + 2 : nullptr);
         launch_layernorm(s, M, s.d_x2, w.ln2_w, w.ln2_b, s.d_ln, nullptr);
         launch_linear(s, M, m.D, m.F, s.d_ln, w.fc_w, make_epi(EPI_GELU, w.fc_b, nullptr, s.d_h), tcm ? tcm + 4 : nullptr);
@@ -824,7 +851,7 @@ static void enqueue_decode_step(DeviceSession& s, int n) {
                                                           s.d_row_hidx, s.d_row_active);
     Rows R{s.d_row_seq, s.d_row_pos, s.d_row_hidx, s.d_row_active};
     s.stats.kernel_launches++; launch_pdl(k_embed, n, 128, 0, s.stream, n, R, s.d_hist, s.hist_cap, s.dm->tok_emb, s.dm->pos_emb, m.D, m.V, s.d_x);
-    run_layers(s, n, R, true, 0, nullptr);
+    run_layers(s, n, R, true, QBlocks{0, nullptr, 0, nullptr});
     launch_layernorm(s, n, s.d_x, s.dm->lnf_w, s.dm->lnf_b, s.d_lnf, nullptr);
     launch_head(s, n, s.d_lnf, nullptr, s.d_logits);
 }
@@ -935,6 +962,7 @@ static void mk_check(DeviceSession& s) {
 
 // Prefill of one chunk: rows described by the uploaded tables.
 // tab layout per chunk: row_seq[rows], row_pos[rows], qblk (int4) [nqblk],
+// qblk2 (int4) [nqblk2],
 // last_row[nslots], out_slot[nslots].
 struct PrefillTables {
     const int* row_seq;
@@ -968,6 +996,7 @@ static void run_prefill_chunk(DeviceSession& s, const ChunkPlan& c, const int* d
     const int* row_seq = d_tab_base + c.row_off;
     const int* row_pos = row_seq + c.rows;
     const int4* qblk = reinterpret_cast<const int4*>(d_tab_base + c.qblk_off);
+    const int4* qblk2 = reinterpret_cast<const int4*>(d_tab_base + c.qblk2_off);
     const int* last_row = d_tab_base + c.slot_off;
     const int* out_slot = last_row + c.nslots;
     s.stats.kernel_launches++; launch_pdl(k_prefill_hidx, ceil_div(c.rows, 256), 256, 0, s.stream, c.rows, row_seq, row_pos, s.d_len, m.ctx,
@@ -975,7 +1004,7 @@ static void run_prefill_chunk(DeviceSession& s, const ChunkPlan& c, const int* d
     Rows R{row_seq, row_pos, s.d_row_hidx, s.d_ones};
     s.stats.kernel_launches++; launch_pdl(k_embed, c.rows, 128, 0, s.stream, c.rows, R, s.d_hist, s.hist_cap, s.dm->tok_emb, s.dm->pos_emb, m.D, m.V,
                                           s.d_x);
-    run_layers(s, c.rows, R, false, c.nqblk, qblk);
+    run_layers(s, c.rows, R, false, QBlocks{c.nqblk, qblk, c.nqblk2, qblk2});
     launch_layernorm(s, c.nslots, s.d_x, s.dm->lnf_w, s.dm->lnf_b, s.d_lnf, last_row);
     // head into the chunk-compact area after the slots' logits, then scatter
     float* tmp = s.d_logits + (size_t)s.nslots * m.V;
@@ -1007,7 +1036,7 @@ static void plan_prefill(const DeviceSession& s, const std::vector<int>& order, 
         c.nslots = (int)(j - i);
         c.row_off = (int)tab.size();
         std::vector<int> seq, pos;
-        std::vector<int> q;
+        std::vector<int> q, q2;
         std::vector<int> last, slot;
         int r = 0;
         for (size_t k = i; k < j; k++) {
@@ -1023,6 +1052,13 @@ static void plan_prefill(const DeviceSession& s, const std::vector<int>& order, 
                 q.push_back(sl);
                 q.push_back(p0);
             }
+            for (int p0 = a; p0 < w; p0 += 128) {
+                int cnt = std::min(128, w - p0);
+                q2.push_back(r + (p0 - a));
+                q2.push_back(cnt);
+                q2.push_back(sl);
+                q2.push_back(p0);
+            }
             last.push_back(r + (w - a) - 1);
             slot.push_back(sl);
             r += w - a;
@@ -1033,6 +1069,9 @@ static void plan_prefill(const DeviceSession& s, const std::vector<int>& order, 
         c.qblk_off = (int)tab.size();
         c.nqblk = (int)(q.size() / 4);
         tab.insert(tab.end(), q.begin(), q.end());
+        c.qblk2_off = (int)tab.size();
+        c.nqblk2 = (int)(q2.size() / 4);
+        tab.insert(tab.end(), q2.begin(), q2.end());
         c.slot_off = (int)tab.size();
         tab.insert(tab.end(), last.begin(), last.end());
         tab.insert(tab.end(), slot.begin(), slot.end());
@@ -2179,7 +2218,7 @@ int32_t fb2_forward_last_logits_noalloc(fb2_model* m, int32_t device_slot, int32
         Rows R{row_seq, row_pos, s.d_row_hidx, s.d_ones};
         launch_pdl(k_embed, n_tokens, 128, 0, s.stream, n_tokens, R, s.d_hist, s.hist_cap, dm.tok_emb, dm.pos_emb, view.D,
                                                 view.V, s.d_x);
-        run_layers(s, n_tokens, R, false, 1, qblk);
+        run_layers(s, n_tokens, R, false, QBlocks{1, qblk, 0, nullptr});
         launch_layernorm(s, 1, s.d_x, dm.lnf_w, dm.lnf_b, s.d_lnf, last_row);
         launch_head(s, 1, s.d_lnf, nullptr, device_logits);
         CK(cudaGetLastError());
