@@ -6,20 +6,22 @@
 // with both products on the 5th-generation tensor cores in TF32 and the
 // 3xTF32 compensation of gemm_tc.cuh (x = hi + lo, hi*hi + hi*lo + lo*hi).
 //
-// One CTA of 128 threads per (query block of <= 128 rows, head); thread t
-// owns query row t, which is also TMEM lane t (warp w reads lanes 32w..).
+// One CTA of 256 threads per (query block of <= 128 rows, head).  Query row
+// r is TMEM lane r; warps w and w + 4 both read lane quarter w % 4, warp w
+// taking columns 0..31 and warp w + 4 columns 32..63 of the S and O tiles,
+// and combine a row's max and sum through shared memory.
 // Per 64-key tile of the cache:
 //   1. the tile's K and V (prefetched into registers during the previous
 //      tile) are split into TF32 halves and written as K-major, 128-byte
 //      swizzled operands: K [64 keys][64 dims], V^T [64 dims][64 keys];
 //   2. thread 0 issues S = Q K^T (M128 N64, 8 k-steps x 3 MMAs) into TMEM
 //      columns 0..63 and commits to an mbarrier;
-//   3. every thread loads its score row (tcgen05.ld), applies scale and the
-//      causal mask, and updates its running max m and sum l (online softmax);
-//      p = exp(s - m) goes back to shared memory as P's TF32 halves;
+//   3. every thread loads its half score row (tcgen05.ld), applies scale and
+//      the causal mask, and updates the row's running max m and sum l (online
+//      softmax); p = exp(s - m) goes back to shared memory as P's TF32 halves;
 //   4. thread 0 issues O_tile = P V (M128 N64, V^T as the K-major operand)
-//      into TMEM columns 64..127; every thread folds its row into registers:
-//      o = o * alpha + O_tile.
+//      into TMEM columns 64..127; every thread folds its half row into
+//      registers: o = o * alpha + O_tile.
 // Rows past the block and keys past the last query are zero operands (the
 // cache beyond them may hold anything); masked scores are -inf.
 // Every mbarrier wait is bounded (kTcTimeoutNs); on expiry the CTA records
@@ -29,7 +31,7 @@
 
 namespace fb2 {
 
-constexpr int ATC_THREADS = 128;
+constexpr int ATC_THREADS = 256;
 constexpr int ATC_BQ = 128, ATC_BK = 64, ATC_HD = 64;
 constexpr int ATC_QB = ATC_BQ * ATC_HD * 4;   // one TF32 half of Q (or P): 32 KB
 constexpr int ATC_KB = ATC_BK * ATC_HD * 4;   // one TF32 half of K (or V^T): 16 KB
@@ -54,11 +56,22 @@ FB2_DEV void st_shared_v4(uint32_t addr, float4 v) {
                  : "memory");
 }
 FB2_DEV void st_shared_f32(uint32_t addr, float v) { asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory"); }
+// x = hi + lo with hi, lo TF32 (round to nearest even, as tf32_round; the
+// 13 low bits cleared explicitly).
+FB2_DEV float tf32_rn(float x) {
+    uint32_t r;
+    asm("cvt.rn.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r & 0xFFFFE000u);
+}
+FB2_DEV void split1(float x, float& hi, float& lo) {
+    hi = tf32_rn(x);
+    lo = tf32_rn(x - hi);
+}
 FB2_DEV void split4(float4 v, float4& hi, float4& lo) {
-    tf32_split(v.x, hi.x, lo.x);
-    tf32_split(v.y, hi.y, lo.y);
-    tf32_split(v.z, hi.z, lo.z);
-    tf32_split(v.w, hi.w, lo.w);
+    split1(v.x, hi.x, lo.x);
+    split1(v.y, hi.y, lo.y);
+    split1(v.z, hi.z, lo.z);
+    split1(v.w, hi.w, lo.w);
 }
 // Shared memory written by the threads -> visible to the tensor cores.
 FB2_DEV void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -86,10 +99,12 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     __shared__ __align__(8) uint64_t mbar, drain;
     __shared__ uint32_t tmem_base;
     __shared__ volatile int s_abort;
+    __shared__ float s_red[2][2][ATC_BQ];  // [max | sum][column half][row]
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(atc_smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t Qh = tc::smem_addr(sm), Ql = Qh + ATC_QB, Ph = Ql + ATC_QB, Pl = Ph + ATC_QB;
     const uint32_t Kh = Pl + ATC_QB, Kl = Kh + ATC_KB, Vh = Kl + ATC_KB, Vl = Vh + ATC_KB;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quarter = warp & 3, half = warp >> 2;
 
     if (tid == 0) {
         s_abort = 0;
@@ -107,7 +122,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     __syncthreads();
     tc::fence_after();
     const uint32_t tmem = tmem_base;
-    const uint32_t t_lane = tmem + ((uint32_t)(32 * warp) << 16);  // this warp's TMEM lane quarter
+    // this warp's lane quarter, its column half of the S (and, +64, O) tile
+    const uint32_t t_mine = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(32 * half);
     pdl_wait();  // barriers and tensor memory set up; global memory from here on
 
     const int4 blk = qblk[blockIdx.x];
@@ -128,14 +144,14 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     const float* Kb = kv_layer + (size_t)seq * kv_slot_stride + (size_t)h * ctx * ATC_HD;
     const float* Vb = Kb + v_offset;
     const int last_key = p0 + nq - 1, ntiles = last_key / ATC_BK + 1;
-    // tile prefetch: K as 8 float4 per thread (16 threads per key row); V as
-    // 8 float4 per thread with a warp's lanes on 32 consecutive keys (the
-    // transposed stores below are then conflict-free)
-    const int vkey = 32 * (warp & 1) + lane, vd0 = 32 * (warp >> 1);
-    float4 kr[8], vr[8];
+    // tile prefetch: K as 4 float4 per thread (16 threads per key row); V as
+    // 4 float4 per thread, a warp's lanes on 32 consecutive keys and 16 dims
+    // (the transposed stores below are then conflict-free)
+    const int vkey = 32 * (warp & 1) + lane, vd0 = 16 * (warp >> 1);
+    float4 kr[4], vr[4];
     auto load_tile = [&](int kt) {
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
+        for (int j = 0; j < 4; j++) {
             const int i = tid + ATC_THREADS * j, key = kt + (i >> 4), c4 = i & 15;
             kr[j] = key <= last_key ? __ldcg(reinterpret_cast<const float4*>(Kb + (size_t)key * ATC_HD) + c4)
                                     : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -146,17 +162,17 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     };
     load_tile(0);
 
-    const int r = tid, qpos = p0 + r;
-    float o[ATC_HD];
+    const int r = 32 * quarter + lane, qpos = p0 + r;
+    float o[32];
 #pragma unroll
-    for (int d = 0; d < ATC_HD; d++) o[d] = 0.f;
+    for (int d = 0; d < 32; d++) o[d] = 0.f;
     float m = -INFINITY, l = 0.f;
     uint32_t phase = 0;
     for (int t = 0; t < ntiles; t++) {
         const int kt = t * ATC_BK;
         // 1. this tile's K, V^T halves
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
+        for (int j = 0; j < 4; j++) {
             const int i = tid + ATC_THREADS * j, key = i >> 4, c4 = i & 15;
             float4 hi, lo;
             atc::split4(kr[j], hi, lo);
@@ -190,33 +206,36 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         phase ^= 1u;
         if (!__syncthreads_and(ok)) break;
         tc::fence_after();
-        float s[ATC_BK];
-#pragma unroll
-        for (int c = 0; c < ATC_BK / 16; c++) tc::tmem_ld16(t_lane + 16 * c, s + 16 * c);
+        float s[32];
+        tc::tmem_ld16(t_mine, s);
+        tc::tmem_ld16(t_mine + 16, s + 16);
         // online softmax of row r over this tile (causal mask: key > position)
+        const int k0 = kt + 32 * half;
         float tmax = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < ATC_BK; j++) {
-            const float v = kt + j > qpos ? -INFINITY : s[j] * scale;
+        for (int j = 0; j < 32; j++) {
+            const float v = k0 + j > qpos ? -INFINITY : s[j] * scale;
             s[j] = v;
             tmax = fmaxf(tmax, v);
         }
-        const float mnew = fmaxf(m, tmax);
+        s_red[0][half][r] = tmax;
+        __syncthreads();
+        const float mnew = fmaxf(m, fmaxf(s_red[0][0][r], s_red[0][1][r]));
         const float alpha = mnew == -INFINITY ? 1.f : __expf(m - mnew);
         float psum = 0.f;
 #pragma unroll
-        for (int j = 0; j < ATC_BK; j++) {
+        for (int j = 0; j < 32; j++) {
             const float p = s[j] == -INFINITY ? 0.f : __expf(s[j] - mnew);
             s[j] = p;
             psum += p;
         }
-        l = l * alpha + psum;
+        s_red[1][half][r] = psum;
         m = mnew;
 #pragma unroll
-        for (int c4 = 0; c4 < ATC_BK / 4; c4++) {
+        for (int c4 = 0; c4 < 8; c4++) {
             float4 hi, lo;
             atc::split4(make_float4(s[4 * c4], s[4 * c4 + 1], s[4 * c4 + 2], s[4 * c4 + 3]), hi, lo);
-            const uint32_t po = atc::swz(r, 4 * c4, ATC_BQ);
+            const uint32_t po = atc::swz(r, 32 * half + 4 * c4, ATC_BQ);
             atc::st_shared_v4(Ph + po, hi);
             atc::st_shared_v4(Pl + po, lo);
         }
@@ -224,6 +243,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         atc::fence_async_shared();
         tc::fence_before();
         __syncthreads();
+        l = l * alpha + (s_red[1][0][r] + s_red[1][1][r]);
         if (tid == 0) {
             tc::fence_after();
             atc::mma_3x(tmem + 64, Ph, Pl, ATC_BQ, Vh, Vl, ATC_HD);
@@ -234,9 +254,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         if (!__syncthreads_and(ok)) break;
         tc::fence_after();
 #pragma unroll
-        for (int c = 0; c < ATC_HD / 16; c++) {
+        for (int c = 0; c < 2; c++) {
             float ot[16];
-            tc::tmem_ld16(t_lane + 64 + 16 * c, ot);
+            tc::tmem_ld16(t_mine + 64 + 16 * c, ot);
 #pragma unroll
             for (int i = 0; i < 16; i++) o[16 * c + i] = o[16 * c + i] * alpha + ot[i];
         }
@@ -244,9 +264,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     }
     if (!s_abort && r < nq) {
         const float inv = 1.0f / l;
-        float4* out = reinterpret_cast<float4*>(ctx_out + (size_t)(row0 + r) * D + h * ATC_HD);
+        float4* out = reinterpret_cast<float4*>(ctx_out + (size_t)(row0 + r) * D + h * ATC_HD + 32 * half);
 #pragma unroll
-        for (int d4 = 0; d4 < ATC_HD / 4; d4++)
+        for (int d4 = 0; d4 < 8; d4++)
             out[d4] = make_float4(o[4 * d4] * inv, o[4 * d4 + 1] * inv, o[4 * d4 + 2] * inv, o[4 * d4 + 3] * inv);
     }
     if (s_abort && tid == 0) {
