@@ -10,18 +10,22 @@
 // r is TMEM lane r; warps w and w + 4 both read lane quarter w % 4, warp w
 // taking columns 0..31 and warp w + 4 columns 32..63 of the S and O tiles,
 // and combine a row's max and sum through shared memory.
-// Per 64-key tile of the cache:
-//   1. the tile's K and V (prefetched into registers during the previous
-//      tile) are split into TF32 halves and written as K-major, 128-byte
-//      swizzled operands: K [64 keys][64 dims], V^T [64 dims][64 keys];
-//   2. thread 0 issues S = Q K^T (M128 N64, 8 k-steps x 3 MMAs) into TMEM
-//      columns 0..63 and commits to an mbarrier;
-//   3. every thread loads its half score row (tcgen05.ld), applies scale and
-//      the causal mask, and updates the row's running max m and sum l (online
-//      softmax); p = exp(s - m) goes back to shared memory as P's TF32 halves;
-//   4. thread 0 issues O_tile = P V (M128 N64, V^T as the K-major operand)
-//      into TMEM columns 64..127; every thread folds its half row into
-//      registers: o = o * alpha + O_tile.
+// K and V tiles (64 keys) are split into TF32 halves and written as K-major,
+// 128-byte swizzled operands, K [64 keys][64 dims] and V^T [64 dims][64
+// keys], from registers loaded one tile ahead.  Thread 0 issues the MMAs
+// (M128 N64, 8 k-steps x 3) and commits them to mbarriers.  The two products
+// are software-pipelined against the threads' work; iteration t:
+//   1. wait for S(t) = Q K(t)^T (TMEM columns 64 (t % 2) ..);
+//   2. write K(t+1) (its buffer is free) and issue S(t+1), which runs on the
+//      tensor cores during the rest of the iteration;
+//   3. load the half score row (tcgen05.ld), apply scale and the causal mask,
+//      update the row's running max m and sum l (online softmax); wait for
+//      O(t-1) = P(t-1) V(t-1) (TMEM columns 128..191) and fold it into the
+//      registers, o = o * alpha(t-1) + O(t-1); write p = exp(s - m) as P's
+//      TF32 halves;
+//   4. write V(t) and issue O(t), which runs during the next iteration's
+//      steps 1-2.
+// The last O is folded after the loop.
 // Rows past the block and keys past the last query are zero operands (the
 // cache beyond them may hold anything); masked scores are -inf.
 // Every mbarrier wait is bounded (kTcTimeoutNs); on expiry the CTA records
@@ -36,7 +40,7 @@ constexpr int ATC_BQ = 128, ATC_BK = 64, ATC_HD = 64;
 constexpr int ATC_QB = ATC_BQ * ATC_HD * 4;   // one TF32 half of Q (or P): 32 KB
 constexpr int ATC_KB = ATC_BK * ATC_HD * 4;   // one TF32 half of K (or V^T): 16 KB
 constexpr int ATC_SMEM = 4 * ATC_QB + 4 * ATC_KB + 1024;  // Q, P, K, V^T halves + alignment slack
-constexpr uint32_t ATC_TMEM_COLS = 128;       // S: columns 0..63, O tile: 64..127
+constexpr uint32_t ATC_TMEM_COLS = 256;       // S: columns 0..63 and 64..127 (double), O tile: 128..191
 
 namespace atc {
 // Byte offset of fp32 element (row, col) in a K-major operand of `rows` rows
@@ -96,7 +100,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
                       long long v_offset, int H, int ctx, float scale, const int4* __restrict__ qblk,
                       float* __restrict__ ctx_out, int* err) {
     extern __shared__ unsigned char atc_smem_raw[];
-    __shared__ __align__(8) uint64_t mbar, drain;
+    __shared__ __align__(8) uint64_t bar_s, bar_o, drain;
     __shared__ uint32_t tmem_base;
     __shared__ volatile int s_abort;
     __shared__ float s_red[2][2][ATC_BQ];  // [max | sum][column half][row]
@@ -108,7 +112,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
 
     if (tid == 0) {
         s_abort = 0;
-        tc::bar_init(&mbar, 1);
+        tc::bar_init(&bar_s, 1);
+        tc::bar_init(&bar_o, 1);
         tc::bar_init(&drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -122,8 +127,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     __syncthreads();
     tc::fence_after();
     const uint32_t tmem = tmem_base;
-    // this warp's lane quarter, its column half of the S (and, +64, O) tile
+    // this warp's lane quarter and column half of a 64-column TMEM tile
     const uint32_t t_mine = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(32 * half);
+    constexpr uint32_t kO = 128;  // TMEM column of the O tile
     pdl_wait();  // barriers and tensor memory set up; global memory from here on
 
     const int4 blk = qblk[blockIdx.x];
@@ -144,33 +150,27 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     const float* Kb = kv_layer + (size_t)seq * kv_slot_stride + (size_t)h * ctx * ATC_HD;
     const float* Vb = Kb + v_offset;
     const int last_key = p0 + nq - 1, ntiles = last_key / ATC_BK + 1;
-    // tile prefetch: K as 4 float4 per thread (16 threads per key row); V as
-    // 4 float4 per thread, a warp's lanes on 32 consecutive keys and 16 dims
-    // (the transposed stores below are then conflict-free)
+    // K as 4 float4 per thread (16 threads per key row); V as 4 float4 per
+    // thread, a warp's lanes on 32 consecutive keys and 16 dims (the
+    // transposed stores are then conflict-free)
     const int vkey = 32 * (warp & 1) + lane, vd0 = 16 * (warp >> 1);
     float4 kr[4], vr[4];
-    auto load_tile = [&](int kt) {
+    auto load_k = [&](int kt) {
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const int i = tid + ATC_THREADS * j, key = kt + (i >> 4), c4 = i & 15;
             kr[j] = key <= last_key ? __ldcg(reinterpret_cast<const float4*>(Kb + (size_t)key * ATC_HD) + c4)
                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-            const int vk = kt + vkey;
-            vr[j] = vk <= last_key ? __ldcg(reinterpret_cast<const float4*>(Vb + (size_t)vk * ATC_HD + vd0) + j)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     };
-    load_tile(0);
-
-    const int r = 32 * quarter + lane, qpos = p0 + r;
-    float o[32];
+    auto load_v = [&](int kt) {
+        const int vk = kt + vkey;
 #pragma unroll
-    for (int d = 0; d < 32; d++) o[d] = 0.f;
-    float m = -INFINITY, l = 0.f;
-    uint32_t phase = 0;
-    for (int t = 0; t < ntiles; t++) {
-        const int kt = t * ATC_BK;
-        // 1. this tile's K, V^T halves
+        for (int j = 0; j < 4; j++)
+            vr[j] = vk <= last_key ? __ldcg(reinterpret_cast<const float4*>(Vb + (size_t)vk * ATC_HD + vd0) + j)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+    auto store_k = [&]() {
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const int i = tid + ATC_THREADS * j, key = i >> 4, c4 = i & 15;
@@ -179,6 +179,11 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
             const uint32_t ko = atc::swz(key, 4 * c4, ATC_BK);
             atc::st_shared_v4(Kh + ko, hi);
             atc::st_shared_v4(Kl + ko, lo);
+        }
+    };
+    auto store_v = [&]() {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
             float4 vh, vl;
             atc::split4(vr[j], vh, vl);
             const int d = vd0 + 4 * j;
@@ -191,25 +196,61 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
             atc::st_shared_f32(Vh + atc::swz(d + 3, vkey, ATC_HD), vh.w);
             atc::st_shared_f32(Vl + atc::swz(d + 3, vkey, ATC_HD), vl.w);
         }
-        // 2. the next tile's loads are in flight during this tile's MMAs
-        if (t + 1 < ntiles) load_tile(kt + ATC_BK);
-        // 3. S = Q K^T
+    };
+    // shared-memory operands written by the threads -> one thread issues
+    auto publish = [&]() {
         atc::fence_async_shared();
         tc::fence_before();
         __syncthreads();
+    };
+    auto issue_s = [&](int t) {
         if (tid == 0) {
             tc::fence_after();
-            atc::mma_3x(tmem, Qh, Ql, ATC_BQ, Kh, Kl, ATC_BK);
-            tc::mma_commit(&mbar);
+            atc::mma_3x(tmem + 64u * (uint32_t)(t & 1), Qh, Ql, ATC_BQ, Kh, Kl, ATC_BK);
+            tc::mma_commit(&bar_s);
         }
-        bool ok = tc::bar_wait(&mbar, phase, &s_abort);
-        phase ^= 1u;
+    };
+
+    // prologue: S(0) in flight, K(1) and V(0) in registers
+    load_k(0);
+    load_v(0);
+    store_k();
+    publish();
+    issue_s(0);
+    if (ntiles > 1) load_k(ATC_BK);
+
+    const int r = 32 * quarter + lane, qpos = p0 + r;
+    float o[32];
+#pragma unroll
+    for (int d = 0; d < 32; d++) o[d] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    auto fold_o = [&](float a) {
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            float ot[16];
+            tc::tmem_ld16(t_mine + kO + 16 * c, ot);
+#pragma unroll
+            for (int i = 0; i < 16; i++) o[16 * c + i] = o[16 * c + i] * a + ot[i];
+        }
+    };
+    bool ok = true;
+    for (int t = 0; t < ntiles; t++) {
+        const int kt = t * ATC_BK;
+        // 1. S(t) complete: the K buffer is free
+        ok = tc::bar_wait(&bar_s, (uint32_t)(t & 1), &s_abort);
         if (!__syncthreads_and(ok)) break;
         tc::fence_after();
+        // 2. K(t+1) and S(t+1)
+        if (t + 1 < ntiles) {
+            store_k();
+            publish();
+            issue_s(t + 1);
+            if (t + 2 < ntiles) load_k(kt + 2 * ATC_BK);
+        }
+        // 3. softmax of this tile's half row
         float s[32];
-        tc::tmem_ld16(t_mine, s);
-        tc::tmem_ld16(t_mine + 16, s + 16);
-        // online softmax of row r over this tile (causal mask: key > position)
+        tc::tmem_ld16(t_mine + 64u * (uint32_t)(t & 1), s);
+        tc::tmem_ld16(t_mine + 64u * (uint32_t)(t & 1) + 16, s + 16);
         const int k0 = kt + 32 * half;
         float tmax = -INFINITY;
 #pragma unroll
@@ -219,7 +260,12 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
             tmax = fmaxf(tmax, v);
         }
         s_red[0][half][r] = tmax;
-        __syncthreads();
+        if (t > 0) {  // O(t-1) complete: P, V and the O tile are free
+            ok = tc::bar_wait(&bar_o, (uint32_t)((t - 1) & 1), &s_abort);
+        }
+        if (!__syncthreads_and(ok)) break;
+        tc::fence_after();
+        if (t > 0) fold_o(alpha_prev);
         const float mnew = fmaxf(m, fmaxf(s_red[0][0][r], s_red[0][1][r]));
         const float alpha = mnew == -INFINITY ? 1.f : __expf(m - mnew);
         float psum = 0.f;
@@ -239,28 +285,24 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
             atc::st_shared_v4(Ph + po, hi);
             atc::st_shared_v4(Pl + po, lo);
         }
-        // 4. O_tile = P V
-        atc::fence_async_shared();
-        tc::fence_before();
-        __syncthreads();
+        // 4. V(t) and O(t) = P(t) V(t)
+        store_v();
+        publish();
         l = l * alpha + (s_red[1][0][r] + s_red[1][1][r]);
+        alpha_prev = alpha;
         if (tid == 0) {
             tc::fence_after();
-            atc::mma_3x(tmem + 64, Ph, Pl, ATC_BQ, Vh, Vl, ATC_HD);
-            tc::mma_commit(&mbar);
+            atc::mma_3x(tmem + kO, Ph, Pl, ATC_BQ, Vh, Vl, ATC_HD);
+            tc::mma_commit(&bar_o);
         }
-        ok = tc::bar_wait(&mbar, phase, &s_abort);
-        phase ^= 1u;
-        if (!__syncthreads_and(ok)) break;
-        tc::fence_after();
-#pragma unroll
-        for (int c = 0; c < 2; c++) {
-            float ot[16];
-            tc::tmem_ld16(t_mine + 64 + 16 * c, ot);
-#pragma unroll
-            for (int i = 0; i < 16; i++) o[16 * c + i] = o[16 * c + i] * alpha + ot[i];
+        if (t + 1 < ntiles) load_v(kt + ATC_BK);
+    }
+    if (!s_abort && ok) {  // the last O tile
+        ok = tc::bar_wait(&bar_o, (uint32_t)((ntiles - 1) & 1), &s_abort);
+        if (__syncthreads_and(ok)) {
+            tc::fence_after();
+            fold_o(alpha_prev);
         }
-        tc::fence_before();  // TMEM reads done before the next tile's MMAs (behind its barrier)
     }
     if (!s_abort && r < nq) {
         const float inv = 1.0f / l;
