@@ -60,22 +60,12 @@ FB2_DEV void st_shared_v4(uint32_t addr, float4 v) {
                  : "memory");
 }
 FB2_DEV void st_shared_f32(uint32_t addr, float v) { asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory"); }
-// x = hi + lo with hi, lo TF32 (round to nearest even, as tf32_round; the
-// 13 low bits cleared explicitly).
-FB2_DEV float tf32_rn(float x) {
-    uint32_t r;
-    asm("cvt.rn.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r & 0xFFFFE000u);
-}
-FB2_DEV void split1(float x, float& hi, float& lo) {
-    hi = tf32_rn(x);
-    lo = tf32_rn(x - hi);
-}
+// x = hi + lo with hi, lo TF32 (tf32_split_rn of gemm_tc.cuh).
 FB2_DEV void split4(float4 v, float4& hi, float4& lo) {
-    split1(v.x, hi.x, lo.x);
-    split1(v.y, hi.y, lo.y);
-    split1(v.z, hi.z, lo.z);
-    split1(v.w, hi.w, lo.w);
+    tf32_split_rn(v.x, hi.x, lo.x);
+    tf32_split_rn(v.y, hi.y, lo.y);
+    tf32_split_rn(v.z, hi.z, lo.z);
+    tf32_split_rn(v.w, hi.w, lo.w);
 }
 // Shared memory written by the threads -> visible to the tensor cores.
 FB2_DEV void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }

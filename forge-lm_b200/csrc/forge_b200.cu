@@ -625,12 +625,12 @@ constexpr int kTcMinRows = 512;
 static bool launch_gemm_tc(cudaStream_t st, int sm_count, int M, int K, int N, const float* A, float* ahi, float* alo,
                            const CUtensorMap* bmaps, Epi e, int* err, float* part, size_t part_cap, int64_t* launches) {
     if (M <= kMaxGemvRows || (K % 4) || (N % 4)) return false;
-    launch_split_tf32(st, A, (size_t)M * K, ahi, alo);
-    (*launches)++;
     TcMaps maps;
     maps.b_hi = bmaps[0];
     maps.b_lo = bmaps[1];
     if (M >= kTcMinRows) {
+        launch_split_tf32(st, A, (size_t)M * K, ahi, alo);
+        (*launches)++;
         if (!tc_encode(&maps.a_hi, ahi, K, M, TC_BM) || !tc_encode(&maps.a_lo, alo, K, M, TC_BM))
             fail(FB2_CUDA_ERROR, "cuTensorMapEncodeTiled failed for a GEMM operand");
         (*launches)++;
@@ -638,9 +638,10 @@ static bool launch_gemm_tc(cudaStream_t st, int sm_count, int M, int K, int N, c
         launch_pdl(k_gemm_tc<128>, std::min(tiles, sm_count), TCP_THREADS, TcCfg<128>::SMEM, st, maps, M, N, K, e, err);
         return true;
     }
+    // decode batches: the kernel splits A's tiles itself (maps.a_hi = A)
     const int bnb = M <= 64 ? 64 : 128;
-    if (!tc_encode(&maps.a_hi, ahi, K, M, bnb) || !tc_encode(&maps.a_lo, alo, K, M, bnb))
-        fail(FB2_CUDA_ERROR, "cuTensorMapEncodeTiled failed for a GEMM operand");
+    if (!tc_encode(&maps.a_hi, A, K, M, bnb)) fail(FB2_CUDA_ERROR, "cuTensorMapEncodeTiled failed for a GEMM operand");
+    maps.a_lo = maps.a_hi;
     const int tiles = ceil_div(N, 128) * ceil_div(M, bnb), nk = ceil_div(K, TC_BK);
     int S = std::max(1, std::min({kTcSplitMax, nk, sm_count / tiles}));
     S = ceil_div(nk, ceil_div(nk, S));  // balanced k blocks per split

@@ -154,6 +154,17 @@ FB2_DEV void tf32_split(float x, float& hi, float& lo) {
     hi = tf32_round(x);
     lo = tf32_round(x - hi);
 }
+// The same rounding in one instruction (cvt.rn: to nearest, ties to even;
+// the 13 low bits cleared explicitly).
+FB2_DEV float tf32_rn(float x) {
+    uint32_t r;
+    asm("cvt.rn.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r & 0xFFFFE000u);
+}
+FB2_DEV void tf32_split_rn(float x, float& hi, float& lo) {
+    hi = tf32_rn(x);
+    lo = tf32_rn(x - hi);
+}
 
 // W [K][N] -> W^T halves hiT, loT [N][K] (32 x 32 tiles through shared memory).
 __global__ void k_split_tf32_transpose(const float* __restrict__ W, int K, int N, float* __restrict__ hiT,
@@ -353,6 +364,10 @@ __global__ void __launch_bounds__(TCP_THREADS, 1) k_gemm_tc(const __grid_constan
 // column n, TMEM column = batch row m.  gridDim = (ceil(N/128),
 // ceil(M/BNB), S): with S > 1 each CTA writes partial[z][M][N] and
 // k_splitk_reduce sums the splits in order and applies the epilogue.
+// The batch rows arrive as plain fp32 (maps.a_hi describes A itself): per
+// stage, warps 2-3 split the landed tile in place into its TF32 halves
+// (the swizzled positions are the same for A, hi and lo) and release it to
+// the MMA warp through split[stage], so no separate split kernel runs.
 template <int BNB>
 struct TcSwabCfg {
     static constexpr int TILE_B = BNB * TC_BK * 4;
@@ -367,7 +382,7 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc_swab(const __grid_constant__
     using Cfg = TcSwabCfg<BNB>;
     constexpr int STAGES = Cfg::STAGES, STAGE = Cfg::STAGE, TILE_B = Cfg::TILE_B;
     extern __shared__ unsigned char tc_smem_raw[];
-    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], accb;
+    __shared__ __align__(8) uint64_t full[STAGES], split[STAGES], empty[STAGES], accb;
     __shared__ uint32_t tmem_base;
     __shared__ volatile int s_abort;
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -382,6 +397,7 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc_swab(const __grid_constant__
         s_abort = 0;
         for (int i = 0; i < STAGES; i++) {
             tc::bar_init(&full[i], 1);
+            tc::bar_init(&split[i], 2);  // one arrival per splitting warp
             tc::bar_init(&empty[i], 1);
         }
         tc::bar_init(&accb, 1);
@@ -404,19 +420,42 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc_swab(const __grid_constant__
             const int st = i % STAGES;
             if (i >= STAGES && !tc::bar_wait(&empty[st], ((i / STAGES) - 1) & 1, &s_abort)) break;
             unsigned char* sb = sm + (size_t)st * STAGE;
-            tc::bar_expect_tx(&full[st], STAGE);
+            tc::bar_expect_tx(&full[st], 2 * TC_TILE_A + TILE_B);
             const int k0 = (kb0 + i) * TC_BK;
-            // maps.b_* = weights W^T (128-row boxes), maps.a_* = batch rows (BNB-row boxes)
+            // maps.b_* = weights W^T (128-row boxes), maps.a_hi = batch rows A (BNB-row boxes, fp32)
             tc::tma_load_2d(sb, &maps.b_hi, k0, n0, &full[st]);
             tc::tma_load_2d(sb + TC_TILE_A, &maps.b_lo, k0, n0, &full[st]);
             tc::tma_load_2d(sb + 2 * TC_TILE_A, &maps.a_hi, k0, m0, &full[st]);
-            tc::tma_load_2d(sb + 2 * TC_TILE_A + TILE_B, &maps.a_lo, k0, m0, &full[st]);
+        }
+    } else if (warp >= 2) {
+        // A tile -> TF32 halves in place (x_hi) and into x_lo
+        const int t = tid - 64;
+        for (int i = 0; i < nk; i++) {
+            const int st = i % STAGES;
+            const bool ok = tc::bar_wait(&full[st], (i / STAGES) & 1, &s_abort);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            float4* xh = reinterpret_cast<float4*>(sm + (size_t)st * STAGE + 2 * TC_TILE_A);
+            float4* xl = reinterpret_cast<float4*>(sm + (size_t)st * STAGE + 2 * TC_TILE_A + TILE_B);
+#pragma unroll 4
+            for (int j = t; j < TILE_B / 16; j += 64) {
+                const float4 v = xh[j];
+                float4 h, l;
+                tf32_split_rn(v.x, h.x, l.x);
+                tf32_split_rn(v.y, h.y, l.y);
+                tf32_split_rn(v.z, h.z, l.z);
+                tf32_split_rn(v.w, h.w, l.w);
+                xh[j] = h;
+                xl[j] = l;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_addr(&split[st])) : "memory");
         }
     } else if (warp == 1 && lane == 0) {
         constexpr uint32_t idesc = tc::idesc_tf32(128, BNB);
         for (int i = 0; i < nk; i++) {
             const int st = i % STAGES;
-            if (!tc::bar_wait(&full[st], (i / STAGES) & 1, &s_abort)) break;
+            if (!tc::bar_wait(&split[st], (i / STAGES) & 1, &s_abort)) break;
             tc::fence_after();
             const uint32_t sa = tc::smem_addr(sm + (size_t)st * STAGE);
             const uint32_t w_hi = sa, w_lo = sa + TC_TILE_A, x_hi = sa + 2 * TC_TILE_A, x_lo = x_hi + TILE_B;
