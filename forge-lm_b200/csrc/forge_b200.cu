@@ -662,8 +662,11 @@ static bool launch_gemm_tc(cudaStream_t st, int sm_count, int M, int K, int N, c
 // selects the tensor-core GEMM when it applies.
 static void launch_linear(DeviceSession& s, int M, int K, int N, const float* A, const float* W, Epi e,
                           const CUtensorMap* bmaps) {
-    // bf16 weights: decode batches stay on the bf16 gemv (half the bytes)
-    if (bmaps && s.d_ahi && !(s.dm->bf16 && M < kTcMinRows) &&
+    // bf16 weights: batches of <= 16 rows stay on the bf16 gemv (half the
+    // bytes); larger batches take the tensor cores like fp32 weights (the
+    // TF32 halves of the bf16-rounded values are exact), which measured
+    // faster than a bf16 gemv pass per 16 rows
+    if (bmaps && s.d_ahi && !(s.dm->bf16 && M <= kMaxGemvRows) &&
         launch_gemm_tc(s.stream, s.dm->sm_count, M, K, N, A, s.d_ahi, s.d_alo, bmaps, e, s.d_tc_err, s.d_tc_part,
                        s.tc_part_cap, &s.stats.kernel_launches))
         return;

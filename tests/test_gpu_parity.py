@@ -263,15 +263,17 @@ def test_bf16_weights(pkg, O, monkeypatch):
     rng = np.random.default_rng(17)
     toks = rng.integers(0, shape[0], (2, 60)).astype(np.int32)
     prompts = [rng.integers(0, shape[0], L).astype(np.int32) for L in (20, 33, 47)]
+    batch20 = [rng.integers(0, shape[0], 5 + i).astype(np.int32) for i in range(20)]
     for mode in ("persistent", "graph"):
         if mode == "graph":
             monkeypatch.setenv("FORGE_B200_DECODE", "graph")
-        be = pkg.B200Backend(pkg.ModelConfig(*shape), params, devices=[0], max_seqs=3, weight_dtype="bf16")
+        be = pkg.B200Backend(pkg.ModelConfig(*shape), params, devices=[0], max_seqs=20, weight_dtype="bf16")
         with be:
             tf = be.teacher_forced_logits(toks, 40)
             got1 = be.generate(prompts[0].tolist(), 40, 0.7, 30, pkg.DotNetRandom(3), repetition_penalty=1.1,
                                no_repeat_ngram_size=4)
             gotb = be.generate_batch([p.tolist() for p in prompts], 24, 0.0, 0)
+            got20 = be.generate_batch([p.tolist() for p in batch20], 6, 0.0, 0)  # decode rows on the tensor cores
         for s_ in range(2):
             for k in (0, 9, 20):
                 want = O.forward_last(ocfg, rparams, toks[s_, :40 + k])
@@ -283,6 +285,9 @@ def test_bf16_weights(pkg, O, monkeypatch):
         check_ids(O, ocfg, rparams, prompts[0], got1, want1)
         for i, p in enumerate(prompts):
             check_ids(O, ocfg, rparams, p, gotb[i], O.generate(ocfg, rparams, p, 24, 0.0, 0, O.DotNetRandom(1)))
+        if mode == "graph":
+            for i, p in enumerate(batch20):
+                check_ids(O, ocfg, rparams, p, got20[i], O.generate(ocfg, rparams, p, 6, 0.0, 0, O.DotNetRandom(1)))
 
 
 def test_forgemodel_checkpoint_round_trip(pkg, O, tmp_path):
@@ -433,3 +438,36 @@ def test_streaming_callback_and_session_rng(pkg, O):
     r = O.DotNetRandom(5)
     want = O.generate(ocfg, params, [1, 2, 3], 7, 0.8, 0, r)
     check_ids(O, ocfg, params, [1, 2, 3], out[0], want)
+
+
+def test_tensor_core_attention_blocks_and_offsets(pkg, O, monkeypatch):
+    """The tcgen05 prefill attention (head_dim 64): windows that end on and
+    around its 64-key tiles and 128-query blocks, against the oracle and
+    against the SIMT kernel (FORGE_B200_ATTN=simt) on the same inputs; and a
+    chat turn whose prefill starts inside a query block."""
+    shape = (512, 400, 128, 2, 2)  # head_dim 64
+    lens = [1, 63, 64, 65, 127, 128, 129, 200, 257, 400]
+    rng = np.random.default_rng(17)
+    wins = [rng.integers(0, shape[0], L).astype(np.int32) for L in lens]
+    ocfg, params, be = make(pkg, O, shape, 3, max_seqs=len(lens))
+    with be:
+        tc = be.forward_last_batch(wins)
+    for i, w in enumerate(wins):
+        assert relerr(tc[i], O.forward_last(ocfg, params, w)) <= TOL, f"window len {lens[i]}"
+    monkeypatch.setenv("FORGE_B200_ATTN", "simt")
+    be2 = pkg.B200Backend(pkg.ModelConfig(*shape), params, devices=[0], max_seqs=len(lens))
+    with be2:
+        simt = be2.forward_last_batch(wins)
+    monkeypatch.delenv("FORGE_B200_ATTN")
+    for i in range(len(lens)):
+        assert relerr(tc[i], simt[i]) <= 1e-4, f"tensor-core vs SIMT attention, window len {lens[i]}"
+    # second chat turn: the cache holds 158 positions, the prefill starts at 157
+    ocfg, params, be = make(pkg, O, shape, 4)
+    p1 = rng.integers(0, shape[0], 150).astype(np.int32).tolist()
+    with be:
+        g1 = be.generate(p1, 8, 0.0, 0, None)
+        p2 = p1 + list(g1) + rng.integers(0, shape[0], 5).astype(np.int32).tolist()
+        be.reset_stats()
+        g2 = be.generate(p2, 10, 0.0, 0, None)
+        assert be.stats()["reused_prefix_rows"] == len(p1) + len(g1) - 1
+    check_ids(O, ocfg, params, np.array(p2), g2, O.generate(ocfg, params, np.array(p2), 10, 0.0, 0, O.DotNetRandom(1)))
