@@ -389,14 +389,22 @@ __global__ void __launch_bounds__(128) k_attn_decode_partial(const float* __rest
     const float4 qv = *reinterpret_cast<const float4*>(q + (size_t)r * D + h * HD + sub * 4);
     const float* Kb = kv_layer + (size_t)R.seq[r] * kv_slot_stride + (size_t)h * ctx * HD;
     const float* Vb = Kb + v_offset;
+    // this lane group's keys j = k0 + (4i + warp) KPW + grp: every K and V
+    // load of the chunk is issued before the first is used (one round trip)
+    constexpr int ROUNDS = (kAttnChunk + 4 * KPW - 1) / (4 * KPW);
+    float4 kk[ROUNDS], vv[ROUNDS];
+#pragma unroll
+    for (int i = 0; i < ROUNDS; i++) {
+        const int j = k0 + (4 * i + warp) * KPW + grp;
+        const bool in = j < k1;
+        kk[i] = in ? ld_cg4(reinterpret_cast<const float4*>(Kb + (size_t)j * HD + sub * 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        vv[i] = in ? ld_cg4(reinterpret_cast<const float4*>(Vb + (size_t)j * HD + sub * 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     // scores
-    for (int j0 = k0 + warp * KPW; j0 < k1; j0 += 4 * KPW) {
-        int j = j0 + grp;
-        float d = 0.f;
-        if (j < k1) {
-            float4 kk = ld_cg4(reinterpret_cast<const float4*>(Kb + (size_t)j * HD + sub * 4));
-            d = qv.x * kk.x + qv.y * kk.y + qv.z * kk.z + qv.w * kk.w;
-        }
+#pragma unroll
+    for (int i = 0; i < ROUNDS; i++) {
+        const int j = k0 + (4 * i + warp) * KPW + grp;
+        float d = qv.x * kk[i].x + qv.y * kk[i].y + qv.z * kk[i].z + qv.w * kk[i].w;
 #pragma unroll
         for (int o = LPK / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
         if (j < k1 && sub == 0) sc[j - k0] = d * scale;
@@ -420,10 +428,12 @@ __global__ void __launch_bounds__(128) k_attn_decode_partial(const float* __rest
     __syncthreads();
     // P.V: lane group accumulates its keys over 4 dims
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = k0 + warp * KPW + grp; j < k1; j += 4 * KPW) {
-        float p = sc[j - k0];
-        float4 vv = ld_cg4(reinterpret_cast<const float4*>(Vb + (size_t)j * HD + sub * 4));
-        acc.x += p * vv.x; acc.y += p * vv.y; acc.z += p * vv.z; acc.w += p * vv.w;
+#pragma unroll
+    for (int i = 0; i < ROUNDS; i++) {
+        const int j = k0 + (4 * i + warp) * KPW + grp;
+        if (j >= k1) break;
+        const float p = sc[j - k0];
+        acc.x += p * vv[i].x; acc.y += p * vv[i].y; acc.z += p * vv[i].z; acc.w += p * vv[i].w;
     }
 #pragma unroll
     for (int o = LPK; o < 32; o <<= 1) {
