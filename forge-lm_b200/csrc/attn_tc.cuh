@@ -84,11 +84,13 @@ FB2_DEV void mma_3x(uint32_t d, uint32_t a_hi, uint32_t a_lo, int a_rows, uint32
 }  // namespace atc
 
 // qblk[b] = {first row, count (<= 128), sequence slot, first position}; the
-// block's rows are that sequence's consecutive positions.
+// block's rows are that sequence's consecutive positions.  ctx_lo != null:
+// ctx_out and ctx_lo receive the TF32 halves of the result (the operand of
+// the next tensor-core GEMM, as k_split_tf32 would make it).
 __global__ void __launch_bounds__(ATC_THREADS, 1)
     k_attn_prefill_tc(const float* __restrict__ q, const float* __restrict__ kv_layer, long long kv_slot_stride,
                       long long v_offset, int H, int ctx, float scale, const int4* __restrict__ qblk,
-                      float* __restrict__ ctx_out, int* err) {
+                      float* __restrict__ ctx_out, int* err, float* __restrict__ ctx_lo) {
     extern __shared__ unsigned char atc_smem_raw[];
     __shared__ __align__(8) uint64_t bar_s, bar_o, drain;
     __shared__ uint32_t tmem_base;
@@ -296,10 +298,23 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     }
     if (!s_abort && r < nq) {
         const float inv = 1.0f / l;
-        float4* out = reinterpret_cast<float4*>(ctx_out + (size_t)(row0 + r) * D + h * ATC_HD + 32 * half);
+        const size_t at = (size_t)(row0 + r) * D + h * ATC_HD + 32 * half;
+        float4* out = reinterpret_cast<float4*>(ctx_out + at);
 #pragma unroll
-        for (int d4 = 0; d4 < 8; d4++)
-            out[d4] = make_float4(o[4 * d4] * inv, o[4 * d4 + 1] * inv, o[4 * d4 + 2] * inv, o[4 * d4 + 3] * inv);
+        for (int d4 = 0; d4 < 8; d4++) {
+            const float4 v = make_float4(o[4 * d4] * inv, o[4 * d4 + 1] * inv, o[4 * d4 + 2] * inv, o[4 * d4 + 3] * inv);
+            if (ctx_lo) {
+                float4 hi, lo;
+                tf32_split(v.x, hi.x, lo.x);
+                tf32_split(v.y, hi.y, lo.y);
+                tf32_split(v.z, hi.z, lo.z);
+                tf32_split(v.w, hi.w, lo.w);
+                out[d4] = hi;
+                reinterpret_cast<float4*>(ctx_lo + at)[d4] = lo;
+            } else {
+                out[d4] = v;
+            }
+        }
     }
     if (s_abort && tid == 0) {
         atomicExch(err, TC_ERR_TIMEOUT);

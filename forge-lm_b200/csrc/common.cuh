@@ -8,6 +8,31 @@
 namespace fb2 {
 
 constexpr int kWarp = 32;
+
+// TF32 halves of an fp32 value for the 3xTF32 tensor-core products:
+// x = hi + lo with hi = x rounded to TF32 and lo = (x - hi) rounded to TF32.
+// Round to the nearest TF32 value (ties to even), kept in an fp32 container.
+FB2_DEV float tf32_round(float x) {
+    const uint32_t b = __float_as_uint(x);
+    if ((b & 0x7F800000u) == 0x7F800000u) return x;  // inf / nan unchanged
+    return __uint_as_float((b + 0x0FFFu + ((b >> 13) & 1u)) & 0xFFFFE000u);
+}
+FB2_DEV void tf32_split(float x, float& hi, float& lo) {
+    hi = tf32_round(x);
+    lo = tf32_round(x - hi);
+}
+// The same rounding in one instruction (cvt.rn: to nearest, ties to even;
+// the 13 low bits cleared explicitly).
+FB2_DEV float tf32_rn(float x) {
+    uint32_t r;
+    asm("cvt.rn.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r & 0xFFFFE000u);
+}
+FB2_DEV void tf32_split_rn(float x, float& hi, float& lo) {
+    hi = tf32_rn(x);
+    lo = tf32_rn(x - hi);
+}
+
 constexpr float kLnEps = 1e-5f;  // LayerNorm eps (src/LLM.Core/Model/Layers.cs:106)
 
 FB2_DEV float warp_sum(float v) {

@@ -455,6 +455,7 @@ struct DeviceSession {
     float *d_x = nullptr, *d_x2 = nullptr, *d_ln = nullptr, *d_q = nullptr, *d_att = nullptr, *d_h = nullptr;
     float *d_ahi = nullptr, *d_alo = nullptr;  // TF32 halves of a GEMM's A operand
     int* d_tc_err = nullptr;
+    float *d_ahi2 = nullptr, *d_alo2 = nullptr;  // TF32 halves of the MLP hidden rows (prefill)
     float* d_tc_part = nullptr;  // split-K partial tiles of the decode GEMM
     size_t tc_part_cap = 0;
     float *d_logits = nullptr, *d_lnf = nullptr;
@@ -564,7 +565,7 @@ static void session_free(DeviceSession* s) {
     dfree(s->d_len); dfree(s->d_count); dfree(s->d_done); dfree(s->d_hist); dfree(s->d_kv);
     dfree(s->d_row_seq); dfree(s->d_row_pos); dfree(s->d_row_hidx); dfree(s->d_row_active); dfree(s->d_ones);
     dfree(s->d_x); dfree(s->d_x2); dfree(s->d_ln); dfree(s->d_q); dfree(s->d_att); dfree(s->d_h);
-    dfree(s->d_ahi); dfree(s->d_alo); dfree(s->d_tc_err); dfree(s->d_tc_part);
+    dfree(s->d_ahi); dfree(s->d_alo); dfree(s->d_ahi2); dfree(s->d_alo2); dfree(s->d_tc_err); dfree(s->d_tc_part);
     dfree(s->d_logits); dfree(s->d_lnf); dfree(s->d_attn_part); dfree(s->d_gemv_part); dfree(s->d_tickets);
     dfree(s->d_tab); dfree(s->d_uni); dfree(s->d_out);
     dfree(s->mk_xq); dfree(s->mk_xacc); dfree(s->mk_cval); dfree(s->mk_cidx); dfree(s->mk_stepdone);
@@ -581,12 +582,12 @@ static void session_free(DeviceSession* s) {
 // launch helpers
 // ---------------------------------------------------------------------------
 static void launch_layernorm(DeviceSession& s, int rows, const float* x, const float* w, const float* b, float* y,
-                             const int* row_map) {
+                             const int* row_map, float* y_lo = nullptr) {
     int D = s.model->D;
     int per = ceil_div(D, 32);
     dim3 grid(ceil_div(rows, 8)), block(256);
 #define LN_CASE(P) \
-    if (per <= P) { s.stats.kernel_launches++; launch_pdl(k_layernorm<P>, grid, block, 0, s.stream, rows, D, x, w, b, y, row_map); return; }
+    if (per <= P) { s.stats.kernel_launches++; launch_pdl(k_layernorm<P>, grid, block, 0, s.stream, rows, D, x, w, b, y, row_map, y_lo); return; }
     LN_CASE(1) LN_CASE(2) LN_CASE(4) LN_CASE(8) LN_CASE(16) LN_CASE(24) LN_CASE(32) LN_CASE(48) LN_CASE(64)
 #undef LN_CASE
     fail(FB2_UNSUPPORTED, "d_model too large for the LayerNorm kernel");
@@ -622,15 +623,20 @@ static void launch_linear(DeviceSession& s, int M, int K, int N, const float* A,
 constexpr int kTcMinRows = 512;
 
 // The launch of one tensor-core projection; false when it does not apply.
+// a_split: A's TF32 halves are already in ahi / alo (written by the producer
+// of A); prefill only.
 static bool launch_gemm_tc(cudaStream_t st, int sm_count, int M, int K, int N, const float* A, float* ahi, float* alo,
-                           const CUtensorMap* bmaps, Epi e, int* err, float* part, size_t part_cap, int64_t* launches) {
+                           const CUtensorMap* bmaps, Epi e, int* err, float* part, size_t part_cap, int64_t* launches,
+                           bool a_split = false) {
     if (M <= kMaxGemvRows || (K % 4) || (N % 4)) return false;
     TcMaps maps;
     maps.b_hi = bmaps[0];
     maps.b_lo = bmaps[1];
     if (M >= kTcMinRows) {
-        launch_split_tf32(st, A, (size_t)M * K, ahi, alo);
-        (*launches)++;
+        if (!a_split) {
+            launch_split_tf32(st, A, (size_t)M * K, ahi, alo);
+            (*launches)++;
+        }
         if (!tc_encode(&maps.a_hi, ahi, K, M, TC_BM) || !tc_encode(&maps.a_lo, alo, K, M, TC_BM))
             fail(FB2_CUDA_ERROR, "cuTensorMapEncodeTiled failed for a GEMM operand");
         (*launches)++;
@@ -671,6 +677,15 @@ static void launch_linear(DeviceSession& s, int M, int K, int N, const float* A,
                        s.tc_part_cap, &s.stats.kernel_launches))
         return;
     launch_linear(s, M, K, N, A, W, e);
+}
+
+// Prefill projection whose operand's TF32 halves the producer already wrote
+// (ahi / alo); the caller checked that the tensor-core path applies.
+static void launch_linear_split(DeviceSession& s, int M, int K, int N, float* ahi, float* alo, const CUtensorMap* bmaps,
+                                Epi e) {
+    if (!launch_gemm_tc(s.stream, s.dm->sm_count, M, K, N, nullptr, ahi, alo, bmaps, e, s.d_tc_err, s.d_tc_part,
+                        s.tc_part_cap, &s.stats.kernel_launches, true))
+        fail(FB2_CUDA_ERROR, "tensor-core GEMM refused a pre-split operand");
 }
 
 static void launch_linear(DeviceSession& s, int M, int K, int N, const float* A, const float* W, Epi e) {
@@ -767,14 +782,18 @@ struct QBlocks {
     const int4* b2;
 };
 
-static void launch_attn_prefill(DeviceSession& s, QBlocks qb, int layer) {
+// ctx_hi / ctx_lo (optional): where the tensor-core kernel writes the TF32
+// halves of the result instead of s.d_att; returns whether it did.
+static bool launch_attn_prefill(DeviceSession& s, QBlocks qb, int layer, float* ctx_hi = nullptr,
+                                float* ctx_lo = nullptr) {
     const fb2_model& m = *s.model;
     if (s.dm->attn_tc && s.dm->tc_ok && s.d_tc_err && qb.b2 && qb.n2 > 0) {
         const float* kvl = s.d_kv + (size_t)layer * s.kv_layer_stride;
         s.stats.kernel_launches++;
         launch_pdl(k_attn_prefill_tc, dim3(qb.n2, m.H), ATC_THREADS, (size_t)ATC_SMEM, s.stream, s.d_q, kvl,
-                   s.kv_slot_stride, s.v_offset, m.H, m.ctx, 1.0f / sqrtf((float)m.hd), qb.b2, s.d_att, s.d_tc_err);
-        return;
+                   s.kv_slot_stride, s.v_offset, m.H, m.ctx, 1.0f / sqrtf((float)m.hd), qb.b2,
+                   ctx_lo ? ctx_hi : s.d_att, s.d_tc_err, ctx_lo);
+        return ctx_lo != nullptr;
     }
     const int nblk = qb.n;
     const int4* qblk = qb.b;
@@ -787,6 +806,7 @@ static void launch_attn_prefill(DeviceSession& s, QBlocks qb, int layer) {
     case 128: launch_attn_prefill_hd<128>(s, nblk, qblk, layer); break;
     default: fail(FB2_UNSUPPORTED, "head_dim must be a power of two in [4, 128]");
     }
+    return false;
 }
 
 static void launch_head(DeviceSession& s, int M, const float* xln, const int* out_slot_host_unused,
@@ -838,6 +858,21 @@ static void run_layers(DeviceSession& s, int M, Rows R, bool decode, QBlocks qb)
         eq.ctx = m.ctx;
         eq.R = R;
         const CUtensorMap* tcm = s.dm->tc_ok ? s.dm->tc_maps[l].data() : nullptr;
+        if (!decode && tcm && s.d_ahi2 && M >= kTcMinRows) {
+            // prefill on the tensor cores: LN1, the attention, LN2 and fc write
+            // their outputs as the next GEMM's TF32 halves (no split kernels)
+            launch_layernorm(s, M, s.d_x, w.ln1_w, w.ln1_b, s.d_ahi, nullptr, s.d_alo);
+            launch_linear_split(s, M, m.D, 3 * m.D, s.d_ahi, s.d_alo, tcm, eq);
+            const Epi ep = make_epi(EPI_RESID, w.proj_b, s.d_x, s.d_x2);
+            if (launch_attn_prefill(s, qb, l, s.d_ahi, s.d_alo)) launch_linear_split(s, M, m.D, m.D, s.d_ahi, s.d_alo, tcm + 2, ep);
+            else launch_linear(s, M, m.D, m.D, s.d_att, w.proj_w, ep, tcm + 2);
+            launch_layernorm(s, M, s.d_x2, w.ln2_w, w.ln2_b, s.d_ahi, nullptr, s.d_alo);
+            Epi ef = make_epi(EPI_GELU_SPLIT, w.fc_b, nullptr, s.d_ahi2);
+            ef.out_lo = s.d_alo2;
+            launch_linear_split(s, M, m.D, m.F, s.d_ahi, s.d_alo, tcm + 4, ef);
+            launch_linear_split(s, M, m.F, m.D, s.d_ahi2, s.d_alo2, tcm + 6, make_epi(EPI_RESID, w.mproj_b, s.d_x2, s.d_x));
+            continue;
+        }
         launch_linear(s, M, m.D, 3 * m.D, s.d_ln, w.qkv_w, eq, tcm);
         if (decode) launch_attn_decode(s, M, l, R);
         else launch_attn_prefill(s, qb, l);
@@ -1743,6 +1778,8 @@ int32_t fb2_session_create(fb2_model* m, int32_t max_seqs, fb2_session** out) {
                 if (s->dm->tc_ok) {
                     s->d_ahi = dalloc<float>(rc * F);
                     s->d_alo = dalloc<float>(rc * F);
+                    s->d_ahi2 = dalloc<float>(rc * F);
+                    s->d_alo2 = dalloc<float>(rc * F);
                     s->d_tc_err = dalloc<int>(1);
                     CK(cudaMemset(s->d_tc_err, 0, sizeof(int)));
                     s->tc_part_cap = (size_t)kTcSplitMax * 128 * (size_t)(4 * D);

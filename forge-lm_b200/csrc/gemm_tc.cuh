@@ -144,28 +144,6 @@ FB2_DEV void tmem_ld16(uint32_t taddr, float* v) {
 
 }  // namespace tc
 
-// Round to the nearest TF32 value (ties to even), kept in an fp32 container.
-FB2_DEV float tf32_round(float x) {
-    const uint32_t b = __float_as_uint(x);
-    if ((b & 0x7F800000u) == 0x7F800000u) return x;  // inf / nan unchanged
-    return __uint_as_float((b + 0x0FFFu + ((b >> 13) & 1u)) & 0xFFFFE000u);
-}
-FB2_DEV void tf32_split(float x, float& hi, float& lo) {
-    hi = tf32_round(x);
-    lo = tf32_round(x - hi);
-}
-// The same rounding in one instruction (cvt.rn: to nearest, ties to even;
-// the 13 low bits cleared explicitly).
-FB2_DEV float tf32_rn(float x) {
-    uint32_t r;
-    asm("cvt.rn.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r & 0xFFFFE000u);
-}
-FB2_DEV void tf32_split_rn(float x, float& hi, float& lo) {
-    hi = tf32_rn(x);
-    lo = tf32_rn(x - hi);
-}
-
 // W [K][N] -> W^T halves hiT, loT [N][K] (32 x 32 tiles through shared memory).
 __global__ void k_split_tf32_transpose(const float* __restrict__ W, int K, int N, float* __restrict__ hiT,
                                        float* __restrict__ loT) {

@@ -64,9 +64,12 @@ __global__ void k_embed(int rows, Rows R, const int* __restrict__ hist, int hist
 // LayerNorm: one warp per row, two-pass mean / biased variance
 // (CpuBackend.cs:377-398).  D <= 32 * 64.
 // ---------------------------------------------------------------------------
+// y_lo != null: y and y_lo receive the TF32 halves of the result (the
+// operand of a tensor-core GEMM, as k_split_tf32 would make it).
 template <int PER_LANE>
 __global__ void k_layernorm(int rows, int D, const float* __restrict__ x, const float* __restrict__ w,
-                            const float* __restrict__ b, float* __restrict__ y, const int* __restrict__ row_map) {
+                            const float* __restrict__ b, float* __restrict__ y, const int* __restrict__ row_map,
+                            float* __restrict__ y_lo) {
     pdl_wait();
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
@@ -93,6 +96,15 @@ __global__ void k_layernorm(int rows, int D, const float* __restrict__ x, const 
     q = warp_sum(q);
     float rs = 1.0f / sqrtf(q / (float)D + kLnEps);
     float* yr = y + (size_t)warp * D;
+    if (y_lo) {
+        float* yl = y_lo + (size_t)warp * D;
+#pragma unroll
+        for (int i = 0; i < PER_LANE; i++) {
+            int c = lane + i * 32;
+            if (c < D) tf32_split((v[i] - mu) * rs * w[c] + b[c], yr[c], yl[c]);
+        }
+        return;
+    }
 #pragma unroll
     for (int i = 0; i < PER_LANE; i++) {
         int c = lane + i * 32;
@@ -106,13 +118,14 @@ __global__ void k_layernorm(int rows, int D, const float* __restrict__ x, const 
 //   EPI_GELU : GELU (Mlp.Forward, Layers.cs:306-313)
 //   EPI_QKV  : Q to q_out, K/V appended to the cache at the row's position.
 // ---------------------------------------------------------------------------
-enum EpiKind { EPI_BIAS = 0, EPI_RESID = 1, EPI_GELU = 2, EPI_QKV = 3 };
+enum EpiKind { EPI_BIAS = 0, EPI_RESID = 1, EPI_GELU = 2, EPI_QKV = 3, EPI_GELU_SPLIT = 4 };
 
 struct Epi {
     int kind;
     const float* bias;
     const float* resid;  // [M][N] for EPI_RESID
-    float* out;          // [M][N] (or q [M][D] for EPI_QKV)
+    float* out;          // [M][N] (or q [M][D] for EPI_QKV; the TF32 hi half for EPI_GELU_SPLIT)
+    float* out_lo;       // [M][N] the TF32 lo half (EPI_GELU_SPLIT)
     // EPI_QKV
     float* kv_layer;     // cache + layer offset (slot 0)
     long long kv_slot_stride;
@@ -128,6 +141,12 @@ FB2_DEV void epi_store1(const Epi& e, int m, int n, int N, float a) {
         a += e.resid[(size_t)m * N + n];
     } else if (e.kind == EPI_GELU) {
         a = gelu_tanh(a);
+    } else if (e.kind == EPI_GELU_SPLIT) {
+        float h, l;
+        tf32_split(gelu_tanh(a), h, l);
+        e.out[(size_t)m * N + n] = h;
+        e.out_lo[(size_t)m * N + n] = l;
+        return;
     } else if (e.kind == EPI_QKV) {
         const int D = e.D;
         if (n < D) {
@@ -154,6 +173,16 @@ FB2_DEV void epi_store4(const Epi& e, int m, int n, int N, float4 a) {
         a.x += r.x; a.y += r.y; a.z += r.z; a.w += r.w;
     } else if (e.kind == EPI_GELU) {
         a.x = gelu_tanh(a.x); a.y = gelu_tanh(a.y); a.z = gelu_tanh(a.z); a.w = gelu_tanh(a.w);
+    } else if (e.kind == EPI_GELU_SPLIT) {  // the next GEMM's operand, as k_split_tf32 would make it
+        a.x = gelu_tanh(a.x); a.y = gelu_tanh(a.y); a.z = gelu_tanh(a.z); a.w = gelu_tanh(a.w);
+        float4 h, l;
+        tf32_split(a.x, h.x, l.x);
+        tf32_split(a.y, h.y, l.y);
+        tf32_split(a.z, h.z, l.z);
+        tf32_split(a.w, h.w, l.w);
+        *reinterpret_cast<float4*>(e.out + (size_t)m * N + n) = h;
+        *reinterpret_cast<float4*>(e.out_lo + (size_t)m * N + n) = l;
+        return;
     } else if (e.kind == EPI_QKV) {
         int D = e.D;
         if (n < D) {
