@@ -86,8 +86,10 @@ struct MkArgs {
 // Trace points per step: 12 per layer for layers 0 and 1 (level A start, after
 // LN1, after QKV, after attention units, after combine weights, after ctx,
 // after proj, after x2 gather, after LN2, after fc, after h gather, after
-// proj2), 24 step start, 25 head input, 27 head logits, 28 candidates,
-// 30 published, 31 token known, 32 step end, 33 + l end of layer l.
+// proj2), 24 step start, 25 head input, 26 after LN_f, 27 head logits,
+// 28 candidates, 29 first head stage ready, 30 published, 31 token known,
+// 32 step end, 33 + l end of layer l, 45 middle head stage, 46 (a duration,
+// not a stamp) thread 0's time in the head's ring waits, 57-62 sampler.
 constexpr int MK_TRACE_POINTS = 64;
 constexpr int MK_ERR_LAYOUT = 16;  // error code: a shared-memory region would be misaligned
 
@@ -1127,36 +1129,63 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         if (sampled && tid < MR)
             ud_next = a.uniforms[(size_t)s_slot[tid] * a.uni_stride + min(s_cnt0[tid] + s, max(sp.max_new - 1, 0))];
         mk_layernorm<MR>(xres, act, D, lnf, scr + 384);
+        MK_TRACE(26);
         const int v0 = (int)(((long long)cta * V) / nW), v1 = (int)(((long long)(cta + 1) * V) / nW);
         const int nsl = v1 - v0;
         {
             const int Rh = max(1, MK_STAGE / (D * 4));
+            unsigned long long head_wait = 0;  // thread 0's time inside the ring waits (traced runs)
             for (int r0 = v0; r0 < v1; r0 += Rh) {
                 const int rows = min(Rh, v1 - r0);
-                wait_full(full, it, a.nstage, a.err, &s_abort);
+                if (a.trace && tid == 0) {
+                    const unsigned long long t0 = gtimer();
+                    wait_full(full, it, a.nstage, a.err, &s_abort);
+                    head_wait += gtimer() - t0;
+                } else {
+                    wait_full(full, it, a.nstage, a.err, &s_abort);
+                }
+                if (r0 == v0) MK_TRACE(29);
+                if (r0 - v0 == ((nsl / Rh) / 2) * Rh) MK_TRACE(45);
                 const float* E = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
-                for (int r = warp; r < rows; r += 8) {
-                    float accm[MR];
+                // slice row idx = r0 - v0 + r goes to warp idx % 8: a warp with no
+                // row here moves on to the next stage while the others finish
+                // (every warp still waits for each stage before releasing it)
+                for (int r = ((warp - (r0 - v0)) % 8 + 8) % 8; r < rows; r += 8) {
+                    float acc0[MR], acc1[MR];
 #pragma unroll
-                    for (int m = 0; m < MR; m++) accm[m] = 0.f;
+                    for (int m = 0; m < MR; m++) acc0[m] = acc1[m] = 0.f;
                     const float4* er = reinterpret_cast<const float4*>(E + (size_t)r * D);
-                    for (int i = lane; i < D / 4; i += 32) {
-                        const float4 e4 = er[i];
+                    const int n4 = D / 4;
+                    int i = lane;
+                    for (; i + 32 < n4; i += 64) {
+                        const float4 e0 = er[i], e1 = er[i + 32];
 #pragma unroll
                         for (int m = 0; m < MR; m++) {
-                            const float4 x4 = *reinterpret_cast<const float4*>(act + m * D + i * 4);
-                            accm[m] += x4.x * e4.x + x4.y * e4.y + x4.z * e4.z + x4.w * e4.w;
+                            const float4 x0 = *reinterpret_cast<const float4*>(act + m * D + i * 4);
+                            const float4 x1 = *reinterpret_cast<const float4*>(act + m * D + (i + 32) * 4);
+                            acc0[m] += x0.x * e0.x + x0.y * e0.y + x0.z * e0.z + x0.w * e0.w;
+                            acc1[m] += x1.x * e1.x + x1.y * e1.y + x1.z * e1.z + x1.w * e1.w;
+                        }
+                    }
+                    if (i < n4) {
+                        const float4 e0 = er[i];
+#pragma unroll
+                        for (int m = 0; m < MR; m++) {
+                            const float4 x0 = *reinterpret_cast<const float4*>(act + m * D + i * 4);
+                            acc0[m] += x0.x * e0.x + x0.y * e0.y + x0.z * e0.z + x0.w * e0.w;
                         }
                     }
 #pragma unroll
                     for (int m = 0; m < MR; m++) {
-                        const float t = warp_sum(accm[m]);
+                        const float t = warp_sum(acc0[m] + acc1[m]);
                         if (lane == 0) slice[m * a.slice_max + (r0 - v0) + r] = t;
                     }
                 }
                 release_stage(empty, it, a.nstage);
                 it++;
             }
+            if (a.trace && tid == 0 && s < a.trace_steps)
+                a.trace[((size_t)cta * a.trace_steps + s) * MK_TRACE_POINTS + 46] = head_wait;
         }
         cons_sync();
         MK_TRACE(27);
