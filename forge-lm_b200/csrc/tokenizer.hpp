@@ -8,7 +8,8 @@
 // (BpeTokenizer.cs:353-389).
 #pragma once
 #include <cstdint>
-#include <deque>
+#include <functional>
+#include <queue>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -86,55 +87,62 @@ struct Bpe {
         return t;
     }
 
-    // BpeTokenizer.Encode (BpeTokenizer.cs:259-318): ranks in learned order;
-    // per rank a queue of positions whose pair had that rank when enqueued,
-    // merged in queue order if still current; merges enqueue the new
-    // neighbouring pairs at their (later) ranks.
+    // BpeTokenizer.Encode (BpeTokenizer.cs:259-318).  Its result is defined
+    // as rank-greedy merging: while some adjacent pair has a merge rank,
+    // merge the pair of lowest rank, its leftmost occurrence first.
+    //
+    // This implementation keeps the byte positions as nodes of a list (a node
+    // stands for the token that starts at its position) and a min-heap of
+    // candidate merges ordered by (rank, position).  A heap entry records the
+    // version of its left node; a node's version changes whenever its token
+    // or its right neighbour changes, so an entry whose pair no longer exists
+    // is recognised and dropped when it surfaces.  Popping (rank, position)
+    // in order is the rank-greedy rule: a merge only creates pairs that
+    // contain its new id, and such a pair has a higher rank than the merge
+    // that made the id (Load requires merges to reference earlier ids).
     std::vector<int32_t> encode(const uint8_t* data, size_t n) const {
         std::vector<int32_t> out;
         if (n == 0) return out;
-        std::vector<int> seq(n), next(n), prev(n);
-        for (size_t i = 0; i < n; i++) {
-            seq[i] = data[i];
-            next[i] = i + 1 < n ? (int)i + 1 : -1;
-            prev[i] = (int)i - 1;
-        }
-        std::vector<std::deque<int>> queues(left.size());
-        auto rank_of = [&](int a, int b) {
-            auto it = rank.find(key(a, b));
-            return it == rank.end() ? -1 : it->second;
+        struct Node {
+            int32_t token;
+            int32_t right;    // next live node, -1 at the end
+            int32_t left;     // previous live node, -1 at the start
+            uint32_t version;
         };
-        for (size_t i = 0; i + 1 < n; i++) {
-            const int r = rank_of(seq[i], seq[i + 1]);
-            if (r >= 0) queues[(size_t)r].push_back((int)i);
-        }
-        for (size_t r = 0; r < queues.size(); r++) {
-            std::deque<int>& q = queues[r];
-            const int new_id = 256 + (int)r;
-            while (!q.empty()) {
-                const int i = q.front();
-                q.pop_front();
-                const int j = next[(size_t)i];
-                if (j < 0) continue;
-                if (rank_of(seq[(size_t)i], seq[(size_t)j]) != (int)r) continue;  // stale
-                seq[(size_t)i] = new_id;
-                const int nj = next[(size_t)j];
-                next[(size_t)i] = nj;
-                next[(size_t)j] = -1;
-                prev[(size_t)j] = -1;
-                if (nj >= 0) {
-                    prev[(size_t)nj] = i;
-                    const int r2 = rank_of(new_id, seq[(size_t)nj]);
-                    if (r2 >= 0) queues[(size_t)r2].push_back(i);
-                }
-                const int p = prev[(size_t)i];
-                if (p >= 0) {
-                    const int r3 = rank_of(seq[(size_t)p], new_id);
-                    if (r3 >= 0) queues[(size_t)r3].push_back(p);
-                }
+        struct Cand {
+            int32_t rank, pos;
+            uint32_t version;
+            bool operator>(const Cand& o) const { return rank != o.rank ? rank > o.rank : pos > o.pos; }
+        };
+        std::vector<Node> nodes(n);
+        for (size_t i = 0; i < n; i++)
+            nodes[i] = Node{data[i], i + 1 < n ? (int32_t)(i + 1) : -1, (int32_t)i - 1, 0u};
+        std::priority_queue<Cand, std::vector<Cand>, std::greater<Cand>> heap;
+        auto offer = [&](int32_t pos) {  // the pair starting at live node pos, if it merges
+            const int32_t r = nodes[(size_t)pos].right;
+            if (r < 0) return;
+            auto it = rank.find(key(nodes[(size_t)pos].token, nodes[(size_t)r].token));
+            if (it != rank.end()) heap.push(Cand{it->second, pos, nodes[(size_t)pos].version});
+        };
+        for (size_t i = 0; i + 1 < n; i++) offer((int32_t)i);
+        while (!heap.empty()) {
+            const Cand c = heap.top();
+            heap.pop();
+            Node& a = nodes[(size_t)c.pos];
+            if (a.version != c.version) continue;  // pair changed since it was offered
+            Node& b = nodes[(size_t)a.right];
+            a.token = 256 + c.rank;
+            a.right = b.right;
+            a.version++;
+            if (b.right >= 0) nodes[(size_t)b.right].left = c.pos;
+            b.version++;  // b is absorbed; its entries are stale now
+            if (a.left >= 0) {
+                nodes[(size_t)a.left].version++;  // its right neighbour's token changed
+                offer(a.left);
             }
+            offer(c.pos);
         }
-        for (int i = 0; i >= 0; i = next[(size_t)i]) out.push_back(seq[(size_t)i]);
+        for (int32_t i = 0; i >= 0; i = nodes[(size_t)i].right) out.push_back(nodes[(size_t)i].token);
         return out;
     }
 };

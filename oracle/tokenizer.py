@@ -5,13 +5,13 @@ The library's native tokenizer (forge-lm_b200/csrc/tokenizer.hpp) is checked
 against this file.  Training restates TrainDocuments (BpeTokenizer.cs:90-236)
 as a recount-every-merge loop with the same selection rule (highest count,
 ties to the lowest pair key (left << 32) | right, at least 2 occurrences,
-no pair across a document boundary); encoding restates Encode
-(BpeTokenizer.cs:259-318) with its per-rank position queues.
+no pair across a document boundary); encoding is the rule Encode
+is defined by (rank-greedy merging, BpeTokenizer.cs:259-318), written as the
+plain repeated search for the lowest-rank pair, not as the reference's queues.
 """
 from __future__ import annotations
 
 import json
-from collections import deque
 
 
 def pair_key(left: int, right: int) -> int:
@@ -56,54 +56,32 @@ def train_documents(documents: list[bytes], num_merges: int) -> list[tuple[int, 
 
 
 def encode(data: bytes, merges: list[tuple[int, int, int]]) -> list[int]:
-    n = len(data)
-    if n == 0:
-        return []
+    """Encode's defining rule (the class remarks of BpeTokenizer.cs, restated
+    here rather than its algorithm at BpeTokenizer.cs:273-318): start from
+    the byte ids; while some adjacent pair is a learned merge, take the pair
+    of lowest rank and merge its leftmost occurrence; repeat.
+
+    One pass per chosen rank merges every occurrence of that pair left to
+    right, skipping overlaps: that is the same sequence of leftmost merges,
+    because merging a pair of rank r only creates pairs that contain the new
+    id 256 + r, and every such pair has a rank above r."""
     rank = {pair_key(l, r): k for k, (l, r, _) in enumerate(merges)}
     seq = list(data)
-    nxt = [i + 1 if i + 1 < n else -1 for i in range(n)]
-    prv = [i - 1 for i in range(n)]
-    queues: list[deque | None] = [None] * len(merges)
-
-    def push(r, i):
-        if queues[r] is None:
-            queues[r] = deque()
-        queues[r].append(i)
-
-    for i in range(n - 1):
-        r = rank.get(pair_key(seq[i], seq[i + 1]))
-        if r is not None:
-            push(r, i)
-    for r in range(len(merges)):
-        q = queues[r]
-        if q is None:
-            continue
-        new_id = merges[r][2]
-        while q:
-            i = q.popleft()
-            j = nxt[i]
-            if j < 0 or rank.get(pair_key(seq[i], seq[j])) != r:
-                continue
-            seq[i] = new_id
-            nj = nxt[j]
-            nxt[i] = nj
-            nxt[j] = -1
-            prv[j] = -1
-            if nj >= 0:
-                prv[nj] = i
-                r2 = rank.get(pair_key(new_id, seq[nj]))
-                if r2 is not None:
-                    push(r2, i)
-            p = prv[i]
-            if p >= 0:
-                r3 = rank.get(pair_key(seq[p], new_id))
-                if r3 is not None:
-                    push(r3, p)
-    out, i = [], 0
-    while i >= 0:
-        out.append(seq[i])
-        i = nxt[i]
-    return out
+    while len(seq) > 1:
+        best = min((rank[k] for k in (pair_key(a, b) for a, b in zip(seq, seq[1:])) if k in rank), default=None)
+        if best is None:
+            break
+        left, right, new_id = merges[best]
+        out, i = [], 0
+        while i < len(seq):
+            if i + 1 < len(seq) and seq[i] == left and seq[i + 1] == right:
+                out.append(new_id)
+                i += 2
+            else:
+                out.append(seq[i])
+                i += 1
+        seq = out
+    return seq
 
 
 def vocab_bytes(merges: list[tuple[int, int, int]]) -> list[bytes]:

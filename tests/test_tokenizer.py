@@ -117,3 +117,28 @@ def test_training_oracle_properties():
     assert OT.train_documents([ab], 1) == [(97, 98, 256)]
     assert len(OT.train_documents([ab], 5)) == 5
     assert OT.train_documents([b"a", b"b", b"a", b"b"], 10) == []
+
+
+def test_encode_random_tables_against_definition(pkg, tmp_path):
+    """Random merge tables (each merge joins earlier ids, as Load requires)
+    over a three-letter alphabet, so runs like "aaaa" overlap and merges nest:
+    the library's encoder against the rank-greedy definition."""
+    rng = np.random.default_rng(23)
+    for t in range(6):
+        merges, pairs = [], set()
+        ids = [97, 98, 99]
+        while len(merges) < 40:
+            a, b = int(rng.choice(ids)), int(rng.choice(ids))
+            if (a, b) in pairs:
+                continue
+            pairs.add((a, b))
+            merges.append((a, b, 256 + len(merges)))
+            ids.append(256 + len(merges) - 1)
+        path = tmp_path / f"rand{t}.json"
+        OT.save(path, merges)
+        tok = pkg.BpeTokenizer(path)
+        for n in (1, 2, 3, 7, 64, 1000):
+            data = bytes(rng.choice([97, 98, 99], n).tolist())
+            assert tok.encode(data) == OT.encode(data, merges), (t, n)
+            assert tok.decode_bytes(tok.encode(data)) == data
+        assert tok.encode(b"a" * 257) == OT.encode(b"a" * 257, merges)
