@@ -40,12 +40,11 @@ sys.path.insert(0, ROOT)
 
 FORGE_98M = dict(vocab_size=16384, context_length=1024, d_model=768, n_layers=12, n_heads=12)
 FORGE_220M = dict(vocab_size=16384, context_length=1024, d_model=1024, n_layers=16, n_heads=16)
-# DRAM bytes per decode step of the persistent kernel on the default C2
-# workload: ncu dram__bytes_read.sum + dram__bytes_write.sum of the first
-# timed launch (511 steps) / 511 (profiles/k_decode_mega_c2.md).  The weight
-# stream goes through L2 evict-first, so the sequence's K/V is served from L2
-# and the DRAM bytes are the weights alone (below the algorithmic bytes).
-MK_DRAM_BYTES_PER_STEP_C2 = (199403027712 + 28204544) / 511
+# Measured DRAM traffic of the dominant kernel is read from a record written
+# by `bench.py --record-traffic <ncu csv>` (the one-pass launch-list capture
+# with dram__bytes_read.sum and dram__bytes_write.sum); it is used only when
+# the record names the SHA-256 of the library file loaded now, else null.
+TRAFFIC_RECORD = os.path.join(ROOT, "profiles", "traffic_record.json")
 WEIGHT_SEED = 1234
 
 WORKLOADS = {
@@ -91,6 +90,10 @@ def parse():
     ap.add_argument("--new-tokens", type=int, default=None, help="override the workload's new-token count "
                     "(smaller cases for profiling; the default is the workload's)")
     ap.add_argument("--skip-e2e", action="store_true", help="omit the host-buffer e2e leg (profiling runs)")
+    ap.add_argument("--record-traffic", metavar="NCU_CSV", default=None,
+                    help="write the DRAM traffic record of --workload from an ncu --csv capture and exit")
+    ap.add_argument("--record-kernel", default="k_decode_mega")
+    ap.add_argument("--record-steps-per-launch", type=int, default=511)
     return ap.parse_args()
 
 
@@ -188,10 +191,37 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_reference_sample(wl: dict, seconds_target: float = 15.0, max_tokens: int | None = None) -> dict:
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def ref_flops_per_token(m: dict, T: int) -> float:
+    """FLOPs of one reference step (GptModel.ForwardLast of a T-token window:
+    every row through the blocks, full T x T attention scores and context
+    before the causal mask, logits of every row, Sampler.cs:91-95)."""
+    D, L, V = m["d_model"], m["n_layers"], m["vocab_size"]
+    return 2.0 * T * (L * 12 * D * D + V * D) + 4.0 * L * T * T * D
+
+
+CPU_SAMPLE_TOKENS = 40
+
+
+def cpu_reference_sample(wl: dict, n_tokens: int = CPU_SAMPLE_TOKENS, full_run: bool = True) -> dict:
     """The reference algorithm (full re-forward of the window for every token,
-    logits for every row; oracle/ restatement of CpuBackend + Sampler) on the
-    host cores: tokens/s over the first tokens of sequence 0 of the workload."""
+    logits for every row; the oracle's restatement of CpuBackend + Sampler)
+    on all host cores.  Measured: the first n_tokens of sequence 0 of the
+    workload.  Those are the cheapest tokens of the run (the window grows),
+    so with full_run the windows of the whole run are also sampled: one
+    reference step is timed at five window lengths spread over the run, a
+    cost model time(T) = a + b*flops(T) is fitted to them, and the run's
+    rate is 'tokens / sum of the model over every step'."""
     from oracle import oracle as O
     O.set_threads(0)
     m = wl["model"]
@@ -200,24 +230,48 @@ def cpu_reference_sample(wl: dict, seconds_target: float = 15.0, max_tokens: int
     if wl.get("weight_dtype") == "bf16":
         params = O.round_bf16(cfg, params)
     prompt = prompts_for(0, 1, wl["prompt_len"], m["vocab_size"])[0]
-    # calibrate: one token, then as many as fit the target time
+    n = max(1, min(wl["new_tokens"], n_tokens))
     t0 = time.perf_counter()
-    O.generate(cfg, params, prompt, 1, wl["temperature"], wl["top_k"], O.DotNetRandom(1),
-               repetition_penalty=wl["penalty"], no_repeat_ngram=wl["ngram"])
-    t1 = time.perf_counter() - t0
-    n = max(2, min(wl["new_tokens"], int(seconds_target / max(t1, 1e-3))))
-    if max_tokens:
-        n = min(n, max_tokens)
-    t0 = time.perf_counter()
-    out = O.generate(cfg, params, prompt, n, wl["temperature"], wl["top_k"], O.DotNetRandom(1),
+    ids = O.generate(cfg, params, prompt, n, wl["temperature"], wl["top_k"], O.DotNetRandom(1),
                      repetition_penalty=wl["penalty"], no_repeat_ngram=wl["ngram"])
     dt = time.perf_counter() - t0
-    return {"value": len(out) / dt, "unit": "tokens/s", "cores": O.get_threads(), "kind": "port",
-            "sample": f"first {len(out)} of {wl['new_tokens']} tokens of sequence 0 (prompt {len(prompt)}), "
-                      f"full re-forward per token as the reference CPU backend does"
-                      + ("" if len(prompt) >= m["context_length"] else
-                         "; later tokens cost more (window grows), so this over-states the full-run rate"),
-            "seconds": dt}
+    ctx = m["context_length"]
+    out = {"value": len(ids) / dt, "unit": "tokens/s", "cores": O.get_threads(), "cpu_model": cpu_model(),
+           "kind": "port",
+           "sample": f"first {len(ids)} of {wl['new_tokens']} tokens of sequence 0 (prompt {len(prompt)}), full "
+                     f"re-forward per token as the reference CPU backend does",
+           "seconds": dt, "ids": ids}
+    if full_run:
+        steps_T = [min(len(prompt) + k, ctx) for k in range(wl["new_tokens"])]
+        probe = sorted(set(int(x) for x in np.linspace(steps_T[0], steps_T[-1], 5)))
+        rng = np.random.default_rng(0)
+        secs = []
+        for T in probe:
+            w = rng.integers(0, m["vocab_size"], T).astype(np.int32)
+            t0 = time.perf_counter()
+            O.forward_last(cfg, params, w)
+            secs.append(time.perf_counter() - t0)
+        x = np.array([ref_flops_per_token(m, T) for T in probe])
+        if len(probe) > 1:
+            b, a = np.polyfit(x, np.array(secs), 1)
+        else:
+            a, b = 0.0, secs[0] / x[0]
+        total = sum(a + b * ref_flops_per_token(m, T) for T in steps_T)
+        out["full_run"] = {"value": wl["new_tokens"] / total, "unit": "tokens/s",
+                           "method": f"one reference step timed at windows {probe}; time(T) = a + b*flops(T) "
+                                     f"fitted and summed over the run's {wl['new_tokens']} steps",
+                           "window_seconds": [round(v, 4) for v in secs]}
+    return out
+
+
+def parity_vs_cpu(device_ids, cpu_ids) -> dict:
+    """Sequence 0's first device ids against the ids the CPU reference leg
+    generated (same weights, prompt and RNG seed)."""
+    dev = [int(t) for t in device_ids[:len(cpu_ids)]]
+    ref = [int(t) for t in cpu_ids]
+    first = next((i for i, (a, b) in enumerate(zip(dev, ref)) if a != b), None)
+    return {"ids_compared": len(ref), "ids_equal": sum(a == b for a, b in zip(dev, ref)),
+            "first_mismatch": first, "reference": "oracle port of the reference CPU loop (sequence 0)"}
 
 
 def run_reference(args, wl):
@@ -226,27 +280,84 @@ def run_reference(args, wl):
         return
     steps = []
     for i in range(args.warmup + args.steps):
-        r = cpu_reference_sample(wl, seconds_target=4.0, max_tokens=8)
+        r = cpu_reference_sample(wl, full_run=(i == args.warmup + args.steps - 1))
         if i >= args.warmup:
             steps.append(r)
-    toks = sum(r["value"] * r["seconds"] for r in steps)
+    toks = sum(len(r["ids"]) for r in steps)
     secs = sum(r["seconds"] for r in steps)
     v = toks / secs
+    last = steps[-1]
     line = {"impl": "reference", "metric": "decode tokens/s", "value": v, "unit": "tokens/s", "n_gpus": 0,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * secs / len(steps),
             "higher_is_better": True, "scaling": wl["scaling"], "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random weights and prompt ids)",
-            "config": {"workload": wl["name"], "sample": steps[0]["sample"]},
-            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": steps[0]["cores"], "kind": "port",
-                             "sample": steps[0]["sample"]},
+            "config": {"workload": wl["name"], "sample": last["sample"]},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": last["cores"], "cpu_model": last["cpu_model"],
+                             "kind": "port", "sample": last["sample"], "full_run": last.get("full_run")},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
+def lib_sha256(path: str) -> str:
+    import hashlib
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for chunk in iter(lambda: f.read(1 << 20), b""):
+            h.update(chunk)
+    return h.hexdigest()
+
+
+def recorded_traffic(workload: str, lib_path: str):
+    """DRAM bytes per decode step from the traffic record, if it was measured
+    on this exact library file; else None."""
+    try:
+        with open(TRAFFIC_RECORD) as f:
+            rec = json.load(f)
+    except (OSError, ValueError):
+        return None
+    r = rec.get(workload)
+    if not r or r.get("lib_sha256") != lib_sha256(lib_path):
+        return None
+    return float(r["dram_bytes_per_step"])
+
+
+def record_traffic(csv_path: str, workload: str, kernel: str, steps_per_launch: int) -> None:
+    """Writes the traffic record from an ncu --csv capture of one or more
+    launches of `kernel` with dram__bytes_read.sum and dram__bytes_write.sum
+    (bytes, or the unit ncu prints), keyed by the library's SHA-256."""
+    import csv
+    import __graft_entry__ as graft
+    unit = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "KB": 1e3, "MB": 1e6, "GB": 1e9}
+    per_launch: dict[str, float] = {}
+    with open(csv_path) as f:
+        lines = [ln for ln in f if ln.startswith('"')]
+    for row in csv.DictReader(lines):
+        if kernel not in row.get("Kernel Name", "") or not row.get("Metric Name", "").startswith("dram__bytes_"):
+            continue
+        v = float(row["Metric Value"].replace(",", "")) * unit.get(row.get("Metric Unit", "byte"), 1)
+        per_launch[row["ID"]] = per_launch.get(row["ID"], 0.0) + v
+    if not per_launch:
+        raise SystemExit(f"no dram__bytes rows for {kernel} in {csv_path}")
+    rec = {}
+    if os.path.exists(TRAFFIC_RECORD):
+        with open(TRAFFIC_RECORD) as f:
+            rec = json.load(f)
+    lib = graft.load_package().library_path()
+    rec[workload] = {"kernel": kernel, "launches": len(per_launch), "steps_per_launch": steps_per_launch,
+                     "dram_bytes_per_step": sum(per_launch.values()) / len(per_launch) / steps_per_launch,
+                     "lib_sha256": lib_sha256(lib)}
+    with open(TRAFFIC_RECORD, "w") as f:
+        json.dump(rec, f, indent=1)
+    print(json.dumps(rec[workload]))
+
+
 def main():
     args = parse()
+    if args.record_traffic:
+        record_traffic(args.record_traffic, args.workload, args.record_kernel, args.record_steps_per_launch)
+        return
     wl = dict(WORKLOADS[args.workload])
-    default_c2 = args.workload == "c2" and not args.new_tokens
+    default_wl = not args.new_tokens
     if args.new_tokens:
         wl["new_tokens"] = args.new_tokens
         wl["name"] += f" [new tokens overridden: {args.new_tokens}]"
@@ -383,8 +494,9 @@ def main():
                               "sampler)" if persistent else "decode step (CUDA graph replay of the step kernels)",
                     "achieved": achieved_gbs, "peak": peak, "unit": "GB/s", "frac": achieved_gbs / peak,
                     "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
-                    "traffic": MK_DRAM_BYTES_PER_STEP_C2 if persistent and default_c2 else None,
-                    "traffic_unit": "bytes per decode step (ncu dram read+write of this workload's launch / steps)",
+                    "traffic": recorded_traffic(args.workload, pkg.library_path()) if default_wl else None,
+                    "traffic_unit": "bytes per decode step: ncu dram__bytes_read.sum + dram__bytes_write.sum of the "
+                                    "workload's launch / its steps, recorded for this library file (else null)",
                     "step_ms": step_ms, "algorithmic_bytes_per_step": bytes_step}
 
     # ---- e2e: the public host-buffer call, copies inside the timed region ----
@@ -410,10 +522,12 @@ def main():
            "h2d_bytes_per_step": int(sum(lens) * 4 + count * 4), "d2h_bytes_per_step": int(count * new * 4 + count * 4)}
 
     cpu = None
+    parity = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             cpu = cpu_reference_sample(wl)
             cpu.pop("seconds", None)
+            parity = parity_vs_cpu(res[0], cpu.pop("ids"))
         except Exception as ex:  # the baseline is informational; never fail the bench on it
             cpu = {"error": str(ex)}
 
@@ -431,6 +545,7 @@ def main():
                              f"of weights"},
             "roofline": roofline,
             "cpu_baseline": cpu,
+            "parity": parity,
             "e2e": e2e,
             "gpu_launches": int(st.get("kernel_launches", 0)),
             "clocks": clk.summary(),

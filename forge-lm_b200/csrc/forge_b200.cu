@@ -593,15 +593,25 @@ static void launch_layernorm(DeviceSession& s, int rows, const float* x, const f
     fail(FB2_UNSUPPORTED, "d_model too large for the LayerNorm kernel");
 }
 
-template <int MR>
-static void launch_gemv_mr(DeviceSession& s, int M, int K, int N, const float* A, const float* W, const Epi& e) {
+// Split-K geometry of k_gemv for a [K][N] weight: S k-splits of kchunk rows.
+struct GemvSplit {
+    int S, kchunk;
+};
+static GemvSplit gemv_split(int sm_count, int K, int N) {
     int nblk = ceil_div(N, 64);
-    int target = 2 * s.dm->sm_count;
+    int target = 2 * sm_count;
     int S = std::max(1, ceil_div(target, nblk));
     S = std::min(S, std::max(1, K / 16));
     int kchunk = ceil_div(ceil_div(K, S), 16) * 16;
     if (kchunk > kGemvMaxKChunk) kchunk = kGemvMaxKChunk;
-    S = ceil_div(K, kchunk);
+    return GemvSplit{ceil_div(K, kchunk), kchunk};
+}
+
+template <int MR>
+static void launch_gemv_mr(DeviceSession& s, int M, int K, int N, const float* A, const float* W, const Epi& e) {
+    int nblk = ceil_div(N, 64);
+    const GemvSplit sp = gemv_split(s.dm->sm_count, K, N);
+    const int S = sp.S, kchunk = sp.kchunk;
     size_t need = (size_t)S * M * N;
     if (S > 1 && need > s.gemv_part_cap) fail(FB2_UNSUPPORTED, "split-K scratch too small");
     size_t smem = (size_t)MR * kchunk * 4 + (size_t)16 * MR * 64 * 4;
@@ -2209,6 +2219,17 @@ int32_t fb2_forward_last_logits_noalloc(fb2_model* m, int32_t device_slot, int32
                                       std::to_string(lay.total * 4) + " bytes of scratch; the library reserves " +
                                       std::to_string(kNoallocScratchFloats * 4));
         const DeviceModel& dm = m->devs[device_slot];
+        // the split-K partial sums of every projection of this window must fit
+        // their region, checked before anything is enqueued
+        const size_t part_cap = (size_t)512 * 1024;
+        const int KN[4][2] = {{m->D, 3 * m->D}, {m->D, m->D}, {m->D, m->F}, {m->F, m->D}};
+        for (const auto& kn : KN) {
+            const GemvSplit sp = gemv_split(dm.sm_count, kn[0], kn[1]);
+            if (sp.S > 1 && (size_t)sp.S * n_tokens * kn[1] > part_cap)
+                fail(FB2_UNSUPPORTED, "fb2_forward_last_logits_noalloc: the split-K partial sums of a " +
+                                          std::to_string(kn[0]) + "x" + std::to_string(kn[1]) + " projection over " +
+                                          std::to_string(n_tokens) + " tokens exceed the scratch region");
+        }
         DeviceGuard g(dm.device);
         float* base = nullptr;
         {
@@ -2240,7 +2261,7 @@ int32_t fb2_forward_last_logits_noalloc(fb2_model* m, int32_t device_slot, int32
         s.v_offset = (long long)view.H * view.ctx * view.hd;
         s.kv_slot_stride = s.kv_layer_stride * view.L;
         s.d_gemv_part = base + lay.part;
-        s.gemv_part_cap = (size_t)512 * 1024;
+        s.gemv_part_cap = part_cap;
         s.d_tickets = reinterpret_cast<unsigned int*>(base + lay.tickets);
         int* ints = reinterpret_cast<int*>(base + lay.ints);
         s.d_row_hidx = ints + 2 * kNoallocMaxRows;

@@ -198,9 +198,9 @@ int32_t fb2_sample_logits(fb2_session* s, int32_t n, const float* logits, const 
 
 /* ---- forward_last without device allocation -----------------------------------
  * No counterpart in the reference: an addition for callers that cannot call
- * cudaMalloc — code that runs while a CUDA stream is being captured, a host
- * runtime that already owns the device's memory budget through its own
- * allocator, or a latency-critical path where cudaMalloc's implicit device
+ * cudaMalloc — a host runtime that already owns the device's memory budget
+ * through its own allocator (a cudaMalloc beside it fails or breaks its
+ * accounting), or a latency-critical path where cudaMalloc's implicit device
  * synchronisation is not acceptable.
  *
  * Computes what fb2_forward_last_logits computes for ONE window of n_tokens
@@ -211,8 +211,9 @@ int32_t fb2_sample_logits(fb2_session* s, int32_t n, const float* logits, const 
  * every GPU that loads it, until the process exits); the call allocates
  * nothing, enqueues its kernels on cuda_stream (a cudaStream_t as void*) and
  * returns without waiting.  Models whose intermediates exceed the 8 MiB
- * (roughly d_model > 1024 or many layers) are rejected with FB2_UNSUPPORTED;
- * longer windows with FB2_INVALID_ARG.  Token ids are not range-checked on
+ * (roughly d_model > 1024 or many layers), or whose split-K partial sums
+ * for this window exceed its region, are rejected with FB2_UNSUPPORTED
+ * before anything is enqueued; longer windows with FB2_INVALID_ARG.  Token ids are not range-checked on
  * the host (they stay on the device); ids outside [0, vocab) read as id 0.
  * The first call on a device looks up the array's device address; make that
  * first call before any stream capture begins.  Every call shares the one

@@ -32,3 +32,38 @@ def test_sequence_bytes_and_window_flops():
         pairs = T * (T + 1) // 2
         attn = L * 2 * (2 * pairs * D)  # scores and context, 2 FLOPs per multiply-add
         assert bench.flops_per_sequence_step(m, T) == T * L * per_row + attn + 2 * D * V
+
+
+def test_reference_step_flops_and_cpu_sample_on_a_tiny_workload(O):
+    """The reference step's cost model counts every row through the blocks,
+    the full T x T scores and context, and every row's logits; the CPU leg
+    returns its ids (for the bench's parity field) and a full-run estimate."""
+    m = dict(vocab_size=300, context_length=32, d_model=32, n_layers=2, n_heads=2)
+    D, L, V = 32, 2, 300
+    assert bench.ref_flops_per_token(m, 10) == 2.0 * 10 * (L * 12 * D * D + V * D) + 4.0 * L * 100 * D
+    wl = dict(name="tiny", model=m, prompt_len=8, new_tokens=40, temperature=0.7, top_k=5, penalty=1.1, ngram=2)
+    r = bench.cpu_reference_sample(wl, n_tokens=6)
+    assert len(r["ids"]) == 6 and r["value"] > 0 and r["cpu_model"]
+    assert r["full_run"]["value"] > 0
+    want = O.generate(O.Config(300, 32, 32, 2, 2), O.init_params(O.Config(300, 32, 32, 2, 2), bench.WEIGHT_SEED),
+                      bench.prompts_for(0, 1, 8, 300)[0], 6, 0.7, 5, O.DotNetRandom(1), repetition_penalty=1.1,
+                      no_repeat_ngram=2)
+    assert list(r["ids"]) == list(want)
+    p = bench.parity_vs_cpu(list(want) + [7, 7], r["ids"])
+    assert p["ids_equal"] == 6 and p["first_mismatch"] is None
+    p = bench.parity_vs_cpu([int(want[0]) + 1] + list(want[1:]), r["ids"])
+    assert p["first_mismatch"] == 0 and p["ids_equal"] == 5
+
+
+def test_traffic_record_is_keyed_by_the_library_file(tmp_path, monkeypatch):
+    """A DRAM-traffic figure is reported only for the library file it was
+    measured on."""
+    lib = tmp_path / "lib.so"
+    lib.write_bytes(b"build A")
+    rec = tmp_path / "traffic.json"
+    monkeypatch.setattr(bench, "TRAFFIC_RECORD", str(rec))
+    rec.write_text('{"c2": {"dram_bytes_per_step": 123.0, "lib_sha256": "%s"}}' % bench.lib_sha256(str(lib)))
+    assert bench.recorded_traffic("c2", str(lib)) == 123.0
+    assert bench.recorded_traffic("c3", str(lib)) is None
+    lib.write_bytes(b"build B")
+    assert bench.recorded_traffic("c2", str(lib)) is None

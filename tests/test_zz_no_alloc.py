@@ -1,6 +1,6 @@
 """fb2_forward_last_logits_noalloc: the entry point for callers that cannot
-call cudaMalloc (inside a stream capture, under a host runtime that owns the
-device memory budget, or on a path that must not synchronise the device).
+call cudaMalloc (under a host runtime that owns the device memory budget,
+or on a path that must not synchronise the device).
 
 It must give what the allocating entry point fb2_forward_last_logits gives
 (same tolerance as every logits test: max |a-e| / max(1, |e|) <= 1e-3), on
@@ -28,13 +28,15 @@ def _relerr(a, e):
     return float(np.max(np.abs(a - e) / np.maximum(1.0, np.abs(e))))
 
 
-def test_noalloc_matches_allocating_entry_point(pkg):
+@pytest.mark.parametrize("weight_dtype", ["fp32", "bf16"])
+def test_noalloc_matches_allocating_entry_point(pkg, weight_dtype):
+    """fp32 weights, and bf16 weights (the gemv path that reads 2-byte copies)."""
     import torch
     from forge_lm_b200 import _native as N
 
     cfg = pkg.ModelConfig(*SHAPE)
     params = pkg.init_params(cfg, 1234)
-    be = pkg.B200Backend(cfg, params, devices=[0])
+    be = pkg.B200Backend(cfg, params, devices=[0], weight_dtype=weight_dtype)
     L = N.load()
     try:
         rng = np.random.default_rng(5)
