@@ -297,8 +297,9 @@ class B200Backend:
 
         Uniform source, in order of precedence: `uniforms` [n, max_new];
         `seeds` (a fresh `new Random(seed)` per sequence); `rng` (one
-        DotNetRandom per sequence, advanced by exactly the draws the
-        reference would make)."""
+        DotNetRandom per sequence, or one shared by all: the library pulls
+        each value from it through FB2_RNG_CALLBACK when it samples, so the
+        generator advances by exactly the draws the reference makes)."""
         n = len(prompts)
         if n == 0:
             return []
@@ -316,15 +317,10 @@ class B200Backend:
         elif seeds is not None:
             mode, seed_arr = N.FB2_RNG_SEEDS, _i32(seeds)
         elif rng is not None:
-            rngs = [rng] if isinstance(rng, DotNetRandom) else list(rng)
+            rngs = [rng] * n if isinstance(rng, DotNetRandom) else list(rng)
             if len(rngs) != n:
                 raise ArgumentError(N.FB2_INVALID_ARG, "one rng per sequence")
-            if temperature > 0:
-                uni = np.empty((n, max(max_new_tokens, 1)), np.float64)
-                for i, r in enumerate(rngs):
-                    c = r.clone()
-                    for k in range(max_new_tokens):
-                        uni[i, k] = c.next_double()
+            mode = N.FB2_RNG_CALLBACK
         elif temperature > 0:
             raise ArgumentError(N.FB2_INVALID_ARG, "rng is required when temperature > 0")
         out = np.zeros((n, max(max_new_tokens, 1)), np.int32)
@@ -335,13 +331,17 @@ class B200Backend:
                 r = on_token(seq, step, token)
                 return 1 if r else 0
             cb = N.TOKEN_CB(_cb)
-        N.check(N.load().fb2_generate(self._session, n, _ptr(toks), _ptr(lens), C.byref(sp), mode,
-                                      _ptr(seed_arr) if seed_arr is not None else None,
-                                      _ptr(uni) if uni is not None else None, _ptr(out), _ptr(counts), cb, None))
-        if rngs is not None and temperature > 0:
-            for r, c in zip(rngs, counts):
-                for _ in range(int(c)):
-                    r.next_double()
+        L = N.load()
+        ucb = N.UNIFORM_CB(0)
+        if rngs is not None:
+            ucb = N.UNIFORM_CB(lambda user, seq: rngs[seq].next_double())
+        N.check(L.fb2_session_set_uniform_source(self._session, ucb, None))
+        try:
+            N.check(L.fb2_generate(self._session, n, _ptr(toks), _ptr(lens), C.byref(sp), mode,
+                                   _ptr(seed_arr) if seed_arr is not None else None,
+                                   _ptr(uni) if uni is not None else None, _ptr(out), _ptr(counts), cb, None))
+        finally:
+            L.fb2_session_set_uniform_source(self._session, N.UNIFORM_CB(0), None)
         return [out[i, :counts[i]].copy() for i in range(n)]
 
     def generate(self, prompt_tokens: Sequence[int], max_new_tokens: int, temperature: float, top_k: int,

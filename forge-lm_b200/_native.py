@@ -26,11 +26,13 @@ FB2_WEIGHTS_BF16 = 1
 FB2_RNG_SEEDS = 0
 FB2_RNG_SESSION = 1
 FB2_RNG_UNIFORMS = 2
+FB2_RNG_CALLBACK = 3
 
 # Every symbol include/forge_b200.h declares.
 EXPORTED = [
     "fb2_version", "fb2_last_error", "fb2_device_count", "fb2_model_create", "fb2_model_destroy",
-    "fb2_session_create", "fb2_session_destroy", "fb2_session_seed", "fb2_session_set_stream",
+    "fb2_session_create", "fb2_session_destroy", "fb2_session_seed", "fb2_session_set_uniform_source",
+    "fb2_session_set_stream",
     "fb2_generate", "fb2_generate_device", "fb2_forward_last_logits", "fb2_teacher_forced_logits",
     "fb2_sample_logits", "fb2_forward_last_logits_noalloc", "fb2_init_params", "fb2_stats", "fb2_stats_reset",
     "fb2_forgemodel_read_header", "fb2_model_load_forgemodel", "fb2_forgemodel_write",
@@ -59,6 +61,7 @@ class Stats(C.Structure):
 
 
 TOKEN_CB = C.CFUNCTYPE(C.c_int32, C.c_void_p, C.c_int32, C.c_int32, C.c_int32)
+UNIFORM_CB = C.CFUNCTYPE(C.c_double, C.c_void_p, C.c_int32)
 
 _lib = None
 
@@ -99,6 +102,7 @@ def load(path: str | None = None):
     L.fb2_session_destroy.restype = None
     L.fb2_session_seed.argtypes = [vp, i32, i32]
     L.fb2_session_set_stream.argtypes = [vp, i32, vp]
+    L.fb2_session_set_uniform_source.argtypes = [vp, UNIFORM_CB, vp]
     L.fb2_generate.argtypes = [vp, i32, i32p, i32p, C.POINTER(Sampling), i32, i32p, f64p, i32p, i32p, TOKEN_CB, vp]
     L.fb2_generate_device.argtypes = [vp, i32, vp, vp, i32p, C.POINTER(Sampling), i32, i32p, vp, vp, vp]
     L.fb2_forward_last_logits.argtypes = [vp, i32, i32p, i32p, f32p]

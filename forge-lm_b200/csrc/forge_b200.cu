@@ -507,6 +507,8 @@ struct fb2_session {
     fb2_model* model = nullptr;
     int max_seqs = 0;
     std::vector<DeviceSession*> ds;
+    fb2_uniform_cb ucb = nullptr;  // FB2_RNG_CALLBACK source
+    void* ucb_user = nullptr;
 };
 
 // Zeroes the persistent kernel's tagged words, counters and error flag and
@@ -1273,7 +1275,9 @@ struct ShardJob {
     int* out_counts;              // host [n] or device
     fb2_token_cb cb;
     void* user;
-    std::mutex* cb_mutex;
+    fb2_uniform_cb ucb;           // FB2_RNG_CALLBACK
+    void* ucb_user;
+    std::mutex* cb_mutex;         // serialises both callbacks across device threads
     std::atomic<int>* stop;
 };
 
@@ -1359,13 +1363,27 @@ static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
             acc += wl0[i];
         }
     }
-    // uniforms
+    // uniforms.  FB2_RNG_CALLBACK pulls them from the caller: all up front
+    // when every sequence will emit max_new tokens (no EOS, no token
+    // callback), else one step at a time, only for sequences still running
+    // (`pull_per_step`; every step then synchronises with the host).
+    const bool pull = sampled && job.rng_mode == FB2_RNG_CALLBACK;
+    const bool pull_per_step = pull && (job.cb || sp.eos_id >= 0);
+    auto draw = [&](int i) {
+        std::lock_guard<std::mutex> lk(*job.cb_mutex);
+        return job.ucb(job.ucb_user, job.first + i);
+    };
     std::vector<double> uni;
     const double* d_uni = nullptr;
     if (sampled && max_new > 0) {
         if (job.rng_mode == FB2_RNG_UNIFORMS) {
             if (job.device_io) d_uni = job.uniforms;
             else uni.assign(job.uniforms, job.uniforms + (size_t)n * max_new);
+        } else if (pull) {
+            uni.assign((size_t)n * max_new, 0.0);
+            if (!pull_per_step)
+                for (int k = 0; k < max_new; k++)
+                    for (int i = 0; i < n; i++) uni[(size_t)i * max_new + k] = draw(i);
         } else {
             uni.resize((size_t)n * max_new);
             for (int i = 0; i < n; i++) {
@@ -1395,6 +1413,19 @@ static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
                                                               s.d_count, s.d_done, d_uni, max_new, P, d_out, max_new);
     };
     std::vector<int> h_tok, h_cnt, prev_cnt(n, 0);
+    std::vector<char> running(n, 1);  // per-step mode: sequences that will sample the next step
+    // per-step uniform pull: the draws for `step` of the running sequences,
+    // copied into their table entries ahead of the step's sampling
+    auto pull_step = [&](int step) {
+        if (!pull_per_step) return;
+        for (int i = 0; i < n; i++) {
+            if (!running[i]) continue;
+            double& u = uni[(size_t)i * max_new + step];
+            u = draw(i);
+            CK(cudaMemcpyAsync(s.d_uni + (size_t)i * max_new + step, &u, sizeof(double), cudaMemcpyHostToDevice,
+                               s.stream));
+        }
+    };
     auto stream_callbacks = [&](int step) -> bool {
         // returns true when generation should stop
         CK(cudaStreamSynchronize(s.stream));
@@ -1404,7 +1435,7 @@ static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
         CK(cudaMemcpy(h_tok.data(), d_out, (size_t)n * max_new * sizeof(int), cudaMemcpyDeviceToHost));
         bool any_active = false;
         for (int i = 0; i < n; i++) {
-            for (int k = prev_cnt[i]; k < h_cnt[i]; k++) {
+            for (int k = prev_cnt[i]; k < h_cnt[i] && job.cb; k++) {
                 int rc;
                 {
                     std::lock_guard<std::mutex> lk(*job.cb_mutex);
@@ -1414,16 +1445,19 @@ static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
             }
             prev_cnt[i] = h_cnt[i];
             bool eos_hit = sp.eos_id >= 0 && h_cnt[i] > 0 && h_tok[(size_t)i * max_new + h_cnt[i] - 1] == sp.eos_id;
-            if (!eos_hit && h_cnt[i] < max_new) any_active = true;
+            running[i] = !eos_hit && h_cnt[i] < max_new;
+            if (running[i]) any_active = true;
         }
         return job.stop->load() != 0 || !any_active;
     };
 
+    const bool per_step = job.cb || pull_per_step;  // the host sees every step's tokens
     if (max_new > 0) {
+        pull_step(0);
         for (const ChunkPlan& c : init_plans) run_prefill_chunk(s, c, s.d_tab);
         sample_all();
         CK(cudaGetLastError());
-        bool stop = job.cb ? stream_callbacks(0) : false;
+        bool stop = per_step ? stream_callbacks(0) : false;
         int step = 1;
         // Persistent kernel for every step before the first slide: one launch
         // (a step per launch when a callback streams tokens; 64-step launches
@@ -1432,11 +1466,12 @@ static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
             const int mk_end = std::min(max_new, slide_at[order[0]]);
             while (step < mk_end && !stop) {
                 int ns = mk_end - step;
-                if (job.cb) ns = 1;
+                if (per_step) ns = 1;
                 else if (sp.eos_id >= 0) ns = std::min(ns, 64);
+                pull_step(step);
                 run_mega(s, n, ns, P, d_uni, d_out, max_new, true);
                 step += ns;
-                if (job.cb) stop = stream_callbacks(step - 1);
+                if (per_step) stop = stream_callbacks(step - 1);
                 else if (sp.eos_id >= 0 && step < mk_end) {
                     std::vector<int> hd(n);
                     CK(cudaMemcpyAsync(hd.data(), s.d_done, n * sizeof(int), cudaMemcpyDeviceToHost, s.stream));
@@ -1451,6 +1486,7 @@ static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
             // slots with slide_at <= step re-prefill; the rest decode
             int k = 0;
             while (k < n && slide_at[order[k]] <= step) k++;
+            pull_step(step);
             if (k < n) run_decode_step(s, n);
             if (k > 0) {
                 size_t pi = 0;
@@ -1459,7 +1495,7 @@ static void run_generate_shard(DeviceSession& s, const ShardJob& job) {
                 s.stats.reprefills += k;
             }
             sample_all();
-            if (job.cb) stop = stream_callbacks(step);
+            if (per_step) stop = stream_callbacks(step);
             else if (sp.eos_id >= 0 && (step % 64) == 0) {
                 // all slots finished? (cheap poll, keeps the pipeline mostly full)
                 std::vector<int> hd(n);
@@ -1831,6 +1867,14 @@ int32_t fb2_session_seed(fb2_session* S, int32_t seq, int32_t seed) {
     });
 }
 
+int32_t fb2_session_set_uniform_source(fb2_session* S, fb2_uniform_cb cb, void* user) {
+    return guarded([&] {
+        if (!S) fail(FB2_INVALID_ARG, "session is NULL");
+        S->ucb = cb;
+        S->ucb_user = cb ? user : nullptr;
+    });
+}
+
 int32_t fb2_session_set_stream(fb2_session* S, int32_t device_slot, void* stream) {
     return guarded([&] {
         if (!S) fail(FB2_INVALID_ARG, "session is NULL");
@@ -1848,10 +1892,12 @@ static void check_generate_args(fb2_session* S, int32_t n_seqs, const int32_t* p
     if (prompt_lens)
         for (int i = 0; i < n_seqs; i++)
             if (prompt_lens[i] <= 0) fail(FB2_INVALID_ARG, "Need at least one prompt token.");
-    if (rng_mode < FB2_RNG_SEEDS || rng_mode > FB2_RNG_UNIFORMS) fail(FB2_INVALID_ARG, "bad rng_mode");
+    if (rng_mode < FB2_RNG_SEEDS || rng_mode > FB2_RNG_CALLBACK) fail(FB2_INVALID_ARG, "bad rng_mode");
     if (sp->temperature > 0.0f && sp->max_new_tokens > 0) {
         if (rng_mode == FB2_RNG_SEEDS && !seeds) fail(FB2_INVALID_ARG, "seeds is NULL");
         if (rng_mode == FB2_RNG_UNIFORMS && !uniforms) fail(FB2_INVALID_ARG, "uniforms is NULL");
+        if (rng_mode == FB2_RNG_CALLBACK && !S->ucb)
+            fail(FB2_INVALID_ARG, "rng must not be null (FB2_RNG_CALLBACK without a uniform source)");
     }
 }
 
@@ -1910,6 +1956,8 @@ int32_t fb2_generate(fb2_session* S, int32_t n_seqs, const int32_t* prompt_token
             j.out_counts = out_counts + std::min(s->slot0, n_seqs);
             j.cb = cb;
             j.user = user;
+            j.ucb = S->ucb;
+            j.ucb_user = S->ucb_user;
             j.cb_mutex = &cbm;
             j.stop = &stop;
             jobs.push_back(j);
@@ -1936,6 +1984,7 @@ int32_t fb2_generate_device(fb2_session* S, int32_t n_seqs, const int32_t* devic
         if (!device_prompt_tokens || !device_prompt_lens || !host_prompt_lens || !device_out_counts)
             fail(FB2_INVALID_ARG, "NULL argument");
         check_generate_args(S, n_seqs, host_prompt_lens, sp, rng_mode, seeds, device_uniforms);
+        if (rng_mode == FB2_RNG_CALLBACK) fail(FB2_INVALID_ARG, "FB2_RNG_CALLBACK needs fb2_generate");
         if (S->ds.size() != 1) fail(FB2_UNSUPPORTED, "fb2_generate_device needs a single-device session");
         if (sp->max_new_tokens > 0 && !device_out_tokens) fail(FB2_INVALID_ARG, "out_tokens is NULL");
         std::mutex cbm;

@@ -88,8 +88,28 @@ typedef enum {
      * fb2_session_seed and carried across calls (chat, Program.cs:730). */
     FB2_RNG_SESSION = 1,
     /* uniforms[i * max_new + n]: the caller's NextDouble() values. */
-    FB2_RNG_UNIFORMS = 2
+    FB2_RNG_UNIFORMS = 2,
+    /* The uniform source set with fb2_session_set_uniform_source: the
+     * library pulls one value per sampled token, so a caller that forwards
+     * its own Random.NextDouble() (the `rng` Sampler.Generate receives,
+     * Sampler.cs:78-80, 61) advances it by exactly the draws the reference
+     * makes.  fb2_generate only. */
+    FB2_RNG_CALLBACK = 3
 } fb2_rng_mode;
+
+/* Uniform source of FB2_RNG_CALLBACK: returns the next NextDouble() value of
+ * sequence `seq`'s stream (in [0, 1)).  The library calls it once per
+ * sampled token (temperature > 0), in step order, on the thread that called
+ * fb2_generate or on one of the library's device threads, never two calls at
+ * once.  A sequence draws for step n only after its tokens of steps < n are
+ * known and it is still running: with eos_id >= 0 or a token callback the
+ * draw for step n comes after the token callback of step n-1 returned, so a
+ * sequence that sampled EOS, or a callback that asked to stop, draws no
+ * more (as Sampler.Generate, a lazy iterator, draws no more).  Without EOS
+ * and without a token callback every sequence emits max_new_tokens tokens,
+ * and the library draws all of them (step by step, sequences in order)
+ * before the first decode step. */
+typedef double (*fb2_uniform_cb)(void* user, int32_t seq);
 
 /* Per-token streaming callback (Program.cs:671-677 prints each id as it is
  * yielded).  Called on the thread that called fb2_generate, in step order,
@@ -142,6 +162,10 @@ int32_t fb2_session_create(fb2_model* m, int32_t max_seqs, fb2_session** out);
 void fb2_session_destroy(fb2_session* s);
 /* Seeds the FB2_RNG_SESSION stream of slot `seq` as `new Random(seed)`. */
 int32_t fb2_session_seed(fb2_session* s, int32_t seq, int32_t seed);
+/* Sets the uniform source used by fb2_generate with FB2_RNG_CALLBACK (cb may
+ * be NULL to clear it).  No reference counterpart as a function: it carries
+ * Sampler.Generate's `Random rng` argument (Sampler.cs:78-80) across the ABI. */
+int32_t fb2_session_set_uniform_source(fb2_session* s, fb2_uniform_cb cb, void* user);
 /* Runs the session's work for device slot `device_slot` on the caller's
  * CUDA stream (a cudaStream_t passed as void*; NULL restores the library's
  * own stream). */
