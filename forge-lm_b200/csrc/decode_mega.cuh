@@ -40,7 +40,10 @@ constexpr int MK_MAX_ROWS = 8;
 constexpr int MK_SLICE_MAX = 256;
 constexpr int MK_SURV_MAX = 512;
 constexpr int MK_MAX_TOPK = 64;
-constexpr unsigned long long MK_TIMEOUT_NS = 2000000000ull;
+constexpr unsigned long long MK_TIMEOUT_NS = 2000000000ull;  // default limit of every bounded wait
+// The launch's wait limit (MkArgs::timeout_ns), set by thread 0 before the
+// first barrier; every bounded wait of the kernel reads it.
+__shared__ unsigned long long mk_wait_ns;
 
 enum MkPhase { MK_QKV = 0, MK_PROJ = 1, MK_FC = 2, MK_PROJ2 = 3 };
 
@@ -81,6 +84,8 @@ struct MkArgs {
     int nsteps;
     unsigned long long* trace;  // optional: [nW][trace_steps][MK_TRACE_POINTS] %globaltimer stamps
     int trace_steps;
+    unsigned long long timeout_ns;  // limit of every bounded wait (MK_TIMEOUT_NS unless a test shortens it)
+    int withhold_cta;               // test hook: this CTA never publishes its q words of step 0, layer 0 (-1: none)
 };
 
 // Trace points per step: 12 per layer for layers 0 and 1 (level A start, after
@@ -191,7 +196,7 @@ FB2_DEV float wait_pair(const unsigned long long* p, uint32_t tag, int* err, vol
         w = ld_pair(p);
         if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
         if (*abort_flag) return 0.f;
-        if (gtimer() - t0 > MK_TIMEOUT_NS) {
+        if (gtimer() - t0 > mk_wait_ns) {
             atomicExch(err, 1);
             *abort_flag = 1;
             return 0.f;
@@ -221,7 +226,7 @@ FB2_DEV void resolve_batch(unsigned long long* w, uint32_t pend, Addr addr, uint
         if (!still || *abort_flag) return;
         const unsigned long long now = gtimer();
         if (!t0) t0 = now;
-        else if (now - t0 > MK_TIMEOUT_NS) {
+        else if (now - t0 > mk_wait_ns) {
             atomicExch(err, 1);
             *abort_flag = 1;
             return;
@@ -275,7 +280,7 @@ FB2_DEV float wait_pair_acquire(const unsigned long long* p, uint32_t tag, int* 
         const unsigned long long w = ld_pair_acquire(p);
         if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
         if (*abort_flag) return 0.f;
-        if (gtimer() - t0 > MK_TIMEOUT_NS) {
+        if (gtimer() - t0 > mk_wait_ns) {
             atomicExch(err, 1);
             *abort_flag = 1;
             return 0.f;
@@ -390,7 +395,7 @@ FB2_DEV void wait_full(uint64_t* full, uint32_t it, int nstage, int* err, volati
     const unsigned long long t0 = gtimer();
     while (!mbar_try(b, par)) {
         if (*abort_flag) return;
-        if (gtimer() - t0 > MK_TIMEOUT_NS) {
+        if (gtimer() - t0 > mk_wait_ns) {
             atomicExch(err, 2);
             *abort_flag = 1;
             return;
@@ -632,6 +637,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     }
     if (tid == 0) {
         s_abort = 0;
+        mk_wait_ns = a.timeout_ns;
         for (int i = 0; i < a.nstage; i++) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 8);
@@ -666,7 +672,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 if (!mbar_try(&empty[st], par)) {
                     const unsigned long long t0 = gtimer();
                     while (!mbar_try(&empty[st], par)) {
-                        if (s_abort || gtimer() - t0 > MK_TIMEOUT_NS) {
+                        if (s_abort || gtimer() - t0 > mk_wait_ns) {
                             if (!s_abort) atomicExch(a.err, 3);
                             s_abort = 1;
                             ok = false;
@@ -701,7 +707,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     const unsigned long long t0 = gtimer();
                     while (ld_acquire_u32(a.stepdone) < target) {
                         __nanosleep(200);
-                        if (s_abort || gtimer() - t0 > MK_TIMEOUT_NS) {
+                        if (s_abort || gtimer() - t0 > mk_wait_ns) {
                             if (!s_abort) atomicExch(a.err, 4);
                             s_abort = 1;
                             ok = false;
@@ -738,7 +744,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         for (uint32_t j = (it > (uint32_t)a.nstage ? it - a.nstage : 0); j < it; j++) {
             const unsigned long long t0 = gtimer();
             while (!mbar_try(&full[j % a.nstage], (j / a.nstage) & 1u))
-                if (gtimer() - t0 > MK_TIMEOUT_NS) break;
+                if (gtimer() - t0 > mk_wait_ns) break;
         }
         return;
     }
@@ -810,10 +816,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
             mk_layernorm<MR>(xres, act, D, ln1, scr + 384);
             MK_TRACE_L(1);
             {
+                const bool withhold = cta == a.withhold_cta && s == 0 && l == 0;
                 auto epi = [&](int m, int n, float v) {
                     v += pb[MK_QKV];
                     if (n < D) {
-                        st_pair(a.xq + m * D + n, v, tg);
+                        if (!withhold) st_pair(a.xq + m * D + n, v, tg);
                         return;
                     }
                     const int which = n < 2 * D ? 0 : 1;

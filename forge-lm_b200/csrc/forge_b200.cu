@@ -112,10 +112,22 @@ struct DeviceGuard {
     }
 };
 
+// Test hook (fb2_test_fail_alloc): the g_fail_alloc_at-th device allocation
+// from now fails as if the device were out of memory; counted over the
+// process, 0 = off.
+std::atomic<long long> g_alloc_count{0};
+std::atomic<long long> g_fail_alloc_at{0};
+
 template <class T>
 T* dalloc(size_t n) {
     void* p = nullptr;
     if (n == 0) n = 1;
+    const long long k = ++g_alloc_count;
+    const long long at = g_fail_alloc_at.load();
+    if (at > 0 && k == at) {
+        g_fail_alloc_at = 0;
+        fail(FB2_OUT_OF_MEMORY, "cudaMalloc: out of memory (injected by fb2_test_fail_alloc)");
+    }
     CK(cudaMalloc(&p, n * sizeof(T)));
     return static_cast<T*>(p);
 }
@@ -501,6 +513,10 @@ struct DeviceSession {
     // stats
     fb2_stats_t stats{};
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    // test hook (fb2_test_mk_withhold): the next persistent launch withholds
+    // one CTA's q words and waits at most test_wait_ns
+    int test_withhold_cta = -1;
+    unsigned long long test_wait_ns = 0;
 };
 
 struct fb2_session {
@@ -976,6 +992,13 @@ static void run_mega(DeviceSession& s, int n, int nsteps, const SampleParams& P,
     a.stepdone = s.mk_stepdone; a.err = s.mk_err;
     a.gstep0 = s.mk_gstep; a.nsteps = nsteps;
     a.trace = s.mk_trace; a.trace_steps = s.mk_trace_steps;
+    a.timeout_ns = MK_TIMEOUT_NS;
+    a.withhold_cta = -1;
+    if (s.test_withhold_cta >= 0) {  // one launch only
+        a.timeout_ns = s.test_wait_ns;
+        a.withhold_cta = s.test_withhold_cta;
+        s.test_withhold_cta = -1;
+    }
     const size_t smem = mk_smem(m, MR, nW, nstage);
     void* args[] = {&a};
     const void* f = MR == 1 ? (const void*)k_decode_mega<1>
@@ -2552,6 +2575,26 @@ int32_t fb2_test_mk_trace(fb2_session* S, uint64_t* out, int64_t capacity, int32
 
 // n successive NextDouble() values of `new Random(seed)` as the library
 // restates it (host code; needs no device).
+int32_t fb2_test_mk_withhold(fb2_session* S, int32_t cta, int64_t wait_ns) {
+    return guarded([&] {
+        if (!S || S->ds.empty()) fail(FB2_INVALID_ARG, "session is NULL");
+        if (cta < 0 || wait_ns <= 0 || wait_ns > (int64_t)MK_TIMEOUT_NS) fail(FB2_INVALID_ARG, "bad hook arguments");
+        DeviceSession& s = *S->ds[0];
+        if (!s.mk_use) fail(FB2_UNSUPPORTED, "the session does not use the persistent decode kernel");
+        if (cta >= s.dm->mk_nW) fail(FB2_INVALID_ARG, "no such CTA");
+        s.test_withhold_cta = cta;
+        s.test_wait_ns = (unsigned long long)wait_ns;
+    });
+}
+
+int32_t fb2_test_fail_alloc(int64_t nth, int64_t* allocs_so_far) {
+    return guarded([&] {
+        if (nth < 0) fail(FB2_INVALID_ARG, "nth must be >= 0");
+        if (allocs_so_far) *allocs_so_far = g_alloc_count.load();
+        g_fail_alloc_at = nth > 0 ? g_alloc_count.load() + nth : 0;
+    });
+}
+
 int32_t fb2_test_dotnet_random(int32_t seed, int32_t n, double* out) {
     return guarded([&] {
         if (!out || n < 0) fail(FB2_INVALID_ARG, "bad arguments");

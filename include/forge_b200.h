@@ -10,7 +10,7 @@
  * The C# side keeps checkpoint loading, the tokenizer and the CLI; it hands
  * the fp32 weights (Parameters.Names order, GptModel.cs:14-18) to
  * fb2_model_create and calls fb2_generate from a B200Backend that the
- * reference's BackendSelection (src/LLM.Core/Tensor/BackendSelection.cs:160-180)
+ * reference's BackendSelection (src/LLM.Core/Tensor/BackendSelection.cs:17-18)
  * selects by the name "b200".
  *
  * Conventions

@@ -34,6 +34,20 @@ struct fb2_session;
 int32_t fb2_test_mk_trace(struct fb2_session* s, uint64_t* out, int64_t capacity, int32_t* n_ctas,
                           int32_t* n_steps);
 
+/* Failure detection without a GPU fault.  The next persistent-kernel launch
+ * of the session's first device: CTA `cta` does not publish its q words of
+ * that launch's first step (layer 0), and every bounded wait of the launch
+ * gives up after wait_ns (<= 2 s) instead of 2 s.  The waiting CTAs record a
+ * timeout, leave together, and the call returns FB2_TIMEOUT; the session
+ * stays usable. */
+int32_t fb2_test_mk_withhold(struct fb2_session* s, int32_t cta, int64_t wait_ns);
+
+/* Host-side allocation failure: the nth device allocation the library makes
+ * from now on (counted over the process) fails as cudaMalloc's
+ * out-of-memory would (FB2_OUT_OF_MEMORY); nth = 0 turns the hook off.
+ * allocs_so_far (may be NULL) receives the allocations made so far. */
+int32_t fb2_test_fail_alloc(int64_t nth, int64_t* allocs_so_far);
+
 /* SHA-256 of n bytes (the checkpoint trailer's hash; host only). */
 int32_t fb2_test_sha256(const void* data, int64_t n, uint8_t* out32);
 
