@@ -27,7 +27,10 @@ def host_exe(pkg, tmp_path_factory):
 
 
 def _lines(out: str) -> dict:
-    return {d["case"]: d for d in (json.loads(ln) for ln in out.splitlines() if ln.startswith("{"))}
+    got: dict = {}
+    for d in (json.loads(ln) for ln in out.splitlines() if ln.startswith("{")):
+        got.setdefault(d["case"], {}).update(d)  # a case's status line and its tokens line
+    return got
 
 
 def test_host_driver_without_a_device(host_exe, tmp_path):
