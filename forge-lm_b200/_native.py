@@ -40,7 +40,7 @@ EXPORTED = [
     "fb2_tokenizer_decode",
 ]
 TEST_EXPORTED = ["fb2_test_expf", "fb2_test_expf_hash", "fb2_test_dotnet_random", "fb2_test_mk_trace",
-                 "fb2_test_gemm_tc", "fb2_test_sha256", "fb2_test_mk_withhold", "fb2_test_fail_alloc"]
+                 "fb2_test_gemm_tc", "fb2_test_sha256", "fb2_test_mk_withhold", "fb2_test_fail_alloc", "fb2_test_mk_geometry"]
 
 
 class ModelDesc(C.Structure):
@@ -120,6 +120,7 @@ def load(path: str | None = None):
     L.fb2_test_sha256.argtypes = [vp, i64, vp]
     L.fb2_test_mk_withhold.argtypes = [vp, i32, i64]
     L.fb2_test_fail_alloc.argtypes = [i64, C.POINTER(i64)]
+    L.fb2_test_mk_geometry.argtypes = [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32), C.POINTER(i32)]
     L.fb2_forgemodel_read_header.argtypes = [C.c_char_p, C.POINTER(ModelDesc), C.c_char_p, i32]
     L.fb2_model_load_forgemodel.argtypes = [C.c_char_p, i32, i32p, i32, C.POINTER(ModelDesc), C.POINTER(vp)]
     L.fb2_forgemodel_write.argtypes = [C.c_char_p, C.POINTER(ModelDesc), C.c_char_p, C.POINTER(vp), i32]

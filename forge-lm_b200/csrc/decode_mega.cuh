@@ -44,6 +44,8 @@ constexpr unsigned long long MK_TIMEOUT_NS = 2000000000ull;  // default limit of
 // The launch's wait limit (MkArgs::timeout_ns), set by thread 0 before the
 // first barrier; every bounded wait of the kernel reads it.
 __shared__ unsigned long long mk_wait_ns;
+// Traced runs: thread 0's time spent waiting for ring stages (reset per phase).
+__shared__ unsigned long long mk_ring_wait;
 
 enum MkPhase { MK_QKV = 0, MK_PROJ = 1, MK_FC = 2, MK_PROJ2 = 3 };
 
@@ -86,6 +88,14 @@ struct MkArgs {
     int trace_steps;
     unsigned long long timeout_ns;  // limit of every bounded wait (MK_TIMEOUT_NS unless a test shortens it)
     int withhold_cta;               // test hook: this CTA never publishes its q words of step 0, layer 0 (-1: none)
+    // head-cluster layer path (hc = 1): clusters of `cs` CTAs; CTAs [0, nhead)
+    // = head h's cluster h (h = cta / cs) run LN1, the head's QKV columns,
+    // attention and the head's rows of the attention projection; CTAs
+    // [nhead, nW) run LN2, fc and mlp.proj over their hidden units.  Both
+    // residual sums go through the counted fixed-point accumulators `acc`
+    // ([2 step parity][L][2: x2, x][MK_MAX_ROWS][D]).
+    int hc, cs, nhead;
+    unsigned long long* acc;
 };
 
 // Trace points per step: 12 per layer for layers 0 and 1 (level A start, after
@@ -172,6 +182,117 @@ FB2_DEV void fence_acq_rel() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); 
 
 FB2_DEV uint32_t mk_tag(unsigned int gs, int layer, int L) { return gs * (unsigned)(L + 1) + (unsigned)layer + 1u; }
 
+// ---- cluster (distributed shared memory) helpers ---------------------------
+// Shared::cluster address of the same shared variable in cluster CTA `rank`.
+FB2_DEV uint32_t dsmem_addr(const void* local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+    return r;
+}
+FB2_DEV void dsmem_st(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+// Arrives on an mbarrier of a cluster CTA, releasing this CTA's earlier
+// writes (a CTA barrier before it makes the other threads' writes earlier).
+FB2_DEV void mbar_arrive_cluster(uint32_t addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+FB2_DEV bool mbar_try_cluster(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+FB2_DEV void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+FB2_DEV int ld_relaxed_i32(const int* p) {
+    int v;
+    asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Bounded wait for phase `parity` of a local mbarrier that cluster CTAs
+// arrive on.  Gives up on this CTA's abort, on a kernel error raised by any
+// CTA (checked every 64 polls), or after the launch's wait limit.
+FB2_DEV void wait_cluster_bar(uint64_t* b, uint32_t parity, int* err, volatile int* abort_flag) {
+    if (mbar_try_cluster(b, parity)) return;
+    const unsigned long long t0 = gtimer();
+    for (int n = 1;; n++) {
+        if (mbar_try_cluster(b, parity) || *abort_flag) return;
+        if ((n & 63) == 0 && ld_relaxed_i32(err) != 0) {
+            *abort_flag = 1;
+            return;
+        }
+        if (gtimer() - t0 > mk_wait_ns) {
+            atomicExch(err, 5);
+            *abort_flag = 1;
+            return;
+        }
+    }
+}
+
+// ---- counted fixed-point accumulators ----------------------------------------
+// A residual sum over many CTAs: word = (sum of round(v * 2^32)) << 8 | count.
+// Every contributor adds (round(v * 2^32) << 8) + 1 with one 64-bit atomic,
+// so the word is complete when its count reaches the number of contributors
+// and its value does not depend on the order of the additions (deterministic).
+// Range: |sum| < 2^23; resolution 2^-32.
+FB2_DEV unsigned long long acc_term(float v) {
+    const long long q = __float2ll_rn(v * 4294967296.0f);
+    return ((unsigned long long)q << 8) + 1ull;
+}
+FB2_DEV float acc_value(unsigned long long w) { return (float)((double)((long long)w >> 8) * 0x1p-32); }
+FB2_DEV void acc_add(unsigned long long* p, unsigned long long term) {
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(term) : "memory");
+}
+// out[i] = value of words src[i], i < n, once each word's count is `count`.
+__device__ __noinline__ void acc_gather(const unsigned long long* src, float* out, int n, uint32_t count, int* err,
+                                        volatile int* abort_flag) {
+    for (int base = 0; base < n; base += 8 * MK_CONS) {
+        unsigned long long w[8];
+        uint32_t pend = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int i = base + k * MK_CONS + (int)threadIdx.x;
+            w[k] = 0ull;
+            if (i < n) {
+                w[k] = ld_pair(src + i);
+                pend |= 1u << k;
+            }
+        }
+        unsigned long long t0 = 0;
+        for (int n_poll = 0;; n_poll++) {
+            uint32_t still = 0;
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if (((pend >> k) & 1u) && (uint32_t)(w[k] & 255ull) != count) still |= 1u << k;
+            if (!still || *abort_flag) break;
+            const unsigned long long now = gtimer();
+            if (!t0) t0 = now;
+            else if (now - t0 > mk_wait_ns) {
+                atomicExch(err, 6);
+                *abort_flag = 1;
+                break;
+            }
+            if ((n_poll & 63) == 63 && ld_relaxed_i32(err) != 0) {
+                *abort_flag = 1;
+                break;
+            }
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if ((still >> k) & 1u) w[k] = ld_pair(src + base + k * MK_CONS + (int)threadIdx.x);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int i = base + k * MK_CONS + (int)threadIdx.x;
+            if (i < n) out[i] = acc_value(w[k]);
+        }
+    }
+}
+
 // Column strip of CTA c for an N-column projection (balanced split).
 FB2_DEV void strip(int N, int nW, int c, int& n0, int& w) {
     n0 = (int)(((long long)c * N) / nW);
@@ -181,7 +302,8 @@ FB2_DEV void strip(int N, int nW, int c, int& n0, int& w) {
 // multiple of 16 bytes).
 FB2_DEV int strip_rows(int w, int K) {
     if (w <= 0) return 0;
-    int R = (MK_STAGE / 4 / w) & ~3;
+    int R = MK_STAGE / 4 / w;
+    if (w & 3) R &= ~3;  // a row of w floats is not a 16-byte multiple: whole groups of 4 rows
     return R < K ? R : K;
 }
 
@@ -401,6 +523,7 @@ FB2_DEV void wait_full(uint64_t* full, uint32_t it, int nstage, int* err, volati
             return;
         }
     }
+    if (threadIdx.x == 0) mk_ring_wait += gtimer() - t0;
 }
 
 FB2_DEV void release_stage(uint64_t* empty, uint32_t it, int nstage) {
@@ -480,12 +603,55 @@ __device__ __noinline__ void mk_layernorm(const float* src, float* dst, int D, c
     cons_sync();
 }
 
+// Shared memory of the head-cluster layer path (offsets in floats from a
+// 16-byte aligned base; every part a multiple of 4 floats):
+//   qkv_in [2][cs][MR][q3]   q/k/v parts pushed by each cluster CTA (q3 = 3 hd / cs)
+//   part_in[2][cs][MR][ps]   attention partials (max, sum, acc[hd]) pushed by each CTA
+//   ctxs   [MR][hd]          the head's combined context
+//   att_p  [np]              scores / probabilities of this CTA's keys of one row
+//   pvred  [256]             p.V partial sums per thread group
+//   ys     [MR][ymax]        outputs of a column slice
+//   hscr   [64]              q of one row, scratch
+//   mbar   [8] (u64)         qkv[2], part[2], exit
+//   lay    [L] MkLayer        the layer table (pointers), copied once per launch
+struct MkHcLayout {
+    int q3, ps, np, ymax;
+    int qkv_in, part_in, ctxs, att_p, pvred, ys, hscr, mbar, lay;
+    int total_floats;
+};
+__host__ __device__ inline int mk_r4(int v) { return (v + 3) & ~3; }
+__host__ __device__ inline MkHcLayout mk_hc_layout(int MR, int D, int F, int hd, int ctx, int cs, int nW, int nlayers) {
+    MkHcLayout L{};
+    const int jmax = (F + nW - 1) / nW;  // every CTA takes a share of the MLP
+    L.q3 = 3 * (hd / cs);
+    L.ps = mk_r4(hd + 2);
+    L.np = mk_r4((ctx + cs - 1) / cs);
+    int ym = L.q3 > D / cs ? L.q3 : D / cs;
+    L.ymax = mk_r4(ym > jmax ? ym : jmax);
+    int o = 0;
+    L.qkv_in = o; o += mk_r4(2 * cs * MR * L.q3);
+    L.part_in = o; o += 2 * cs * MR * L.ps;
+    L.ctxs = o; o += mk_r4(MR * hd);
+    L.att_p = o; o += L.np;
+    L.pvred = o; o += 256;
+    L.ys = o; o += MR * L.ymax;
+    L.hscr = o; o += 64;
+    L.mbar = o; o += 16;  // 8 x u64
+    L.lay = o; o += nlayers * (int)(sizeof(MkLayer) / 4);
+    L.total_floats = o;
+    return L;
+}
+
 // Shared-memory bytes the kernel needs besides the ring.
 inline size_t mk_aux_bytes(int MR, int D, int F, int H, int ctx, int slice_max, int maxc, int nstage) {
     size_t floats = (size_t)MR * F + 2 * (size_t)MR * D + (size_t)MR * 256 + (size_t)MR * slice_max + 512 + 512 + 2048;
     size_t ints = 2048 + (size_t)MR * ctx;
     size_t wts = 2 * (size_t)MR * H * maxc;
     return 2 * (size_t)nstage * 8 + floats * 4 + ints * 4 + MK_SURV_MAX * 8 + wts * 4;
+}
+// ... plus the head-cluster region (and its 16-byte alignment) when used.
+inline size_t mk_hc_bytes(int MR, int D, int F, int hd, int ctx, int cs, int nW, int nlayers) {
+    return (size_t)mk_hc_layout(MR, D, F, hd, ctx, cs, nW, nlayers).total_floats * 4 + 16;
 }
 
 // y[m][c] = sum_k act[m][k] * W[k][n0 + c] over this CTA's strip, with the
@@ -563,6 +729,110 @@ __device__ __noinline__ uint32_t mk_gemv_strip(const float* actv, int K, int N, 
     return it;
 }
 
+// y[m][c] = sum_k act[m][k] * W[k][c] for a [K][w] slice (w <= 256) whose
+// rows arrive through the ring in stages of strip_rows(w, K) rows.  Row
+// groups g (of G = 256 / w) keep four partial sums each; the G partials of
+// an output are summed in a fixed order.  ys[MR*w] holds the results behind
+// a barrier.  Returns the ring position after the slice.
+template <int MR>
+__device__ __noinline__ uint32_t mk_gemv_cols(const float* actv, int K, int w, unsigned char* ring, uint64_t* full,
+                                              uint64_t* empty, int nstage, uint32_t it, float* red, float* ys, int* err,
+                                              volatile int* abort_flag) {
+    const int tid = threadIdx.x;
+    const int R = strip_rows(w, K);
+    const int G = MK_CONS / w, g = tid / w, c = tid - g * w;
+    const bool valid = tid < G * w;
+    float acc[MR][4];
+#pragma unroll
+    for (int m = 0; m < MR; m++) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
+    for (int r0 = 0; r0 < K; r0 += R) {
+        const int rows = min(R, K - r0);
+        wait_full(full, it, nstage, err, abort_flag);
+        const float* st = reinterpret_cast<const float*>(ring + (size_t)(it % nstage) * MK_STAGE);
+        if (valid) {
+            const float* av = actv + r0;
+            int r = g;
+            for (; r + 3 * G < rows; r += 4 * G) {
+                const float v0 = st[r * w + c], v1 = st[(r + G) * w + c];
+                const float v2 = st[(r + 2 * G) * w + c], v3 = st[(r + 3 * G) * w + c];
+#pragma unroll
+                for (int m = 0; m < MR; m++) {
+                    acc[m][0] += av[m * K + r] * v0;
+                    acc[m][1] += av[m * K + r + G] * v1;
+                    acc[m][2] += av[m * K + r + 2 * G] * v2;
+                    acc[m][3] += av[m * K + r + 3 * G] * v3;
+                }
+            }
+            for (; r < rows; r += G) {
+                const float v = st[r * w + c];
+#pragma unroll
+                for (int m = 0; m < MR; m++) acc[m][0] += av[m * K + r] * v;
+            }
+        }
+        release_stage(empty, it, nstage);
+        it++;
+    }
+#pragma unroll
+    for (int m = 0; m < MR; m++) red[m * 256 + tid] = valid ? (acc[m][0] + acc[m][1]) + (acc[m][2] + acc[m][3]) : 0.f;
+    cons_sync();
+    for (int p = tid; p < MR * w; p += MK_CONS) {
+        const int m = p / w, cc = p - m * w;
+        const float* rp = red + m * 256 + cc;
+        float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+        int gg = 0;
+        for (; gg + 3 < G; gg += 4) {
+            t0 += rp[gg * w];
+            t1 += rp[(gg + 1) * w];
+            t2 += rp[(gg + 2) * w];
+            t3 += rp[(gg + 3) * w];
+        }
+        for (; gg < G; gg++) t0 += rp[gg * w];
+        ys[p] = (t0 + t1) + (t2 + t3);
+    }
+    cons_sync();
+    return it;
+}
+
+// Wide slice (256 < w <= 1024 columns): thread t sums columns t + 256 i over
+// the K rows, and adds each output to the fixed-point accumulator
+// out[m * w + c] (one count).  Returns the ring position after the slice.
+template <int MR>
+__device__ __noinline__ uint32_t mk_gemv_wide_acc(const float* actv, int K, int w, unsigned char* ring,
+                                                  uint64_t* full, uint64_t* empty, int nstage, uint32_t it,
+                                                  unsigned long long* out, int* err, volatile int* abort_flag) {
+    const int tid = threadIdx.x;
+    const int R = strip_rows(w, K);
+    float acc[MR][4];
+#pragma unroll
+    for (int m = 0; m < MR; m++) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
+    for (int r0 = 0; r0 < K; r0 += R) {
+        const int rows = min(R, K - r0);
+        wait_full(full, it, nstage, err, abort_flag);
+        const float* st = reinterpret_cast<const float*>(ring + (size_t)(it % nstage) * MK_STAGE);
+        for (int r = 0; r < rows; r++) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int c = tid + i * MK_CONS;
+                if (c < w) {
+                    const float v = st[r * w + c];
+#pragma unroll
+                    for (int m = 0; m < MR; m++) acc[m][i] += actv[m * K + r0 + r] * v;
+                }
+            }
+        }
+        release_stage(empty, it, nstage);
+        it++;
+    }
+#pragma unroll
+    for (int m = 0; m < MR; m++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int c = tid + i * MK_CONS;
+            if (c < w) acc_add(out + (size_t)m * w + c, acc_term(acc[m][i]));
+        }
+    return it;
+}
+
 #define MK_TRACE(pt)                                                                                 \
     do {                                                                                             \
         if (a.trace && tid == 0 && s < a.trace_steps && (pt) < MK_TRACE_POINTS)                     \
@@ -572,6 +842,11 @@ __device__ __noinline__ uint32_t mk_gemv_strip(const float* actv, int K, int N, 
     do {                                                                                             \
         if (a.trace && s < a.trace_steps && (pt) < MK_TRACE_POINTS)                                  \
             a.trace[((size_t)cta * a.trace_steps + s) * MK_TRACE_POINTS + (pt)] = gtimer();          \
+    } while (0)
+#define MK_TRACE_DUR(pt, v)                                                                         \
+    do {                                                                                            \
+        if (a.trace && tid == 0 && s < a.trace_steps && (pt) < MK_TRACE_POINTS)                    \
+            a.trace[((size_t)cta * a.trace_steps + s) * MK_TRACE_POINTS + (pt)] = (v);              \
     } while (0)
 #define MK_TRACE_L(off)                  \
     do {                                 \
@@ -602,6 +877,19 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     float* surv_v = reinterpret_cast<float*>(win + MR * a.ctx);  // [MK_SURV_MAX]
     int* surv_i = reinterpret_cast<int*>(surv_v + MK_SURV_MAX);  // [MK_SURV_MAX]
     float* wts_m = reinterpret_cast<float*>(surv_i + MK_SURV_MAX);  // [MR*H][maxc] chunk weights
+    // head-cluster region (hc launches only)
+    const MkHcLayout hcl = mk_hc_layout(MR, D, F, hd, a.ctx, a.hc ? a.cs : 1, nW, L);
+    float* hcb = reinterpret_cast<float*>(
+        (reinterpret_cast<uintptr_t>(wts_m + 2 * MR * H * a.maxc) + 15) & ~(uintptr_t)15);
+    float* qkv_in = hcb + hcl.qkv_in;
+    float* part_in = hcb + hcl.part_in;
+    float* ctxs = hcb + hcl.ctxs;
+    float* att_p = hcb + hcl.att_p;
+    float* pvred = hcb + hcl.pvred;
+    float* hc_ys = hcb + hcl.ys;
+    float* hscr = hcb + hcl.hscr;
+    uint64_t* hc_mbar = reinterpret_cast<uint64_t*>(hcb + hcl.mbar);  // qkv[2], part[2], exit
+    MkLayer* hc_lay = reinterpret_cast<MkLayer*>(hcb + hcl.lay);
     // iscr regions
     uint32_t* seen = reinterpret_cast<uint32_t*>(iscr);  // [8] bits of the slice
     uint32_t* ban = seen + 8;                            // [8]
@@ -642,9 +930,16 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 8);
         }
+        if (a.hc && cta < a.nhead)
+            for (int i = 0; i < 5; i++) mbar_init(&hc_mbar[i], a.cs);  // one arrival per cluster CTA and round
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    if (a.hc)
+        for (int i = tid; i < L * (int)(sizeof(MkLayer) / 8); i += MK_THREADS)
+            reinterpret_cast<const float**>(hc_lay)[i] = reinterpret_cast<const float* const*>(a.layers)[i];
     __syncthreads();
+    // the cluster's mbarriers are initialised before any CTA arrives on them
+    if (a.hc) cluster_sync_all();
 
     // positions at step s (dummy rows stay at 0); attention units (m, h, c)
     // cover the cached keys [0, pos-1) in chunks of KC
@@ -694,9 +989,30 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
             const float* base = Wt + (size_t)K * n0;
             for (int r0 = 0; r0 < K && ok; r0 += R) issue(base + (size_t)r0 * w, (uint32_t)(min(R, K - r0) * w * 4), true);
         };
+        auto issue_cols = [&](const float* W, int K, int w) {
+            const int R = strip_rows(w, K);
+            if (R == 0) return;
+            for (int r0 = 0; r0 < K && ok; r0 += R) issue(W + (size_t)r0 * w, (uint32_t)(min(R, K - r0) * w * 4), true);
+        };
         for (int s = 0; s < a.nsteps && ok; s++) {
             const unsigned int gs = a.gstep0 + s;
-            for (int l = 0; l < L && ok; l++) {
+            if (a.hc) {
+                // this CTA's slices of every layer, in the order the consumers use them
+                const int q3 = hcl.q3, wp = D / a.cs;
+                const int j0 = (int)((long long)cta * F / nW), j1 = (int)((long long)(cta + 1) * F / nW);
+                for (int l = 0; l < L && ok; l++) {
+                    const MkLayer& ly = hc_lay[l];
+                    if (cta < a.nhead) {
+                        issue_cols(ly.w[MK_QKV] + (size_t)cta * D * q3, D, q3);
+                        issue_cols(ly.w[MK_PROJ] + (size_t)cta * hd * wp, hd, wp);
+                    }
+                    if (j1 > j0) {
+                        issue_cols(ly.w[MK_FC] + (size_t)D * j0, D, j1 - j0);
+                        issue_cols(ly.w[MK_PROJ2] + (size_t)j0 * D, j1 - j0, D);
+                    }
+                }
+            }
+            for (int l = 0; l < L && ok && !a.hc; l++) {
                 const MkLayer& ly = a.layers[l];
                 issue_strip(ly.w[MK_QKV], D, 3 * D);
                 if (l == 0 && gs >= 2 && ok) {
@@ -750,6 +1066,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     }
 
     // =========================== consumers ==================================
+    // (a lambda: every early exit of the consumers returns here, so that the
+    // head clusters' exit handshake below always runs)
+    auto consumers = [&]() {
     const int lane = tid & 31, warp = tid >> 5;
     const float scale = 1.0f / sqrtf((float)hd);  // Layers.cs:174
     const SampleParams sp = a.sp;
@@ -785,7 +1104,273 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         }
         cons_sync();
         MK_TRACE(24);
-        for (int l = 0; l < L; l++) {
+        if (a.hc) {
+            // ======== head-cluster layers ========
+            // Per layer two exchanges through global memory: the attention
+            // projection's head partials -> x2, every CTA's MLP partials -> x
+            // (counted fixed-point accumulators).  q/k/v parts and attention
+            // partials move inside a head's cluster (DSMEM).  Parameters a
+            // phase needs are loaded before the wait that precedes it.
+            const int cs = a.cs, nhead = a.nhead;
+            const bool is_head = cta < nhead;
+            const int hh = cta / cs, rk = cta - (cta / cs) * cs;
+            const int hq = hd / cs, q3 = hcl.q3, wp = D / cs, ps = hcl.ps;
+            const int j0 = (int)((long long)cta * F / nW);
+            const int J = (int)((long long)(cta + 1) * F / nW) - j0;
+            const unsigned int par = gs & 1u;
+            // per-thread columns n = tid + 256 k (D <= 1024)
+            auto load_cols = [&](const float* b, float (&r)[4]) {
+#pragma unroll
+                for (int k = 0; k < 4; k++) r[k] = tid + k * MK_CONS < D ? __ldg(b + tid + k * MK_CONS) : 0.f;
+            };
+            LnRegs ln1{};
+            float bqkv = 0.f;
+            if (is_head) {
+                ln1 = ln_prefetch(hc_lay[0].ln1w, hc_lay[0].ln1b, D);
+                const int c = tid % q3, part = c / hq, i = c - part * hq;
+                if (tid < MR * q3) bqkv = __ldg(hc_lay[0].b[MK_QKV] + part * D + hh * hd + rk * hq + i);
+            }
+            for (int l = 0; l < L; l++) {
+                const MkLayer& ly = hc_lay[l];
+                unsigned long long* accx2 = a.acc + (((size_t)par * L + l) * 2) * MK_MAX_ROWS * D;
+                unsigned long long* accx = accx2 + (size_t)MK_MAX_ROWS * D;
+                // the cluster mbarriers start at phase 0 in every launch: rounds count
+                // from the launch's first step
+                const unsigned int rnd = (unsigned)s * (unsigned)L + (unsigned)l;
+                const int buf = (int)(rnd & 1u);
+                const uint32_t bpar = (rnd >> 1) & 1u;
+                MK_TRACE_L(0);
+                if (l == 0) {
+                    for (int m = 0; m < MR; m++) {
+                        const float* te = a.tok_emb + (size_t)s_tok[m] * D;
+                        const float* pe = a.pos_emb + (size_t)pos_of(m, s) * D;
+                        for (int i = tid; i < D; i += MK_CONS) xres[m * D + i] = __ldg(te + i) + __ldg(pe + i);
+                    }
+                    cons_sync();
+                }
+                float bproj[4];
+                load_cols(ly.b[MK_PROJ], bproj);
+                if (is_head) {
+                    // ---- LN1 -> this CTA's q, k, v columns of head hh --------------
+                    mk_layernorm<MR>(xres, act, D, ln1, scr + 384);
+                    MK_TRACE_L(1);
+                    if (tid == 0) mk_ring_wait = 0;
+                    it = mk_gemv_cols<MR>(act, D, q3, ring, full, empty, a.nstage, it, red, hc_ys, a.err, &s_abort);
+                    MK_TRACE_L(2);
+                    if (l == 0) MK_TRACE_DUR(14, mk_ring_wait);
+                    const bool withhold = cta == a.withhold_cta && s == 0 && l == 0;
+                    for (int p = tid; p < MR * q3; p += MK_CONS) {
+                        const int m = p / q3, c = p - m * q3, part = c / hq, i = c - part * hq;
+                        const float v = hc_ys[p] + (p < MK_CONS ? bqkv  // loaded ahead by this thread
+                                                     : __ldg(ly.b[MK_QKV] + part * D + hh * hd + rk * hq + i));
+                        if (part > 0 && !s_dummy[m])
+                            a.kv[(size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
+                                 (part == 2 ? a.v_offset : 0) + ((size_t)hh * a.ctx + pos_of(m, s)) * hd + rk * hq + i] = v;
+                        float* dst = qkv_in + ((buf * cs + rk) * MR + m) * q3 + c;
+                        for (int q = 0; q < cs; q++) dsmem_st(dsmem_addr(dst, q), v);
+                    }
+                    cons_sync();
+                    MK_TRACE_L(19);
+                    if (tid == 0 && !withhold)
+                        for (int q = 0; q < cs; q++) mbar_arrive_cluster(dsmem_addr(&hc_mbar[buf], q));
+                    // keys of row 0 older than the current one, loaded while the
+                    // cluster's q/k/v parts arrive (thread t: key k0 + t)
+                    float4 kreg[16];
+                    {
+                        const int pos = pos_of(0, s), T = pos + 1;
+                        const int j = (int)((long long)rk * T / cs) + tid;
+                        const int k1 = (int)((long long)(rk + 1) * T / cs);
+                        const float4* kr = reinterpret_cast<const float4*>(
+                            a.kv + (size_t)s_slot[0] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
+                            ((size_t)hh * a.ctx + j) * hd);
+#pragma unroll
+                        for (int e = 0; e < 16; e++)
+                            kreg[e] = (j < k1 && j < pos && e < hd / 4) ? __ldcg(kr + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                    wait_cluster_bar(&hc_mbar[buf], bpar, a.err, &s_abort);
+                    MK_TRACE_L(3);
+                    if (cons_sync_or(s_abort)) return;
+                    // ---- attention of head hh over this CTA's share of the keys -----
+                    for (int m = 0; m < MR; m++) {
+                        const int pos = pos_of(m, s), T = pos + 1;
+                        const int k0 = (int)((long long)rk * T / cs), k1 = (int)((long long)(rk + 1) * T / cs);
+                        const int nk = k1 - k0;
+                        const float* qin = qkv_in + (buf * cs * MR + m) * q3;  // rank q at + q * MR * q3
+                        auto qkv_at = [&](int part, int d) {  // element d of q / k / v of row m
+                            return qin[(d / hq) * MR * q3 + part * hq + (d % hq)];
+                        };
+                        if (tid < hd) hscr[tid] = qkv_at(0, tid);
+                        cons_sync();
+                        const float* kbase = a.kv + (size_t)s_slot[m] * a.kv_slot_stride +
+                                             (size_t)l * a.kv_layer_stride + (size_t)hh * a.ctx * hd;
+                        const float* vbase = kbase + a.v_offset;
+                        float mloc = -INFINITY;
+                        for (int t = tid; t < nk; t += MK_CONS) {
+                            const int j = k0 + t;
+                            float d = 0.f;
+                            if (j < pos) {
+                                const float4* q4 = reinterpret_cast<const float4*>(hscr);
+                                if (m == 0 && t < MK_CONS) {
+#pragma unroll
+                                    for (int e = 0; e < 16; e++)
+                                        if (e < hd / 4) {
+                                            const float4 kv4 = kreg[e], qv = q4[e];
+                                            d += qv.x * kv4.x + qv.y * kv4.y + qv.z * kv4.z + qv.w * kv4.w;
+                                        }
+                                } else {
+                                    const float4* kr = reinterpret_cast<const float4*>(kbase + (size_t)j * hd);
+                                    for (int e = 0; e < hd / 4; e++) {
+                                        const float4 kv4 = __ldcg(kr + e), qv = q4[e];
+                                        d += qv.x * kv4.x + qv.y * kv4.y + qv.z * kv4.z + qv.w * kv4.w;
+                                    }
+                                }
+                            } else {
+                                for (int e = 0; e < hd; e++) d += hscr[e] * qkv_at(1, e);
+                            }
+                            const float sc = d * scale;
+                            att_p[t] = sc;
+                            mloc = fmaxf(mloc, sc);
+                        }
+                        // this thread's V values (dimension d, keys g, g + ng, ...),
+                        // loaded before the softmax reductions
+                        const int ng = MK_CONS / hd, d = tid % hd, g = tid / hd;
+                        float vv[8];
+                        const int nv = (nk - g + ng - 1) / ng;
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const int j = k0 + g + i * ng;
+                            vv[i] = 0.f;
+                            if (i < nv) vv[i] = j < pos ? __ldcg(vbase + (size_t)j * hd + d) : qkv_at(2, d);
+                        }
+                        mloc = warp_max(mloc);
+                        if (lane == 0) scr[256 + warp] = mloc;
+                        cons_sync();
+                        float M = -INFINITY;
+#pragma unroll
+                        for (int w8 = 0; w8 < 8; w8++) M = fmaxf(M, scr[256 + w8]);
+                        float lsum = 0.f;
+                        for (int t = tid; t < nk; t += MK_CONS) {
+                            const float pr = __expf(att_p[t] - M);
+                            att_p[t] = pr;
+                            lsum += pr;
+                        }
+                        const float S = cons_sum_slot(lsum, scr + 272);  // barrier: att_p complete
+                        if (m == 0) MK_TRACE_L(20);
+                        float av0 = 0.f, av1 = 0.f;
+#pragma unroll
+                        for (int i = 0; i < 8; i += 2) {
+                            if (i < nv) av0 += att_p[g + i * ng] * vv[i];
+                            if (i + 1 < nv) av1 += att_p[g + (i + 1) * ng] * vv[i + 1];
+                        }
+                        for (int i = 8; i < nv; i++) {
+                            const int j = k0 + g + i * ng;
+                            av0 += att_p[g + i * ng] * (j < pos ? __ldcg(vbase + (size_t)j * hd + d) : qkv_at(2, d));
+                        }
+                        pvred[g * hd + d] = av0 + av1;
+                        cons_sync();
+                        if (m == 0) MK_TRACE_L(21);
+                        float* pdst = part_in + ((buf * cs + rk) * MR + m) * ps;
+                        if (tid < hd) {
+                            float A = 0.f;
+                            for (int gg = 0; gg < ng; gg++) A += pvred[gg * hd + tid];
+                            for (int q = 0; q < cs; q++) dsmem_st(dsmem_addr(pdst + 2 + tid, q), A);
+                        } else if (tid == hd) {
+                            for (int q = 0; q < cs; q++) {
+                                dsmem_st(dsmem_addr(pdst, q), nk > 0 ? M : -INFINITY);
+                                dsmem_st(dsmem_addr(pdst + 1, q), nk > 0 ? S : 0.f);
+                            }
+                        }
+                        cons_sync();
+                    }
+                    MK_TRACE_L(4);
+                    if (tid == 0)
+                        for (int q = 0; q < cs; q++) mbar_arrive_cluster(dsmem_addr(&hc_mbar[2 + buf], q));
+                    wait_cluster_bar(&hc_mbar[2 + buf], bpar, a.err, &s_abort);
+                    MK_TRACE_L(5);
+                    if (cons_sync_or(s_abort)) return;
+                    // ---- combine the cluster's partials -> ctx of head hh -------------
+                    for (int p = tid; p < MR * hd; p += MK_CONS) {
+                        const int m = p / hd, dd = p - m * hd;
+                        const float* pr = part_in + (buf * cs * MR + m) * ps;
+                        float Ms = -INFINITY;
+                        for (int q = 0; q < cs; q++) Ms = fmaxf(Ms, pr[q * MR * ps]);
+                        float ls = 0.f, A = 0.f;
+                        for (int q = 0; q < cs; q++) {
+                            const float* pq = pr + q * MR * ps;
+                            const float w = pq[0] == -INFINITY ? 0.f : __expf(pq[0] - Ms);
+                            ls += pq[1] * w;
+                            A += pq[2 + dd] * w;
+                        }
+                        ctxs[p] = A / ls;
+                    }
+                    cons_sync();
+                    MK_TRACE_L(18);
+                    // ---- this CTA's columns of ctx_hh * Wproj[hh rows] -> x2 partials --
+                    if (tid == 0) mk_ring_wait = 0;
+                    it = mk_gemv_cols<MR>(ctxs, hd, wp, ring, full, empty, a.nstage, it, red, hc_ys, a.err, &s_abort);
+                    MK_TRACE_L(6);
+                    if (l == 0) MK_TRACE_DUR(15, mk_ring_wait);
+                    for (int p = tid; p < MR * wp; p += MK_CONS) {
+                        const int m = p / wp, c = p - m * wp;
+                        acc_add(accx2 + (size_t)m * D + rk * wp + c, acc_term(hc_ys[p]));
+                    }
+                    MK_TRACE_L(7);
+                }
+                // ---- x2 = x + attention projection; LN2 -> fc -> GELU -> proj2 ------
+                const LnRegs ln2 = ln_prefetch(ly.ln2w, ly.ln2b, D);
+                const float bfc = tid < MR * J ? __ldg(ly.b[MK_FC] + j0 + tid % J) : 0.f;
+                acc_gather(accx2, act, MR * D, (uint32_t)(nhead / cs), a.err, &s_abort);
+                cons_sync();
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int n = tid + k * MK_CONS;
+                    if (n < D)
+                        for (int m = 0; m < MR; m++) x2res[m * D + n] = xres[m * D + n] + (act[m * D + n] + bproj[k]);
+                }
+                MK_TRACE_L(8);
+                if (cons_sync_or(s_abort)) return;
+                float bproj2[4];
+                load_cols(ly.b[MK_PROJ2], bproj2);
+                mk_layernorm<MR>(x2res, act, D, ln2, scr + 384);
+                MK_TRACE_L(11);
+                if (J > 0) {
+                    float* hb = act + MR * D;  // [MR][J]
+                    if (tid == 0) mk_ring_wait = 0;
+                    it = mk_gemv_cols<MR>(act, D, J, ring, full, empty, a.nstage, it, red, hc_ys, a.err, &s_abort);
+                    MK_TRACE_L(12);
+                    if (l == 0) MK_TRACE_DUR(16, mk_ring_wait);
+                    for (int p = tid; p < MR * J; p += MK_CONS)
+                        hb[p] = gelu_tanh(hc_ys[p] + (p < MK_CONS ? bfc : __ldg(ly.b[MK_FC] + j0 + p % J)));
+                    cons_sync();
+                    MK_TRACE_L(13);
+                    if (tid == 0) mk_ring_wait = 0;
+                    it = mk_gemv_wide_acc<MR>(hb, J, D, ring, full, empty, a.nstage, it, accx, a.err, &s_abort);
+                    if (l == 0) MK_TRACE_DUR(17, mk_ring_wait);
+                } else {
+                    for (int p = tid; p < MR * D; p += MK_CONS) acc_add(accx + p, acc_term(0.f));
+                }
+                MK_TRACE_L(9);
+                // next layer's LN1 parameters and qkv bias, loaded during the wait
+                if (is_head && l + 1 < L) {
+                    ln1 = ln_prefetch(hc_lay[l + 1].ln1w, hc_lay[l + 1].ln1b, D);
+                    const int c = tid % q3, part = c / hq, i = c - part * hq;
+                    if (tid < MR * q3) bqkv = __ldg(hc_lay[l + 1].b[MK_QKV] + part * D + hh * hd + rk * hq + i);
+                }
+                // ---- x of the next layer (every CTA) --------------------------------
+                acc_gather(accx, act, MR * D, (uint32_t)nW, a.err, &s_abort);
+                cons_sync();
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int n = tid + k * MK_CONS;
+                    if (n < D)
+                        for (int m = 0; m < MR; m++) xres[m * D + n] = x2res[m * D + n] + (act[m * D + n] + bproj2[k]);
+                }
+                if (cons_sync_or(s_abort)) return;
+                MK_TRACE_L(10);
+                if (l < 24) MK_TRACE(33 + l);
+            }
+        }
+        for (int l = 0; l < L && !a.hc; l++) {
             const MkLayer& ly = a.layers[l];
             const uint32_t tg = mk_tag(gs, l, L);
             MK_TRACE_L(0);
@@ -1125,9 +1710,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         // ---- head: LN_f -> logits of this CTA's vocabulary slice ----------------
         const uint32_t th = mk_tag(gs, L, L);
         const LnRegs lnf = ln_prefetch(a.lnf_w, a.lnf_b, D);
-        {
+        if (!a.hc) {
             gather_tagged(a.xx, xres, MR * D, mk_tag(gs, L - 1, L), a.err, &s_abort);
             if (cons_sync_or(s_abort)) return;
+        } else {
+            // zero the accumulator set the next step uses (the previous step's,
+            // read by every CTA before this step began); the fence before this
+            // step's header publish orders the zeros before the next step's adds
+            const size_t W = (size_t)L * 2 * MK_MAX_ROWS * D;
+            unsigned long long* z = a.acc + (size_t)((gs & 1u) ^ 1u) * W;
+            const size_t z0 = (size_t)cta * W / nW, z1 = (size_t)(cta + 1) * W / nW;
+            for (size_t i = z0 + tid; i < z1; i += MK_CONS) z[i] = 0ull;
         }
         MK_TRACE(25);
         // this step's uniform for row tid, loaded before the head (a cold
@@ -1377,6 +1970,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
 #pragma unroll
                 for (int q4 = 0; q4 < 9; q4++) w[q4] = ld_pair(hp + q4);
                 resolve_batch<9>(w, 0x1ffu, [&](int k) { return hp + k; }, th, a.err, &s_abort);
+                if (m == 0) MK_TRACE(55);
                 cnts[tid] = __float_as_int(pair_value(w[0]));
 #pragma unroll
                 for (int q4 = 0; q4 < 4; q4++) {
@@ -1385,6 +1979,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 }
             }
             if (cons_sync_or(s_abort)) return;
+            if (m == 0) MK_TRACE(56);
             fence_acq_rel();
             if (m == 0) MK_TRACE(57);
             if (!sampled) {
@@ -1684,6 +2279,19 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
             atomicAdd(a.stepdone, 1u);
         }
         MK_TRACE(32);
+    }
+    };
+    consumers();
+    if (a.hc && cta < a.nhead) {
+        // no CTA of a head cluster leaves while a cluster CTA may still write
+        // into its shared memory: each arrives on every CTA's exit barrier after
+        // its last push, then waits (bounded) for all of them
+        cons_sync();
+        if (tid == 0)
+            for (int q = 0; q < a.cs; q++) mbar_arrive_cluster(dsmem_addr(&hc_mbar[4], q));
+        const unsigned long long t0 = gtimer();
+        while (!mbar_try_cluster(&hc_mbar[4], 0))
+            if (gtimer() - t0 > 4 * mk_wait_ns) break;
     }
 }
 

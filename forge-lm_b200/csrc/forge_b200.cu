@@ -162,6 +162,10 @@ struct DeviceModel {
     // persistent decode kernel: projections re-laid as per-CTA column strips
     bool mk_ok = false;
     int mk_nW = 0;
+    // head-cluster layout of the persistent kernel: clusters of mk_cs CTAs,
+    // mk_nhead = H * mk_cs attention CTAs, the rest run the MLP
+    bool mk_hc = false;
+    int mk_cs = 1, mk_nhead = 0;
     float* relaid = nullptr;
     MkLayer* d_mk_layers = nullptr;
     // tensor-core GEMM: TF32 hi/lo halves of the four projections per layer
@@ -266,14 +270,16 @@ static int mk_maxc(int ctx, int hd) { return ceil_div(ctx, mk_keys_per_chunk(hd)
 // shared-memory region after the slices stays 16-byte aligned.
 static int mk_slice_max(int V, int nW) { return (ceil_div(V, nW) + 3) & ~3; }
 
-// Dynamic shared memory of k_decode_mega<MR> with `nstage` ring stages.
-static size_t mk_smem(const fb2_model& m, int MR, int nW, int nstage) {
+// Dynamic shared memory of k_decode_mega<MR> with `nstage` ring stages
+// (cs > 0: the head-cluster layout, clusters of cs CTAs).
+static size_t mk_smem(const fb2_model& m, int MR, int nW, int nstage, int cs = 0) {
     return (size_t)nstage * MK_STAGE +
-           mk_aux_bytes(MR, m.D, m.F, m.H, m.ctx, mk_slice_max(m.V, nW), mk_maxc(m.ctx, m.hd), nstage) + 256;
+           mk_aux_bytes(MR, m.D, m.F, m.H, m.ctx, mk_slice_max(m.V, nW), mk_maxc(m.ctx, m.hd), nstage) +
+           (cs > 0 ? mk_hc_bytes(MR, m.D, m.F, m.hd, m.ctx, cs, nW, m.L) : 0) + 256;
 }
 
 // Ring stages that fit next to the kernel's other shared memory (0: does not fit).
-static int mk_nstage(const fb2_model& m, int MR, int nW, int device) {
+static int mk_nstage(const fb2_model& m, int MR, int nW, int device, int cs = 0) {
     int optin = 0;
     CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
     cudaFuncAttributes fa;
@@ -284,8 +290,31 @@ static int mk_nstage(const fb2_model& m, int MR, int nW, int device) {
     CK(cudaFuncGetAttributes(&fa, f));
     const long long avail = (long long)optin - (long long)fa.sharedSizeBytes;
     int ns = 16;
-    while (ns >= 4 && (long long)mk_smem(m, MR, nW, ns) > avail) ns--;
+    while (ns >= 4 && (long long)mk_smem(m, MR, nW, ns, cs) > avail) ns--;
     return ns >= 4 ? ns : 0;
+}
+
+// Clusters of `cs` CTAs of k_decode_mega<1> that can be resident at once.
+static int mk_max_clusters(const fb2_model& m, int nW, int cs, int device) {
+    const int ns = mk_nstage(m, 1, nW, device, cs);
+    if (ns == 0) return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nW);
+    cfg.blockDim = dim3(MK_THREADS);
+    cfg.dynamicSmemBytes = mk_smem(m, 1, nW, ns, cs);
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cs;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)k_decode_mega<1>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
 }
 
 // ---- bf16 weights ---------------------------------------------------------------
@@ -385,9 +414,37 @@ static void tc_setup(const fb2_model& m, DeviceModel& dm) {
 
 // Re-lays every projection W[K][N] as consecutive column strips [K][w_c],
 // one per CTA (the split k_decode_mega streams), and uploads the layer table.
+// Head-cluster geometry for this model on this device, if it applies:
+// clusters of 4 CTAs, one per head; at least half as many MLP CTAs as
+// attention CTAs; every slice no wider than the column kernels take.
+static bool mk_hc_plan(const fb2_model& m, DeviceModel& dm) {
+    const char* env = getenv("FORGE_B200_MK");
+    if (!(env && std::string(env) == "hc")) return false;  // opt-in while it is tuned
+    const char* ecs = getenv("FORGE_B200_MK_CS");
+    const int want = ecs ? atoi(ecs) : 0;
+    // clusters of 8 when 8 CTAs per head fit the resident grid, else of 4
+    for (int cs : {8, 4}) {
+        if (want && cs != want) continue;
+        if (m.hd % cs != 0 || m.D % (4 * cs) != 0 || m.D > 1024 || 3 * m.hd / cs > 256) continue;
+        const int nhead = m.H * cs;
+        int nW = (dm.sm_count / cs) * cs;
+        const int nc = mk_max_clusters(m, nW, cs, dm.device);
+        nW = std::min(nW, nc * cs);
+        if (nhead > nW || ceil_div(m.F, nW) > 256 || nW < 32) continue;
+        if (mk_slice_max(m.V, nW) > MK_SLICE_MAX) continue;
+        dm.mk_hc = true;
+        dm.mk_cs = cs;
+        dm.mk_nhead = nhead;
+        dm.mk_nW = nW;
+        return true;
+    }
+    return false;
+}
+
 static void mk_setup(const fb2_model& m, DeviceModel& dm, const float* const* params) {
     dm.mk_ok = false;
-    const int nW = dm.sm_count;
+    dm.mk_hc = false;
+    int nW = dm.sm_count;
     if (!(m.hd == 32 || m.hd == 64)) return;
     if (mk_maxc(m.ctx, m.hd) > 32) return;
     if (m.V <= m.ctx) return;  // the ban of a whole window could then cover the vocabulary
@@ -395,6 +452,8 @@ static void mk_setup(const fb2_model& m, DeviceModel& dm, const float* const* pa
     if (m.D * 4 > MK_STAGE) return;
     if (8 * ceil_div(4 * m.D, nW) > 512) return;  // strip outputs staged in a 512-float scratch
     if (mk_nstage(m, 1, nW, dm.device) == 0) return;
+    const bool hc = mk_hc_plan(m, dm);
+    if (hc) nW = dm.mk_nW;
     const size_t D = m.D, F = m.F;
     const size_t per_layer = 3 * D * D + D * D + D * F + F * D;
     dm.relaid = dalloc<float>(per_layer * m.L);
@@ -406,10 +465,45 @@ static void mk_setup(const fb2_model& m, DeviceModel& dm, const float* const* pa
         size_t off = per_layer * l;
         for (int ph = 0; ph < 4; ph++) {
             const size_t K = mats[ph].K, N = mats[ph].N;
-            for (int c = 0; c < nW; c++) {
-                const size_t n0 = (size_t)c * N / nW, n1 = (size_t)(c + 1) * N / nW, w = n1 - n0;
-                for (size_t k = 0; k < K; k++)
-                    std::memcpy(&tmp[K * n0 + k * w], mats[ph].W + k * N + n0, w * sizeof(float));
+            const float* W = mats[ph].W;
+            if (hc) {
+                // head CTA c = (head h, rank r) reads QKV as [D][3 hq] (its q, k, v
+                // columns of head h) and proj as [hd][D/cs] (head h's rows, its
+                // column quarter); MLP CTA j reads fc as [D][J_j] (its hidden
+                // units); mlp.proj keeps its layout (rows j0..j1 are contiguous)
+                const size_t cs = dm.mk_cs, hd = m.hd, hq = hd / cs, nhead = dm.mk_nhead, nmlp = nW;
+                size_t o = 0;
+                if (ph == MK_QKV) {
+                    for (size_t c = 0; c < nhead; c++) {
+                        const size_t h = c / cs, r = c % cs;
+                        for (size_t k = 0; k < K; k++)
+                            for (size_t part = 0; part < 3; part++)
+                                for (size_t i = 0; i < hq; i++)
+                                    tmp[o + k * 3 * hq + part * hq + i] = W[k * N + part * D + h * hd + r * hq + i];
+                        o += K * 3 * hq;
+                    }
+                } else if (ph == MK_PROJ) {
+                    const size_t wp = D / cs;
+                    for (size_t c = 0; c < nhead; c++) {
+                        const size_t h = c / cs, r = c % cs;
+                        for (size_t d = 0; d < hd; d++)
+                            std::memcpy(&tmp[o + d * wp], W + (h * hd + d) * N + r * wp, wp * sizeof(float));
+                        o += hd * wp;
+                    }
+                } else if (ph == MK_FC) {
+                    for (size_t j = 0; j < nmlp; j++) {
+                        const size_t j0 = j * F / nmlp, j1 = (j + 1) * F / nmlp, w = j1 - j0;
+                        for (size_t k = 0; k < K; k++) std::memcpy(&tmp[K * j0 + k * w], W + k * N + j0, w * sizeof(float));
+                    }
+                } else {
+                    std::memcpy(tmp.data(), W, K * N * sizeof(float));
+                }
+            } else {
+                for (int c = 0; c < nW; c++) {
+                    const size_t n0 = (size_t)c * N / nW, n1 = (size_t)(c + 1) * N / nW, w = n1 - n0;
+                    for (size_t k = 0; k < K; k++)
+                        std::memcpy(&tmp[K * n0 + k * w], W + k * N + n0, w * sizeof(float));
+                }
             }
             CK(cudaMemcpy(dm.relaid + off, tmp.data(), K * N * sizeof(float), cudaMemcpyHostToDevice));
             host[l].w[ph] = dm.relaid + off;
@@ -507,6 +601,8 @@ struct DeviceSession {
     int *mk_err = nullptr, *mk_rows = nullptr;
     unsigned int mk_gstep = 0;
     size_t mk_tagged_words = 0;
+    unsigned long long* mk_acc = nullptr;  // head-cluster layout: counted fixed-point accumulators
+    size_t mk_acc_words = 0;
     unsigned long long* mk_trace = nullptr;
     int mk_trace_steps = 0;
 
@@ -534,6 +630,7 @@ static void mk_reset(DeviceSession& s) {
     CK(cudaMemsetAsync(s.mk_xq, 0, s.mk_tagged_words * 8, s.stream));
     CK(cudaMemsetAsync(s.mk_stepdone, 0, sizeof(unsigned int), s.stream));
     CK(cudaMemsetAsync(s.mk_err, 0, sizeof(int), s.stream));
+    if (s.mk_acc) CK(cudaMemsetAsync(s.mk_acc, 0, s.mk_acc_words * 8, s.stream));
     s.mk_gstep = 0;
 }
 
@@ -561,6 +658,10 @@ static void mk_session_alloc(DeviceSession& s) {
     s.mk_cidx = dalloc<int>(R * nW * slice);
     s.mk_stepdone = dalloc<unsigned int>(1);
     s.mk_err = dalloc<int>(1);
+    if (dm.mk_hc) {
+        s.mk_acc_words = 2 * (size_t)m.L * 2 * MK_MAX_ROWS * D;
+        s.mk_acc = dalloc<unsigned long long>(s.mk_acc_words);
+    }
     s.mk_rows = dalloc<int>(R);
     if (const char* tr = getenv("FORGE_B200_MK_TRACE")) {  // per-phase timestamps of the first steps
         s.mk_trace_steps = std::max(0, std::min(64, atoi(tr)));
@@ -587,7 +688,7 @@ static void session_free(DeviceSession* s) {
     dfree(s->d_logits); dfree(s->d_lnf); dfree(s->d_attn_part); dfree(s->d_gemv_part); dfree(s->d_tickets);
     dfree(s->d_tab); dfree(s->d_uni); dfree(s->d_out);
     dfree(s->mk_xq); dfree(s->mk_xacc); dfree(s->mk_cval); dfree(s->mk_cidx); dfree(s->mk_stepdone);
-    dfree(s->mk_err); dfree(s->mk_rows); dfree(s->mk_trace);
+    dfree(s->mk_err); dfree(s->mk_rows); dfree(s->mk_trace); dfree(s->mk_acc);
     if (s->h_tab) cudaFreeHost(s->h_tab);
     if (s->tab_event) cudaEventDestroy(s->tab_event);
     if (s->ev0) cudaEventDestroy(s->ev0);
@@ -969,7 +1070,8 @@ static void run_mega(DeviceSession& s, int n, int nsteps, const SampleParams& P,
     const DeviceModel& dm = *s.dm;
     const int MR = n <= 1 ? 1 : n <= 2 ? 2 : n <= 4 ? 4 : 8;
     const int nW = dm.mk_nW;
-    const int nstage = mk_nstage(m, MR, nW, s.device);
+    const int hc_cs = dm.mk_hc ? dm.mk_cs : 0;
+    const int nstage = mk_nstage(m, MR, nW, s.device, hc_cs);
     if (nstage == 0) fail(FB2_UNSUPPORTED, "persistent decode kernel does not fit shared memory");
     MkArgs a{};
     a.V = m.V; a.ctx = m.ctx; a.D = m.D; a.L = m.L; a.H = m.H; a.hd = m.hd; a.F = m.F;
@@ -999,13 +1101,37 @@ static void run_mega(DeviceSession& s, int n, int nsteps, const SampleParams& P,
         a.withhold_cta = s.test_withhold_cta;
         s.test_withhold_cta = -1;
     }
-    const size_t smem = mk_smem(m, MR, nW, nstage);
+    a.hc = dm.mk_hc ? 1 : 0;
+    a.cs = dm.mk_hc ? dm.mk_cs : 1;
+    a.nhead = dm.mk_hc ? dm.mk_nhead : 0;
+    a.acc = s.mk_acc;
+    const size_t smem = mk_smem(m, MR, nW, nstage, hc_cs);
     void* args[] = {&a};
     const void* f = MR == 1 ? (const void*)k_decode_mega<1>
                   : MR == 2 ? (const void*)k_decode_mega<2>
                   : MR == 4 ? (const void*)k_decode_mega<4>
                             : (const void*)k_decode_mega<8>;
-    CK(cudaLaunchCooperativeKernel(f, dim3(nW), dim3(MK_THREADS), args, smem, s.stream));
+    if (dm.mk_hc) {
+        // clusters of mk_cs CTAs; cooperative, so the launch fails rather than
+        // runs if not every CTA can be resident (the CTAs wait on one another)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(nW);
+        cfg.blockDim = dim3(MK_THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = s.stream;
+        cudaLaunchAttribute at[2];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = dm.mk_cs;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        at[1].id = cudaLaunchAttributeCooperative;
+        at[1].val.cooperative = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 2;
+        CK(cudaLaunchKernelExC(&cfg, f, args));
+    } else {
+        CK(cudaLaunchCooperativeKernel(f, dim3(nW), dim3(MK_THREADS), args, smem, s.stream));
+    }
     s.stats.kernel_launches++;
     s.stats.decode_steps += nsteps;
     s.stats.persistent_steps += nsteps;
@@ -2584,6 +2710,18 @@ int32_t fb2_test_mk_withhold(fb2_session* S, int32_t cta, int64_t wait_ns) {
         if (cta >= s.dm->mk_nW) fail(FB2_INVALID_ARG, "no such CTA");
         s.test_withhold_cta = cta;
         s.test_wait_ns = (unsigned long long)wait_ns;
+    });
+}
+
+int32_t fb2_test_mk_geometry(fb2_session* S, int32_t* n_ctas, int32_t* cluster, int32_t* attn_ctas, int32_t* stages) {
+    return guarded([&] {
+        if (!S || S->ds.empty() || !n_ctas || !cluster || !attn_ctas || !stages) fail(FB2_INVALID_ARG, "NULL argument");
+        DeviceSession& s = *S->ds[0];
+        const DeviceModel& dm = *s.dm;
+        *n_ctas = s.mk_use ? dm.mk_nW : 0;
+        *cluster = dm.mk_hc ? dm.mk_cs : 0;
+        *attn_ctas = dm.mk_hc ? dm.mk_nhead : 0;
+        *stages = s.mk_use ? mk_nstage(*s.model, 1, dm.mk_nW, s.device, dm.mk_hc ? dm.mk_cs : 0) : 0;
     });
 }
 

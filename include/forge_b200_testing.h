@@ -42,6 +42,12 @@ int32_t fb2_test_mk_trace(struct fb2_session* s, uint64_t* out, int64_t capacity
  * stays usable. */
 int32_t fb2_test_mk_withhold(struct fb2_session* s, int32_t cta, int64_t wait_ns);
 
+/* Geometry of the session's persistent decode kernel on its first device:
+ * CTAs, cluster size and attention CTAs of the head-cluster layout (0 when
+ * it uses column strips), and ring stages at one row. */
+int32_t fb2_test_mk_geometry(struct fb2_session* s, int32_t* n_ctas, int32_t* cluster, int32_t* attn_ctas,
+                             int32_t* stages);
+
 /* Host-side allocation failure: the nth device allocation the library makes
  * from now on (counted over the process) fails as cudaMalloc's
  * out-of-memory would (FB2_OUT_OF_MEMORY); nth = 0 turns the hook off.
