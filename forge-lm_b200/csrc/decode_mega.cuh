@@ -35,7 +35,8 @@ namespace fb2 {
 
 constexpr int MK_THREADS = 288;
 constexpr int MK_CONS = 256;
-constexpr int MK_STAGE = 16384;  // bytes per ring stage
+constexpr int MK_STAGE = 16384;     // bytes per ring stage (column-strip path)
+constexpr int MK_STAGE_HC = 32768;  // bytes per ring stage on the head-cluster path
 constexpr int MK_MAX_ROWS = 8;
 constexpr int MK_SLICE_MAX = 256;
 constexpr int MK_SURV_MAX = 512;
@@ -44,8 +45,14 @@ constexpr unsigned long long MK_TIMEOUT_NS = 2000000000ull;  // default limit of
 // The launch's wait limit (MkArgs::timeout_ns), set by thread 0 before the
 // first barrier; every bounded wait of the kernel reads it.
 __shared__ unsigned long long mk_wait_ns;
+// The launch's ring stage size in bytes (MkArgs::stage_bytes; MK_STAGE on
+// the column-strip path), set with mk_wait_ns.
+__shared__ int mk_sbytes;
 // Traced runs: thread 0's time spent waiting for ring stages (reset per phase).
 __shared__ unsigned long long mk_ring_wait;
+// Traced runs: thread 0's stamps inside the last column GEMV (start, after
+// the stages, after the reduction).
+__shared__ unsigned long long mk_gemv_t[3];
 
 enum MkPhase { MK_QKV = 0, MK_PROJ = 1, MK_FC = 2, MK_PROJ2 = 3 };
 
@@ -96,6 +103,8 @@ struct MkArgs {
     // ([2 step parity][L][2: x2, x][MK_MAX_ROWS][D]).
     int hc, cs, nhead;
     unsigned long long* acc;
+    unsigned int prod_sleep_ns;  // the producer's back-off while the ring is full
+    int stage_bytes;             // ring stage size: MK_STAGE, or MK_STAGE_HC on the head-cluster path
 };
 
 // Trace points per step: 12 per layer for layers 0 and 1 (level A start, after
@@ -234,6 +243,33 @@ FB2_DEV void wait_cluster_bar(uint64_t* b, uint32_t parity, int* err, volatile i
     }
 }
 
+FB2_DEV void dsmem_st_pair(uint32_t addr, float v, uint32_t tag) {
+    const unsigned long long w = ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+    asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(addr), "l"(w) : "memory");
+}
+// Waits until words buf[0..n) of this CTA's shared memory (pushed by cluster
+// CTAs) carry `tag`; bounded like every other wait.
+FB2_DEV void wait_tags_smem(const unsigned long long* buf, int n, uint32_t tag, int* err, volatile int* abort_flag) {
+    for (int i = threadIdx.x; i < n; i += MK_CONS) {
+        const volatile unsigned long long* p = buf + i;
+        if ((uint32_t)(*p >> 32) == tag) continue;
+        const unsigned long long t0 = gtimer();
+        for (int k = 1;; k++) {
+            if ((uint32_t)(*p >> 32) == tag) break;
+            if (*abort_flag) return;
+            if ((k & 63) == 0 && ld_relaxed_i32(err) != 0) {
+                *abort_flag = 1;
+                return;
+            }
+            if (gtimer() - t0 > mk_wait_ns) {
+                atomicExch(err, 5);
+                *abort_flag = 1;
+                return;
+            }
+        }
+    }
+}
+
 // ---- counted fixed-point accumulators ----------------------------------------
 // A residual sum over many CTAs: word = (sum of round(v * 2^32)) << 8 | count.
 // Every contributor adds (round(v * 2^32) << 8) + 1 with one 64-bit atomic,
@@ -302,7 +338,7 @@ FB2_DEV void strip(int N, int nW, int c, int& n0, int& w) {
 // multiple of 16 bytes).
 FB2_DEV int strip_rows(int w, int K) {
     if (w <= 0) return 0;
-    int R = MK_STAGE / 4 / w;
+    int R = mk_sbytes / 4 / w;
     if (w & 3) R &= ~3;  // a row of w floats is not a 16-byte multiple: whole groups of 4 rows
     return R < K ? R : K;
 }
@@ -510,9 +546,17 @@ __device__ __noinline__ float cons_kth_largest(const float* vals, int n, int k, 
     return key_float((uint32_t)st[0]);
 }
 
+// A consumer's ring position: stage index in the low 16 bits, the stage's
+// phase parity in bit 16 (advanced without a division).
+FB2_DEV uint32_t rp_stage(uint32_t it) { return it & 0xFFFFu; }
+FB2_DEV uint32_t rp_next(uint32_t it, int nstage) {
+    const uint32_t st = (it & 0xFFFFu) + 1u;
+    return st == (uint32_t)nstage ? ((it ^ 0x10000u) & 0x10000u) : ((it & 0x10000u) | st);
+}
 FB2_DEV void wait_full(uint64_t* full, uint32_t it, int nstage, int* err, volatile int* abort_flag) {
-    uint64_t* b = &full[it % nstage];
-    const uint32_t par = (it / nstage) & 1u;
+    (void)nstage;
+    uint64_t* b = &full[it & 0xFFFFu];
+    const uint32_t par = (it >> 16) & 1u;
     if (mbar_try(b, par)) return;
     const unsigned long long t0 = gtimer();
     while (!mbar_try(b, par)) {
@@ -527,8 +571,9 @@ FB2_DEV void wait_full(uint64_t* full, uint32_t it, int nstage, int* err, volati
 }
 
 FB2_DEV void release_stage(uint64_t* empty, uint32_t it, int nstage) {
+    (void)nstage;
     __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[it % nstage]);
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[it & 0xFFFFu]);
 }
 
 // Sum over the 256 consumer threads through shared scratch `scr` (8 floats).
@@ -605,8 +650,15 @@ __device__ __noinline__ void mk_layernorm(const float* src, float* dst, int D, c
 
 // Shared memory of the head-cluster layer path (offsets in floats from a
 // 16-byte aligned base; every part a multiple of 4 floats):
-//   qkv_in [2][cs][MR][q3]   q/k/v parts pushed by each cluster CTA (q3 = 3 hd / cs)
-//   part_in[2][cs][MR][ps]   attention partials (max, sum, acc[hd]) pushed by each CTA
+//   qkv_in [cs][MR][q3]      q/k/v parts pushed by each cluster CTA (q3 = 3 hd / cs),
+//                            64-bit words (round tag << 32 | value bits)
+//   part_in[cs][MR][ps]      attention partials (max, sum, acc[hd]) pushed by each CTA,
+//                            tagged words as qkv_in
+//   red_in [cs][MR][D / cs]  (MR <= 2) MLP partials of this CTA's column block
+//                            pushed by each cluster CTA, tagged words
+// One buffer each suffices: a round's words are read before any CTA can
+// reach the next round (that needs the layer's global sum, to which every
+// reader contributes after reading).
 //   ctxs   [MR][hd]          the head's combined context
 //   att_p  [np]              scores / probabilities of this CTA's keys of one row
 //   pvred  [256]             p.V partial sums per thread group
@@ -616,7 +668,7 @@ __device__ __noinline__ void mk_layernorm(const float* src, float* dst, int D, c
 //   lay    [L] MkLayer        the layer table (pointers), copied once per launch
 struct MkHcLayout {
     int q3, ps, np, ymax;
-    int qkv_in, part_in, ctxs, att_p, pvred, ys, hscr, mbar, lay;
+    int qkv_in, part_in, red_in, ctxs, att_p, pvred, ys, hscr, mbar, lay;
     int total_floats;
 };
 __host__ __device__ inline int mk_r4(int v) { return (v + 3) & ~3; }
@@ -629,14 +681,16 @@ __host__ __device__ inline MkHcLayout mk_hc_layout(int MR, int D, int F, int hd,
     int ym = L.q3 > D / cs ? L.q3 : D / cs;
     L.ymax = mk_r4(ym > jmax ? ym : jmax);
     int o = 0;
-    L.qkv_in = o; o += mk_r4(2 * cs * MR * L.q3);
-    L.part_in = o; o += 2 * cs * MR * L.ps;
+    L.qkv_in = o; o += 2 * mk_r4(cs * MR * L.q3);  // u64 words
+    L.part_in = o; o += 2 * (cs * MR * L.ps);
+    L.red_in = o; o += MR <= 2 ? 2 * mk_r4(cs * MR * (D / cs)) : 0;
     L.ctxs = o; o += mk_r4(MR * hd);
     L.att_p = o; o += L.np;
     L.pvred = o; o += 256;
     L.ys = o; o += MR * L.ymax;
     L.hscr = o; o += 64;
-    L.mbar = o; o += 16;  // 8 x u64
+    L.mbar = o; o += 16;  // 8 x u64; then 3 x 8 u32: cluster addresses of qkv_in, part_in, red_in per rank
+    o += 24;
     L.lay = o; o += nlayers * (int)(sizeof(MkLayer) / 4);
     L.total_floats = o;
     return L;
@@ -675,7 +729,7 @@ __device__ __noinline__ uint32_t mk_gemv_strip(const float* actv, int K, int N, 
     for (int r0 = 0; r0 < K; r0 += R) {
         const int rows = min(R, K - r0);
         wait_full(full, it, nstage, err, abort_flag);
-        const float* st = reinterpret_cast<const float*>(ring + (size_t)(it % nstage) * MK_STAGE);
+        const float* st = reinterpret_cast<const float*>(ring + (size_t)rp_stage(it) * mk_sbytes);
         if (valid) {
             const float* av = actv + r0;
             int r = g;
@@ -697,7 +751,7 @@ __device__ __noinline__ uint32_t mk_gemv_strip(const float* actv, int K, int N, 
             }
         }
         release_stage(empty, it, nstage);
-        it++;
+        it = rp_next(it, nstage);
     }
 #pragma unroll
     for (int m = 0; m < MR; m++) red[m * 256 + tid] = valid ? (acc[m][0] + acc[m][1]) + (acc[m][2] + acc[m][3]) : 0.f;
@@ -748,7 +802,7 @@ __device__ __noinline__ uint32_t mk_gemv_cols(const float* actv, int K, int w, u
     for (int r0 = 0; r0 < K; r0 += R) {
         const int rows = min(R, K - r0);
         wait_full(full, it, nstage, err, abort_flag);
-        const float* st = reinterpret_cast<const float*>(ring + (size_t)(it % nstage) * MK_STAGE);
+        const float* st = reinterpret_cast<const float*>(ring + (size_t)rp_stage(it) * mk_sbytes);
         if (valid) {
             const float* av = actv + r0;
             int r = g;
@@ -770,7 +824,7 @@ __device__ __noinline__ uint32_t mk_gemv_cols(const float* actv, int K, int w, u
             }
         }
         release_stage(empty, it, nstage);
-        it++;
+        it = rp_next(it, nstage);
     }
 #pragma unroll
     for (int m = 0; m < MR; m++) red[m * 256 + tid] = valid ? (acc[m][0] + acc[m][1]) + (acc[m][2] + acc[m][3]) : 0.f;
@@ -793,6 +847,159 @@ __device__ __noinline__ uint32_t mk_gemv_cols(const float* actv, int K, int w, u
     return it;
 }
 
+// y[m][c] = sum_k act[m][k] * W[k][c] for a [K][w] slice, w % 4 == 0: thread
+// (g, q) reads column quad q of rows g, g + G, ... as float4 (consecutive
+// threads read consecutive 16-byte words of a stage), two row chains each;
+// the G partials of an output go through scr (4096 floats) and are summed in
+// a fixed order into ys[MR*w] behind a barrier.
+// Geometry of a [K][w] column-quad slice (w % 4 == 0), computed once per
+// launch: R rows per ring stage; thread (g, q) = (tid >> lgp, tid & (2^lgp - 1))
+// reads quad q of rows g, g + G, ... (threads with q >= w / 4 or g >= G idle).
+struct MkGeo {
+    int R, G, lgp;
+};
+FB2_DEV MkGeo mk_geo(int w, int K, int MR) {
+    MkGeo g{0, 1, 0};
+    if (w <= 0) return g;
+    g.R = strip_rows(w, K);
+    const int nq = w >> 2;
+    while ((1 << g.lgp) < nq) g.lgp++;
+    g.G = MK_CONS >> g.lgp;
+    const int gcap = 4096 / (w * MR);
+    if (g.G > gcap) g.G = gcap;
+    if (g.G < 1) g.G = 1;
+    return g;
+}
+
+// y[m][c] = sum_k act[m][k] * W[k][c] for a [K][w] slice, w % 4 == 0: thread
+// (g, q) reads column quad q of rows g, g + G, ... as float4 (consecutive
+// threads read consecutive 16-byte words of a stage row), two row chains
+// each; the G partials of an output go through scr (4096 floats) and are
+// summed in a fixed order into ys[MR*w] behind a barrier.  No division in
+// the loops: the geometry comes precomputed.
+template <int MR>
+__device__ __noinline__ uint32_t mk_gemv_q4(const float* actv, int K, int w, MkGeo geo, unsigned char* ring,
+                                            uint64_t* full, uint64_t* empty, int nstage, uint32_t it, float* scr4k,
+                                            float* ys, int* err, volatile int* abort_flag) {
+    const int tid = threadIdx.x;
+    const int R = geo.R, G = geo.G, nq = w >> 2;
+    const int q = tid & ((1 << geo.lgp) - 1), g = tid >> geo.lgp;
+    const bool valid = g < G && q < nq;
+    if (tid == 0) mk_gemv_t[0] = gtimer();
+    float4 a0[MR], a1[MR];
+#pragma unroll
+    for (int m = 0; m < MR; m++) a0[m] = a1[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r0 = 0; r0 < K; r0 += R) {
+        const int rows = min(R, K - r0);
+        wait_full(full, it, nstage, err, abort_flag);
+        const float4* st = reinterpret_cast<const float4*>(ring + (size_t)rp_stage(it) * mk_sbytes);
+        if (valid) {
+            const float* av = actv + r0;
+            int r = g;
+            for (; r + G < rows; r += 2 * G) {
+                const float4 w0 = st[r * nq + q], w1 = st[(r + G) * nq + q];
+#pragma unroll
+                for (int m = 0; m < MR; m++) {
+                    const float x0 = av[m * K + r], x1 = av[m * K + r + G];
+                    a0[m].x += x0 * w0.x; a0[m].y += x0 * w0.y; a0[m].z += x0 * w0.z; a0[m].w += x0 * w0.w;
+                    a1[m].x += x1 * w1.x; a1[m].y += x1 * w1.y; a1[m].z += x1 * w1.z; a1[m].w += x1 * w1.w;
+                }
+            }
+            if (r < rows) {
+                const float4 w0 = st[r * nq + q];
+#pragma unroll
+                for (int m = 0; m < MR; m++) {
+                    const float x0 = av[m * K + r];
+                    a0[m].x += x0 * w0.x; a0[m].y += x0 * w0.y; a0[m].z += x0 * w0.z; a0[m].w += x0 * w0.w;
+                }
+            }
+        }
+        release_stage(empty, it, nstage);
+        it = rp_next(it, nstage);
+    }
+    if (tid == 0) mk_gemv_t[1] = gtimer();
+    if (valid)
+#pragma unroll
+        for (int m = 0; m < MR; m++)
+            reinterpret_cast<float4*>(scr4k)[((m * G + g) * w >> 2) + q] =
+                make_float4(a0[m].x + a1[m].x, a0[m].y + a1[m].y, a0[m].z + a1[m].z, a0[m].w + a1[m].w);
+    cons_sync();
+#pragma unroll
+    for (int m = 0; m < MR; m++)
+        for (int c = tid; c < w; c += MK_CONS) {
+            const float* rp = scr4k + (m * G) * w + c;
+            float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+            int gg = 0;
+            for (; gg + 3 < G; gg += 4) {
+                t0 += rp[gg * w];
+                t1 += rp[(gg + 1) * w];
+                t2 += rp[(gg + 2) * w];
+                t3 += rp[(gg + 3) * w];
+            }
+            for (; gg < G; gg++) t0 += rp[gg * w];
+            ys[m * w + c] = (t0 + t1) + (t2 + t3);
+        }
+    cons_sync();
+    if (tid == 0) mk_gemv_t[2] = gtimer();
+    return it;
+}
+
+// Wide [K][w] slice, w % 4 == 0, w <= 1024: thread t sums column quad t over
+// the K rows (float4 loads) and adds each output to the fixed-point
+// accumulator out[m * w + c] (one count).  Returns the ring position.
+template <int MR>
+__device__ __noinline__ uint32_t mk_gemv_wide_q4(const float* actv, int K, int w, int R, unsigned char* ring,
+                                                 uint64_t* full, uint64_t* empty, int nstage, uint32_t it,
+                                                 unsigned long long* out, const uint32_t* red_remote, int rank,
+                                                 int blk, uint32_t tag, int* err, volatile int* abort_flag) {
+    const int tid = threadIdx.x;
+    const int nq = w >> 2;
+    float4 acc[MR];
+#pragma unroll
+    for (int m = 0; m < MR; m++) acc[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r0 = 0; r0 < K; r0 += R) {
+        const int rows = min(R, K - r0);
+        wait_full(full, it, nstage, err, abort_flag);
+        const float4* st = reinterpret_cast<const float4*>(ring + (size_t)rp_stage(it) * mk_sbytes);
+        if (tid < nq)
+            for (int r = 0; r < rows; r++) {
+                const float4 v = st[r * nq + tid];
+#pragma unroll
+                for (int m = 0; m < MR; m++) {
+                    const float x = actv[m * K + r0 + r];
+                    acc[m].x += x * v.x; acc[m].y += x * v.y; acc[m].z += x * v.z; acc[m].w += x * v.w;
+                }
+            }
+        release_stage(empty, it, nstage);
+        it = rp_next(it, nstage);
+    }
+    if (tid < nq) {
+        if (out) {
+            // straight to the global accumulators (one count each)
+#pragma unroll
+            for (int m = 0; m < MR; m++) {
+                unsigned long long* o = out + (size_t)m * w + 4 * tid;
+                acc_add(o, acc_term(acc[m].x));
+                acc_add(o + 1, acc_term(acc[m].y));
+                acc_add(o + 2, acc_term(acc[m].z));
+                acc_add(o + 3, acc_term(acc[m].w));
+            }
+        } else {
+            // to the cluster CTA that owns columns 4 tid .. 4 tid + 3 (blocks of blk)
+            const int c = 4 * tid, own = c / blk, oc = c - own * blk;
+#pragma unroll
+            for (int m = 0; m < MR; m++) {
+                const uint32_t dst = red_remote[own] + (uint32_t)((rank * MR + m) * blk + oc) * 8u;
+                dsmem_st_pair(dst, acc[m].x, tag);
+                dsmem_st_pair(dst + 8u, acc[m].y, tag);
+                dsmem_st_pair(dst + 16u, acc[m].z, tag);
+                dsmem_st_pair(dst + 24u, acc[m].w, tag);
+            }
+        }
+    }
+    return it;
+}
+
 // Wide slice (256 < w <= 1024 columns): thread t sums columns t + 256 i over
 // the K rows, and adds each output to the fixed-point accumulator
 // out[m * w + c] (one count).  Returns the ring position after the slice.
@@ -808,7 +1015,7 @@ __device__ __noinline__ uint32_t mk_gemv_wide_acc(const float* actv, int K, int 
     for (int r0 = 0; r0 < K; r0 += R) {
         const int rows = min(R, K - r0);
         wait_full(full, it, nstage, err, abort_flag);
-        const float* st = reinterpret_cast<const float*>(ring + (size_t)(it % nstage) * MK_STAGE);
+        const float* st = reinterpret_cast<const float*>(ring + (size_t)rp_stage(it) * mk_sbytes);
         for (int r = 0; r < rows; r++) {
 #pragma unroll
             for (int i = 0; i < 4; i++) {
@@ -821,7 +1028,7 @@ __device__ __noinline__ uint32_t mk_gemv_wide_acc(const float* actv, int K, int 
             }
         }
         release_stage(empty, it, nstage);
-        it++;
+        it = rp_next(it, nstage);
     }
 #pragma unroll
     for (int m = 0; m < MR; m++)
@@ -862,7 +1069,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     const int D = a.D, F = a.F, L = a.L, H = a.H, hd = a.hd, V = a.V;
     const int KC = MK_STAGE / (hd * 4);  // keys per attention chunk
     unsigned char* ring = mk_smem_raw;
-    uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)a.nstage * MK_STAGE);
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)a.nstage * a.stage_bytes);
     uint64_t* empty = full + a.nstage;
     float* act = reinterpret_cast<float*>(empty + a.nstage);  // [MR][F]
     float* xres = act + MR * F;                                // [MR][D]
@@ -881,15 +1088,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     const MkHcLayout hcl = mk_hc_layout(MR, D, F, hd, a.ctx, a.hc ? a.cs : 1, nW, L);
     float* hcb = reinterpret_cast<float*>(
         (reinterpret_cast<uintptr_t>(wts_m + 2 * MR * H * a.maxc) + 15) & ~(uintptr_t)15);
-    float* qkv_in = hcb + hcl.qkv_in;
-    float* part_in = hcb + hcl.part_in;
+    unsigned long long* qkv_in = reinterpret_cast<unsigned long long*>(hcb + hcl.qkv_in);
+    unsigned long long* part_in = reinterpret_cast<unsigned long long*>(hcb + hcl.part_in);
     float* ctxs = hcb + hcl.ctxs;
     float* att_p = hcb + hcl.att_p;
     float* pvred = hcb + hcl.pvred;
     float* hc_ys = hcb + hcl.ys;
     float* hscr = hcb + hcl.hscr;
-    uint64_t* hc_mbar = reinterpret_cast<uint64_t*>(hcb + hcl.mbar);  // qkv[2], part[2], exit
+    uint64_t* hc_mbar = reinterpret_cast<uint64_t*>(hcb + hcl.mbar);  // [4]: exit handshake
+    unsigned long long* red_in = reinterpret_cast<unsigned long long*>(hcb + hcl.red_in);
     MkLayer* hc_lay = reinterpret_cast<MkLayer*>(hcb + hcl.lay);
+    uint32_t* hc_rb = reinterpret_cast<uint32_t*>(hcb + hcl.mbar + 16);  // [3][8]
     // iscr regions
     uint32_t* seen = reinterpret_cast<uint32_t*>(iscr);  // [8] bits of the slice
     uint32_t* ban = seen + 8;                            // [8]
@@ -904,6 +1113,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     __shared__ double s_ud[MK_MAX_ROWS];  // this step's uniform draw per row
     __shared__ int s_len0[MK_MAX_ROWS], s_dead[MK_MAX_ROWS], s_dummy[MK_MAX_ROWS], s_ubase[MK_MAX_ROWS + 1];
     __shared__ volatile int s_abort;
+    __shared__ MkGeo s_geo[3];  // head-cluster slices: qkv, proj, fc (column quads)
+    __shared__ int s_hci[8];    // log2 cs, log2 hq, log2 hd, j0, J, proj2 stage rows
 
     // float4 accesses to the scratch regions need slice_max % 4 == 0
     if ((a.slice_max & 3) != 0) {
@@ -926,17 +1137,31 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     if (tid == 0) {
         s_abort = 0;
         mk_wait_ns = a.timeout_ns;
+        mk_sbytes = a.stage_bytes;
         for (int i = 0; i < a.nstage; i++) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 8);
         }
-        if (a.hc && cta < a.nhead)
-            for (int i = 0; i < 5; i++) mbar_init(&hc_mbar[i], a.cs);  // one arrival per cluster CTA and round
+        if (a.hc) mbar_init(&hc_mbar[4], a.cs);  // exit handshake: one arrival per cluster CTA
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (a.hc)
+    if (a.hc) {
         for (int i = tid; i < L * (int)(sizeof(MkLayer) / 8); i += MK_THREADS)
             reinterpret_cast<const float**>(hc_lay)[i] = reinterpret_cast<const float* const*>(a.layers)[i];
+        {
+            // the exchange words start untagged in every launch (no word of an
+            // earlier launch can carry a tag of this one)
+            const int nq = a.cs * MR * hcl.q3, np = a.cs * MR * hcl.ps, nr = MR <= 2 ? a.cs * MR * (D / a.cs) : 0;
+            for (int i = tid; i < nq; i += MK_THREADS) qkv_in[i] = 0ull;
+            for (int i = tid; i < np; i += MK_THREADS) part_in[i] = 0ull;
+            for (int i = tid; i < nr; i += MK_THREADS) red_in[i] = 0ull;
+            if (tid < a.cs) {
+                hc_rb[tid] = dsmem_addr(qkv_in, tid);
+                hc_rb[8 + tid] = dsmem_addr(part_in, tid);
+                hc_rb[16 + tid] = dsmem_addr(red_in, tid);
+            }
+        }
+    }
     __syncthreads();
     // the cluster's mbarriers are initialised before any CTA arrives on them
     if (a.hc) cluster_sync_all();
@@ -967,6 +1192,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 if (!mbar_try(&empty[st], par)) {
                     const unsigned long long t0 = gtimer();
                     while (!mbar_try(&empty[st], par)) {
+                        // the producer's warp shares a scheduler with consumer warps 0
+                        // and 4: back off instead of competing with them for issue slots
+                        __nanosleep(a.prod_sleep_ns);
                         if (s_abort || gtimer() - t0 > mk_wait_ns) {
                             if (!s_abort) atomicExch(a.err, 3);
                             s_abort = 1;
@@ -977,8 +1205,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 }
             }
             mbar_expect_tx(&full[st], bytes);
-            if (streamed) bulk_g2s_hint(ring + (size_t)st * MK_STAGE, src, bytes, &full[st], stream_policy);
-            else bulk_g2s(ring + (size_t)st * MK_STAGE, src, bytes, &full[st]);
+            if (streamed) bulk_g2s_hint(ring + (size_t)st * mk_sbytes, src, bytes, &full[st], stream_policy);
+            else bulk_g2s(ring + (size_t)st * mk_sbytes, src, bytes, &full[st]);
             it++;
         };
         auto issue_strip = [&](const float* Wt, int K, int N) {
@@ -999,7 +1227,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
             if (a.hc) {
                 // this CTA's slices of every layer, in the order the consumers use them
                 const int q3 = hcl.q3, wp = D / a.cs;
-                const int j0 = (int)((long long)cta * F / nW), j1 = (int)((long long)(cta + 1) * F / nW);
+                const int j0 = 4 * (int)((long long)cta * (F / 4) / nW), j1 = 4 * (int)((long long)(cta + 1) * (F / 4) / nW);
                 for (int l = 0; l < L && ok; l++) {
                     const MkLayer& ly = hc_lay[l];
                     if (cta < a.nhead) {
@@ -1052,7 +1280,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 issue_strip(ly.w[MK_PROJ2], F, D);
             }
             const int v0 = (int)(((long long)cta * V) / nW), v1 = (int)(((long long)(cta + 1) * V) / nW);
-            const int Rh = max(1, MK_STAGE / (D * 4));
+            const int Rh = max(1, mk_sbytes / (D * 4));
             for (int r0 = v0; r0 < v1 && ok; r0 += Rh)
                 issue(a.tok_emb + (size_t)r0 * D, (uint32_t)(min(Rh, v1 - r0) * D * 4), true);
         }
@@ -1092,6 +1320,24 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         for (int p = tid; p < MR * w; p += MK_CONS) epilogue(p / w, n0 + p % w, uacc[p]);
     };
 
+    if (a.hc && tid == 0) {
+        // the head-cluster geometry, with the launch's only divisions
+        int lcs = 0, lhd = 0;
+        while ((1 << lcs) < a.cs) lcs++;
+        while ((1 << lhd) < hd) lhd++;
+        const int j0 = 4 * (int)((long long)cta * (F / 4) / nW);
+        const int J = 4 * (int)((long long)(cta + 1) * (F / 4) / nW) - j0;
+        s_hci[0] = lcs;
+        s_hci[1] = lhd - lcs;
+        s_hci[2] = lhd;
+        s_hci[3] = j0;
+        s_hci[4] = J;
+        s_hci[5] = J > 0 ? strip_rows(D, J) : 0;
+        s_geo[0] = mk_geo(hcl.q3, D, MR);
+        s_geo[1] = mk_geo(D >> lcs, hd, MR);
+        s_geo[2] = mk_geo(J, D, MR);
+    }
+    cons_sync();
     for (int s = 0; s < a.nsteps; s++) {
         const unsigned int gs = a.gstep0 + s;
         if (tid == 0) {
@@ -1113,10 +1359,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
             // phase needs are loaded before the wait that precedes it.
             const int cs = a.cs, nhead = a.nhead;
             const bool is_head = cta < nhead;
-            const int hh = cta / cs, rk = cta - (cta / cs) * cs;
-            const int hq = hd / cs, q3 = hcl.q3, wp = D / cs, ps = hcl.ps;
-            const int j0 = (int)((long long)cta * F / nW);
-            const int J = (int)((long long)(cta + 1) * F / nW) - j0;
+            const int lcs = s_hci[0], lhq = s_hci[1], lhd = s_hci[2];
+            const int hh = cta >> lcs, rk = cta & (cs - 1);
+            const int hq = 1 << lhq, q3 = hcl.q3, wp = D >> lcs, ps = hcl.ps;
+            // hidden units in groups of 4 (every slice a whole number of float4 columns)
+            const int j0 = s_hci[3], J = s_hci[4];
+            // this thread's q / k / v column of head hh (threads < q3)
+            const int qpart = tid >> lhq, qi = tid & (hq - 1);
+            const int qcol = qpart * D + hh * hd + rk * hq + qi;
+            float* gscr = hstage;  // 4096 floats (hstage + iscr), free while the layers run
             const unsigned int par = gs & 1u;
             // per-thread columns n = tid + 256 k (D <= 1024)
             auto load_cols = [&](const float* b, float (&r)[4]) {
@@ -1127,8 +1378,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
             float bqkv = 0.f;
             if (is_head) {
                 ln1 = ln_prefetch(hc_lay[0].ln1w, hc_lay[0].ln1b, D);
-                const int c = tid % q3, part = c / hq, i = c - part * hq;
-                if (tid < MR * q3) bqkv = __ldg(hc_lay[0].b[MK_QKV] + part * D + hh * hd + rk * hq + i);
+                if (tid < q3) bqkv = __ldg(hc_lay[0].b[MK_QKV] + qcol);
             }
             for (int l = 0; l < L; l++) {
                 const MkLayer& ly = hc_lay[l];
@@ -1137,8 +1387,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 // the cluster mbarriers start at phase 0 in every launch: rounds count
                 // from the launch's first step
                 const unsigned int rnd = (unsigned)s * (unsigned)L + (unsigned)l;
-                const int buf = (int)(rnd & 1u);
-                const uint32_t bpar = (rnd >> 1) & 1u;
+                const int buf = 0;  // one buffer per exchange (see the layout)
                 MK_TRACE_L(0);
                 if (l == 0) {
                     for (int m = 0; m < MR; m++) {
@@ -1155,49 +1404,58 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     mk_layernorm<MR>(xres, act, D, ln1, scr + 384);
                     MK_TRACE_L(1);
                     if (tid == 0) mk_ring_wait = 0;
-                    it = mk_gemv_cols<MR>(act, D, q3, ring, full, empty, a.nstage, it, red, hc_ys, a.err, &s_abort);
+                    it = mk_gemv_q4<MR>(act, D, q3, s_geo[0], ring, full, empty, a.nstage, it, gscr, hc_ys, a.err,
+                                        &s_abort);
                     MK_TRACE_L(2);
+                    if (l == 0) {
+                        MK_TRACE_DUR(22, mk_gemv_t[0]);
+                        MK_TRACE_DUR(23, mk_gemv_t[1]);
+                        MK_TRACE_DUR(47, mk_gemv_t[2]);
+                    }
                     if (l == 0) MK_TRACE_DUR(14, mk_ring_wait);
                     const bool withhold = cta == a.withhold_cta && s == 0 && l == 0;
-                    for (int p = tid; p < MR * q3; p += MK_CONS) {
-                        const int m = p / q3, c = p - m * q3, part = c / hq, i = c - part * hq;
-                        const float v = hc_ys[p] + (p < MK_CONS ? bqkv  // loaded ahead by this thread
-                                                     : __ldg(ly.b[MK_QKV] + part * D + hh * hd + rk * hq + i));
-                        if (part > 0 && !s_dummy[m])
-                            a.kv[(size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
-                                 (part == 2 ? a.v_offset : 0) + ((size_t)hh * a.ctx + pos_of(m, s)) * hd + rk * hq + i] = v;
-                        float* dst = qkv_in + ((buf * cs + rk) * MR + m) * q3 + c;
-                        for (int q = 0; q < cs; q++) dsmem_st(dsmem_addr(dst, q), v);
-                    }
-                    cons_sync();
+                    const uint32_t xtag = rnd + 1u;  // exchange words of this round
+                    if (tid < q3)  // q3 <= 256
+                        for (int m = 0; m < MR; m++) {
+                            const float v = hc_ys[m * q3 + tid] + bqkv;
+                            if (qpart > 0 && !s_dummy[m])
+                                a.kv[(size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
+                                     (qpart == 2 ? a.v_offset : 0) + ((size_t)hh * a.ctx + pos_of(m, s)) * hd + rk * hq +
+                                     qi] = v;
+                            const uint32_t off = (uint32_t)(((buf * cs + rk) * MR + m) * q3 + tid) * 8u;
+                            if (!withhold)
+                                for (int q = 0; q < cs; q++) dsmem_st_pair(hc_rb[q] + off, v, xtag);
+                        }
                     MK_TRACE_L(19);
-                    if (tid == 0 && !withhold)
-                        for (int q = 0; q < cs; q++) mbar_arrive_cluster(dsmem_addr(&hc_mbar[buf], q));
-                    // keys of row 0 older than the current one, loaded while the
-                    // cluster's q/k/v parts arrive (thread t: key k0 + t)
-                    float4 kreg[16];
-                    {
-                        const int pos = pos_of(0, s), T = pos + 1;
-                        const int j = (int)((long long)rk * T / cs) + tid;
-                        const int k1 = (int)((long long)(rk + 1) * T / cs);
-                        const float4* kr = reinterpret_cast<const float4*>(
-                            a.kv + (size_t)s_slot[0] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
-                            ((size_t)hh * a.ctx + j) * hd);
-#pragma unroll
-                        for (int e = 0; e < 16; e++)
-                            kreg[e] = (j < k1 && j < pos && e < hd / 4) ? __ldcg(kr + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    // the cached K and V rows of this CTA's keys, pulled into L1 while
+                    // the cluster's q/k/v parts arrive (4 lines of 128 bytes per key
+                    // at head_dim 64; they are read below with L1-cached loads)
+                    for (int m = 0; m < MR; m++) {
+                        const int pos = pos_of(m, s), T = pos + 1;
+                        const int k0 = (rk * T) >> lcs;
+                        const int kend = min(((rk + 1) * T) >> lcs, pos);
+                        const int lpr = hd >> 5;  // 128-byte lines per row
+                        const char* kb = reinterpret_cast<const char*>(
+                            a.kv + (size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
+                            (size_t)hh * a.ctx * hd);
+                        for (int i = tid; i < 2 * lpr * (kend - k0); i += MK_CONS) {
+                            const int key = k0 + (i >> (lhd - 4)), part = i & (2 * lpr - 1);
+                            const char* ln = kb + (part >= lpr ? (size_t)a.v_offset * 4 : 0) +
+                                             ((size_t)key * hd) * 4 + (size_t)(part % lpr) * 128;
+                            asm volatile("prefetch.global.L1 [%0];" ::"l"(ln));
+                        }
                     }
-                    wait_cluster_bar(&hc_mbar[buf], bpar, a.err, &s_abort);
+                    wait_tags_smem(qkv_in + buf * cs * MR * q3, cs * MR * q3, xtag, a.err, &s_abort);
                     MK_TRACE_L(3);
                     if (cons_sync_or(s_abort)) return;
                     // ---- attention of head hh over this CTA's share of the keys -----
                     for (int m = 0; m < MR; m++) {
                         const int pos = pos_of(m, s), T = pos + 1;
-                        const int k0 = (int)((long long)rk * T / cs), k1 = (int)((long long)(rk + 1) * T / cs);
+                        const int k0 = (rk * T) >> lcs, k1 = ((rk + 1) * T) >> lcs;
                         const int nk = k1 - k0;
-                        const float* qin = qkv_in + (buf * cs * MR + m) * q3;  // rank q at + q * MR * q3
+                        const unsigned long long* qin = qkv_in + (buf * cs * MR + m) * q3;  // rank q at + q * MR * q3
                         auto qkv_at = [&](int part, int d) {  // element d of q / k / v of row m
-                            return qin[(d / hq) * MR * q3 + part * hq + (d % hq)];
+                            return __uint_as_float((uint32_t)qin[(d >> lhq) * MR * q3 + part * hq + (d & (hq - 1))]);
                         };
                         if (tid < hd) hscr[tid] = qkv_at(0, tid);
                         cons_sync();
@@ -1210,18 +1468,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                             float d = 0.f;
                             if (j < pos) {
                                 const float4* q4 = reinterpret_cast<const float4*>(hscr);
-                                if (m == 0 && t < MK_CONS) {
+                                const float4* kr = reinterpret_cast<const float4*>(kbase + (size_t)j * hd);
+                                for (int e0 = 0; e0 < hd / 4; e0 += 4) {
+                                    float4 kv4[4];
 #pragma unroll
-                                    for (int e = 0; e < 16; e++)
-                                        if (e < hd / 4) {
-                                            const float4 kv4 = kreg[e], qv = q4[e];
-                                            d += qv.x * kv4.x + qv.y * kv4.y + qv.z * kv4.z + qv.w * kv4.w;
-                                        }
-                                } else {
-                                    const float4* kr = reinterpret_cast<const float4*>(kbase + (size_t)j * hd);
-                                    for (int e = 0; e < hd / 4; e++) {
-                                        const float4 kv4 = __ldcg(kr + e), qv = q4[e];
-                                        d += qv.x * kv4.x + qv.y * kv4.y + qv.z * kv4.z + qv.w * kv4.w;
+                                    for (int e = 0; e < 4; e++) kv4[e] = __ldca(kr + e0 + e);
+#pragma unroll
+                                    for (int e = 0; e < 4; e++) {
+                                        const float4 qv = q4[e0 + e];
+                                        d += qv.x * kv4[e].x + qv.y * kv4[e].y + qv.z * kv4[e].z + qv.w * kv4[e].w;
                                     }
                                 }
                             } else {
@@ -1233,14 +1488,14 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                         }
                         // this thread's V values (dimension d, keys g, g + ng, ...),
                         // loaded before the softmax reductions
-                        const int ng = MK_CONS / hd, d = tid % hd, g = tid / hd;
+                        const int ng = MK_CONS >> lhd, d = tid & (hd - 1), g = tid >> lhd;
                         float vv[8];
-                        const int nv = (nk - g + ng - 1) / ng;
+                        const int nv = (nk - g + ng - 1) >> (8 - lhd);
 #pragma unroll
                         for (int i = 0; i < 8; i++) {
                             const int j = k0 + g + i * ng;
                             vv[i] = 0.f;
-                            if (i < nv) vv[i] = j < pos ? __ldcg(vbase + (size_t)j * hd + d) : qkv_at(2, d);
+                            if (i < nv) vv[i] = j < pos ? __ldca(vbase + (size_t)j * hd + d) : qkv_at(2, d);
                         }
                         mloc = warp_max(mloc);
                         if (lane == 0) scr[256 + warp] = mloc;
@@ -1269,37 +1524,59 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                         pvred[g * hd + d] = av0 + av1;
                         cons_sync();
                         if (m == 0) MK_TRACE_L(21);
-                        float* pdst = part_in + ((buf * cs + rk) * MR + m) * ps;
+                        const uint32_t poff = (uint32_t)(((buf * cs + rk) * MR + m) * ps) * 8u;
                         if (tid < hd) {
                             float A = 0.f;
                             for (int gg = 0; gg < ng; gg++) A += pvred[gg * hd + tid];
-                            for (int q = 0; q < cs; q++) dsmem_st(dsmem_addr(pdst + 2 + tid, q), A);
+                            for (int q = 0; q < cs; q++) dsmem_st_pair(hc_rb[8 + q] + poff + 8u * (2 + tid), A, xtag);
                         } else if (tid == hd) {
                             for (int q = 0; q < cs; q++) {
-                                dsmem_st(dsmem_addr(pdst, q), nk > 0 ? M : -INFINITY);
-                                dsmem_st(dsmem_addr(pdst + 1, q), nk > 0 ? S : 0.f);
+                                dsmem_st_pair(hc_rb[8 + q] + poff, nk > 0 ? M : -INFINITY, xtag);
+                                dsmem_st_pair(hc_rb[8 + q] + poff + 8u, nk > 0 ? S : 0.f, xtag);
                             }
                         }
                         cons_sync();
                     }
                     MK_TRACE_L(4);
-                    if (tid == 0)
-                        for (int q = 0; q < cs; q++) mbar_arrive_cluster(dsmem_addr(&hc_mbar[2 + buf], q));
-                    wait_cluster_bar(&hc_mbar[2 + buf], bpar, a.err, &s_abort);
+                    {
+                        // every pushed word of every rank and row (the padding words
+                        // past hd + 2 are never written)
+                        const unsigned long long* pb = part_in + buf * cs * MR * ps;
+                        for (int i = tid; i < cs * MR * ps; i += MK_CONS) {
+                            if (i % ps >= hd + 2) continue;
+                            const volatile unsigned long long* pw = pb + i;
+                            if ((uint32_t)(*pw >> 32) == xtag) continue;
+                            const unsigned long long t0 = gtimer();
+                            for (int k = 1; (uint32_t)(*pw >> 32) != xtag; k++) {
+                                if (s_abort) break;
+                                if ((k & 63) == 0 && ld_relaxed_i32(a.err) != 0) {
+                                    s_abort = 1;
+                                    break;
+                                }
+                                if (gtimer() - t0 > mk_wait_ns) {
+                                    atomicExch(a.err, 5);
+                                    s_abort = 1;
+                                    break;
+                                }
+                            }
+                        }
+                    }
                     MK_TRACE_L(5);
                     if (cons_sync_or(s_abort)) return;
                     // ---- combine the cluster's partials -> ctx of head hh -------------
                     for (int p = tid; p < MR * hd; p += MK_CONS) {
-                        const int m = p / hd, dd = p - m * hd;
-                        const float* pr = part_in + (buf * cs * MR + m) * ps;
+                        const int m = p >> lhd, dd = p & (hd - 1);
+                        const unsigned long long* pr = part_in + (buf * cs * MR + m) * ps;
+                        auto val = [](unsigned long long w) { return __uint_as_float((uint32_t)w); };
                         float Ms = -INFINITY;
-                        for (int q = 0; q < cs; q++) Ms = fmaxf(Ms, pr[q * MR * ps]);
+                        for (int q = 0; q < cs; q++) Ms = fmaxf(Ms, val(pr[q * MR * ps]));
                         float ls = 0.f, A = 0.f;
                         for (int q = 0; q < cs; q++) {
-                            const float* pq = pr + q * MR * ps;
-                            const float w = pq[0] == -INFINITY ? 0.f : __expf(pq[0] - Ms);
-                            ls += pq[1] * w;
-                            A += pq[2 + dd] * w;
+                            const unsigned long long* pq = pr + q * MR * ps;
+                            const float mq = val(pq[0]);
+                            const float w = mq == -INFINITY ? 0.f : __expf(mq - Ms);
+                            ls += val(pq[1]) * w;
+                            A += val(pq[2 + dd]) * w;
                         }
                         ctxs[p] = A / ls;
                     }
@@ -1307,18 +1584,18 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     MK_TRACE_L(18);
                     // ---- this CTA's columns of ctx_hh * Wproj[hh rows] -> x2 partials --
                     if (tid == 0) mk_ring_wait = 0;
-                    it = mk_gemv_cols<MR>(ctxs, hd, wp, ring, full, empty, a.nstage, it, red, hc_ys, a.err, &s_abort);
+                    it = mk_gemv_q4<MR>(ctxs, hd, wp, s_geo[1], ring, full, empty, a.nstage, it, gscr, hc_ys, a.err,
+                                        &s_abort);
                     MK_TRACE_L(6);
                     if (l == 0) MK_TRACE_DUR(15, mk_ring_wait);
-                    for (int p = tid; p < MR * wp; p += MK_CONS) {
-                        const int m = p / wp, c = p - m * wp;
-                        acc_add(accx2 + (size_t)m * D + rk * wp + c, acc_term(hc_ys[p]));
-                    }
+                    for (int m = 0; m < MR; m++)
+                        for (int c = tid; c < wp; c += MK_CONS)
+                            acc_add(accx2 + (size_t)m * D + rk * wp + c, acc_term(hc_ys[m * wp + c]));
                     MK_TRACE_L(7);
                 }
                 // ---- x2 = x + attention projection; LN2 -> fc -> GELU -> proj2 ------
                 const LnRegs ln2 = ln_prefetch(ly.ln2w, ly.ln2b, D);
-                const float bfc = tid < MR * J ? __ldg(ly.b[MK_FC] + j0 + tid % J) : 0.f;
+                const float bfc = tid < J ? __ldg(ly.b[MK_FC] + j0 + tid) : 0.f;
                 acc_gather(accx2, act, MR * D, (uint32_t)(nhead / cs), a.err, &s_abort);
                 cons_sync();
 #pragma unroll
@@ -1336,28 +1613,51 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 if (J > 0) {
                     float* hb = act + MR * D;  // [MR][J]
                     if (tid == 0) mk_ring_wait = 0;
-                    it = mk_gemv_cols<MR>(act, D, J, ring, full, empty, a.nstage, it, red, hc_ys, a.err, &s_abort);
+                    it = mk_gemv_q4<MR>(act, D, J, s_geo[2], ring, full, empty, a.nstage, it, gscr, hc_ys, a.err,
+                                        &s_abort);
                     MK_TRACE_L(12);
                     if (l == 0) MK_TRACE_DUR(16, mk_ring_wait);
-                    for (int p = tid; p < MR * J; p += MK_CONS)
-                        hb[p] = gelu_tanh(hc_ys[p] + (p < MK_CONS ? bfc : __ldg(ly.b[MK_FC] + j0 + p % J)));
+                    if (tid < J)  // J <= 256
+                        for (int m = 0; m < MR; m++) hb[m * J + tid] = gelu_tanh(hc_ys[m * J + tid] + bfc);
                     cons_sync();
                     MK_TRACE_L(13);
                     if (tid == 0) mk_ring_wait = 0;
-                    it = mk_gemv_wide_acc<MR>(hb, J, D, ring, full, empty, a.nstage, it, accx, a.err, &s_abort);
+                    it = mk_gemv_wide_q4<MR>(hb, J, D, s_hci[5], ring, full, empty, a.nstage, it,
+                                             MR <= 2 ? nullptr : accx, hc_rb + 16, rk, wp, (uint32_t)rnd + 1u, a.err,
+                                             &s_abort);
                     if (l == 0) MK_TRACE_DUR(17, mk_ring_wait);
-                } else {
+                } else if (MR > 2) {
                     for (int p = tid; p < MR * D; p += MK_CONS) acc_add(accx + p, acc_term(0.f));
+                } else {
+                    // no hidden units here: zeros for every column block of the cluster
+                    for (int m = 0; m < MR; m++)
+                        for (int c = tid; c < D; c += MK_CONS) {
+                            const int own = c / wp;
+                            dsmem_st_pair(hc_rb[16 + own] + (uint32_t)((rk * MR + m) * wp + (c - own * wp)) * 8u, 0.f,
+                                          (uint32_t)rnd + 1u);
+                        }
+                }
+                if (MR <= 2) {
+                    // this CTA's column block: the cluster's partials summed in rank order,
+                    // one fixed-point term per cluster and column
+                    wait_tags_smem(red_in, cs * MR * wp, (uint32_t)rnd + 1u, a.err, &s_abort);
+                    if (cons_sync_or(s_abort)) return;  // every word verified before any is summed
+                    for (int m = 0; m < MR; m++)
+                        for (int c = tid; c < wp; c += MK_CONS) {
+                            float sum = 0.f;
+                            for (int q = 0; q < cs; q++)
+                                sum += __uint_as_float((uint32_t)red_in[(q * MR + m) * wp + c]);
+                            acc_add(accx + (size_t)m * D + rk * wp + c, acc_term(sum));
+                        }
                 }
                 MK_TRACE_L(9);
                 // next layer's LN1 parameters and qkv bias, loaded during the wait
                 if (is_head && l + 1 < L) {
                     ln1 = ln_prefetch(hc_lay[l + 1].ln1w, hc_lay[l + 1].ln1b, D);
-                    const int c = tid % q3, part = c / hq, i = c - part * hq;
-                    if (tid < MR * q3) bqkv = __ldg(hc_lay[l + 1].b[MK_QKV] + part * D + hh * hd + rk * hq + i);
+                    if (tid < q3) bqkv = __ldg(hc_lay[l + 1].b[MK_QKV] + qcol);
                 }
                 // ---- x of the next layer (every CTA) --------------------------------
-                acc_gather(accx, act, MR * D, (uint32_t)nW, a.err, &s_abort);
+                acc_gather(accx, act, MR * D, (uint32_t)(MR <= 2 ? nW / cs : nW), a.err, &s_abort);
                 cons_sync();
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
@@ -1437,7 +1737,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                         if (tid < hd) qs[tid] = wait_pair(a.xq + m * D + h * hd + tid, tg, a.err, &s_abort);
                         cons_sync();
                         wait_full(full, it, a.nstage, a.err, &s_abort);
-                        const float* Kt = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
+                        const float* Kt = reinterpret_cast<const float*>(ring + (size_t)rp_stage(it) * mk_sbytes);
                         const int j = warp * kpw + kw;  // this lane's key
                         float d = 0.f;
                         if (j < nk) {
@@ -1452,12 +1752,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                         for (int o = 1; o < lpk; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
                         const float sc = j < nk ? d * scale : -INFINITY;
                         release_stage(empty, it, a.nstage);
-                        it++;
+                        it = rp_next(it, a.nstage);
                         const float mw = warp_max(sc);
                         const float p = j < nk ? __expf(sc - mw) : 0.f;
                         const float lw = warp_sum(part == 0 ? p : 0.f);
                         wait_full(full, it, a.nstage, a.err, &s_abort);
-                        const float* Vt = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
+                        const float* Vt = reinterpret_cast<const float*>(ring + (size_t)rp_stage(it) * mk_sbytes);
                         float a0 = 0.f, a1 = 0.f;
                         for (int kk = 0; kk < kpw; kk++) {
                             const float pk = __shfl_sync(0xffffffffu, p, kk * lpk);
@@ -1468,7 +1768,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                             }
                         }
                         release_stage(empty, it, a.nstage);
-                        it++;
+                        it = rp_next(it, a.nstage);
                         wacc[warp * hd + lane] = a0;
                         if (hd > 32) wacc[warp * hd + lane + 32] = a1;
                         if (lane == 0) {
@@ -1733,7 +2033,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         const int v0 = (int)(((long long)cta * V) / nW), v1 = (int)(((long long)(cta + 1) * V) / nW);
         const int nsl = v1 - v0;
         {
-            const int Rh = max(1, MK_STAGE / (D * 4));
+            const int Rh = max(1, mk_sbytes / (D * 4));
             unsigned long long head_wait = 0;  // thread 0's time inside the ring waits (traced runs)
             for (int r0 = v0; r0 < v1; r0 += Rh) {
                 const int rows = min(Rh, v1 - r0);
@@ -1746,7 +2046,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 }
                 if (r0 == v0) MK_TRACE(29);
                 if (r0 - v0 == ((nsl / Rh) / 2) * Rh) MK_TRACE(45);
-                const float* E = reinterpret_cast<const float*>(ring + (size_t)(it % a.nstage) * MK_STAGE);
+                const float* E = reinterpret_cast<const float*>(ring + (size_t)rp_stage(it) * mk_sbytes);
                 // slice row idx = r0 - v0 + r goes to warp idx % 8: a warp with no
                 // row here moves on to the next stage while the others finish
                 // (every warp still waits for each stage before releasing it)
@@ -1782,7 +2082,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     }
                 }
                 release_stage(empty, it, a.nstage);
-                it++;
+                it = rp_next(it, a.nstage);
             }
             if (a.trace && tid == 0 && s < a.trace_steps)
                 a.trace[((size_t)cta * a.trace_steps + s) * MK_TRACE_POINTS + 46] = head_wait;
@@ -2282,8 +2582,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     }
     };
     consumers();
-    if (a.hc && cta < a.nhead) {
-        // no CTA of a head cluster leaves while a cluster CTA may still write
+    if (a.hc) {
+        // no CTA of a cluster leaves while a cluster CTA may still write
         // into its shared memory: each arrives on every CTA's exit barrier after
         // its last push, then waits (bounded) for all of them
         cons_sync();

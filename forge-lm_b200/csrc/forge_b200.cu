@@ -272,14 +272,14 @@ static int mk_slice_max(int V, int nW) { return (ceil_div(V, nW) + 3) & ~3; }
 
 // Dynamic shared memory of k_decode_mega<MR> with `nstage` ring stages
 // (cs > 0: the head-cluster layout, clusters of cs CTAs).
-static size_t mk_smem(const fb2_model& m, int MR, int nW, int nstage, int cs = 0) {
-    return (size_t)nstage * MK_STAGE +
+static size_t mk_smem(const fb2_model& m, int MR, int nW, int nstage, int cs = 0, int sb = MK_STAGE) {
+    return (size_t)nstage * sb +
            mk_aux_bytes(MR, m.D, m.F, m.H, m.ctx, mk_slice_max(m.V, nW), mk_maxc(m.ctx, m.hd), nstage) +
            (cs > 0 ? mk_hc_bytes(MR, m.D, m.F, m.hd, m.ctx, cs, nW, m.L) : 0) + 256;
 }
 
 // Ring stages that fit next to the kernel's other shared memory (0: does not fit).
-static int mk_nstage(const fb2_model& m, int MR, int nW, int device, int cs = 0) {
+static int mk_nstage(const fb2_model& m, int MR, int nW, int device, int cs = 0, int sb = MK_STAGE) {
     int optin = 0;
     CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
     cudaFuncAttributes fa;
@@ -290,7 +290,7 @@ static int mk_nstage(const fb2_model& m, int MR, int nW, int device, int cs = 0)
     CK(cudaFuncGetAttributes(&fa, f));
     const long long avail = (long long)optin - (long long)fa.sharedSizeBytes;
     int ns = 16;
-    while (ns >= 4 && (long long)mk_smem(m, MR, nW, ns, cs) > avail) ns--;
+    while (ns >= 4 && (long long)mk_smem(m, MR, nW, ns, cs, sb) > avail) ns--;
     return ns >= 4 ? ns : 0;
 }
 
@@ -419,7 +419,7 @@ static void tc_setup(const fb2_model& m, DeviceModel& dm) {
 // attention CTAs; every slice no wider than the column kernels take.
 static bool mk_hc_plan(const fb2_model& m, DeviceModel& dm) {
     const char* env = getenv("FORGE_B200_MK");
-    if (!(env && std::string(env) == "hc")) return false;  // opt-in while it is tuned
+    if (env && std::string(env) == "strips") return false;
     const char* ecs = getenv("FORGE_B200_MK_CS");
     const int want = ecs ? atoi(ecs) : 0;
     // clusters of 8 when 8 CTAs per head fit the resident grid, else of 4
@@ -492,7 +492,7 @@ static void mk_setup(const fb2_model& m, DeviceModel& dm, const float* const* pa
                     }
                 } else if (ph == MK_FC) {
                     for (size_t j = 0; j < nmlp; j++) {
-                        const size_t j0 = j * F / nmlp, j1 = (j + 1) * F / nmlp, w = j1 - j0;
+                        const size_t j0 = 4 * (j * (F / 4) / nmlp), j1 = 4 * ((j + 1) * (F / 4) / nmlp), w = j1 - j0;
                         for (size_t k = 0; k < K; k++) std::memcpy(&tmp[K * j0 + k * w], W + k * N + j0, w * sizeof(float));
                     }
                 } else {
@@ -1071,7 +1071,15 @@ static void run_mega(DeviceSession& s, int n, int nsteps, const SampleParams& P,
     const int MR = n <= 1 ? 1 : n <= 2 ? 2 : n <= 4 ? 4 : 8;
     const int nW = dm.mk_nW;
     const int hc_cs = dm.mk_hc ? dm.mk_cs : 0;
-    const int nstage = mk_nstage(m, MR, nW, s.device, hc_cs);
+    // head-cluster path: 32 KB stages (fewer per-stage waits) when at least
+    // five fit next to the rest, else 16 KB
+    int sb = MK_STAGE;
+    int nstage = 0;
+    if (dm.mk_hc) {
+        nstage = mk_nstage(m, MR, nW, s.device, hc_cs, MK_STAGE_HC);
+        if (nstage >= 5) sb = MK_STAGE_HC;
+    }
+    if (sb == MK_STAGE) nstage = mk_nstage(m, MR, nW, s.device, hc_cs, MK_STAGE);
     if (nstage == 0) fail(FB2_UNSUPPORTED, "persistent decode kernel does not fit shared memory");
     MkArgs a{};
     a.V = m.V; a.ctx = m.ctx; a.D = m.D; a.L = m.L; a.H = m.H; a.hd = m.hd; a.F = m.F;
@@ -1101,11 +1109,16 @@ static void run_mega(DeviceSession& s, int n, int nsteps, const SampleParams& P,
         a.withhold_cta = s.test_withhold_cta;
         s.test_withhold_cta = -1;
     }
+    {
+        const char* ps = getenv("FORGE_B200_MK_PSLEEP");
+        a.prod_sleep_ns = ps ? (unsigned)atoi(ps) : 200u;
+    }
+    a.stage_bytes = sb;
     a.hc = dm.mk_hc ? 1 : 0;
     a.cs = dm.mk_hc ? dm.mk_cs : 1;
     a.nhead = dm.mk_hc ? dm.mk_nhead : 0;
     a.acc = s.mk_acc;
-    const size_t smem = mk_smem(m, MR, nW, nstage, hc_cs);
+    const size_t smem = mk_smem(m, MR, nW, nstage, hc_cs, sb);
     void* args[] = {&a};
     const void* f = MR == 1 ? (const void*)k_decode_mega<1>
                   : MR == 2 ? (const void*)k_decode_mega<2>
@@ -2721,7 +2734,12 @@ int32_t fb2_test_mk_geometry(fb2_session* S, int32_t* n_ctas, int32_t* cluster, 
         *n_ctas = s.mk_use ? dm.mk_nW : 0;
         *cluster = dm.mk_hc ? dm.mk_cs : 0;
         *attn_ctas = dm.mk_hc ? dm.mk_nhead : 0;
-        *stages = s.mk_use ? mk_nstage(*s.model, 1, dm.mk_nW, s.device, dm.mk_hc ? dm.mk_cs : 0) : 0;
+        int ns = s.mk_use ? mk_nstage(*s.model, 1, dm.mk_nW, s.device, dm.mk_hc ? dm.mk_cs : 0) : 0;
+        if (s.mk_use && dm.mk_hc) {
+            const int n32 = mk_nstage(*s.model, 1, dm.mk_nW, s.device, dm.mk_cs, MK_STAGE_HC);
+            if (n32 >= 5) ns = n32;  // 32 KB stages
+        }
+        *stages = ns;
     });
 }
 
