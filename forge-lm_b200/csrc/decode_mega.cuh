@@ -60,6 +60,12 @@ struct MkLayer {
     const float* w[4];  // re-laid column strips
     const float* b[4];
     const float *ln1w, *ln1b, *ln2w, *ln2b;
+    // head-cluster path: LayerNorm folded into the next projection.  The
+    // re-laid qkv / fc weights are g_k W[k][c]; fold[0] / fold[1] hold per
+    // qkv / fc column c the pair (S_c = sum_k g_k W[k][c],
+    // B_c = sum_k beta_k W[k][c] + bias_c), so that
+    // LN(x) W + bias = rstd (x (gW) - mu S) + B.
+    const float* fold[2];
 };
 
 struct MkArgs {
@@ -614,6 +620,42 @@ FB2_DEV float cons_sum_slot(float v, float* slot) {
     for (int i = 0; i < 8; i++) t += slot[i];
     return t;
 }
+// Per-warp partial moments of MR rows of x [MR][D] (sum and sum of squares)
+// into slots[m * 16 + warp] and slots[m * 16 + 8 + warp]; no barrier (a
+// later one orders them before mk_row_stats reads them).
+template <int MR>
+FB2_DEV void mk_row_moments(const float* x, int D, float* slots) {
+#pragma unroll
+    for (int m = 0; m < MR; m++) {
+        float s1 = 0.f, s2 = 0.f;
+        for (int i = threadIdx.x; i < D; i += MK_CONS) {
+            const float v = x[m * D + i];
+            s1 += v;
+            s2 += v * v;
+        }
+        s1 = warp_sum(s1);
+        s2 = warp_sum(s2);
+        if ((threadIdx.x & 31) == 0) {
+            slots[m * 16 + (threadIdx.x >> 5)] = s1;
+            slots[m * 16 + 8 + (threadIdx.x >> 5)] = s2;
+        }
+    }
+}
+// Mean and 1/sqrt(biased variance + eps) of row m from the partial moments
+// (LayerNorm statistics, CpuBackend.cs:377-398; variance as E[x^2] - mean^2
+// in double).
+FB2_DEV void mk_row_stats(const float* slots, int m, int D, float& mu, float& rstd) {
+    double s1 = 0.0, s2 = 0.0;
+#pragma unroll
+    for (int w = 0; w < 8; w++) {
+        s1 += slots[m * 16 + w];
+        s2 += slots[m * 16 + 8 + w];
+    }
+    const double mean = s1 / D, var = s2 / D - mean * mean;
+    mu = (float)mean;
+    rstd = 1.0f / sqrtf((float)(var > 0.0 ? var : 0.0) + kLnEps);
+}
+
 // Two-pass LayerNorm of MR rows of length D <= 2048 from src into dst
 // (shared), CpuBackend.cs:377-398.  `slots` = 16*MR floats of scratch that
 // stay untouched until the next barrier-separated phase.
@@ -1374,11 +1416,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
 #pragma unroll
                 for (int k = 0; k < 4; k++) r[k] = tid + k * MK_CONS < D ? __ldg(b + tid + k * MK_CONS) : 0.f;
             };
-            LnRegs ln1{};
-            float bqkv = 0.f;
-            if (is_head) {
-                ln1 = ln_prefetch(hc_lay[0].ln1w, hc_lay[0].ln1b, D);
-                if (tid < q3) bqkv = __ldg(hc_lay[0].b[MK_QKV] + qcol);
+            float fqS = 0.f, fqB = 0.f;  // this thread's qkv column: folded LN1 sum and bias
+            if (is_head && tid < q3) {
+                fqS = __ldg(hc_lay[0].fold[0] + 2 * qcol);
+                fqB = __ldg(hc_lay[0].fold[0] + 2 * qcol + 1);
             }
             for (int l = 0; l < L; l++) {
                 const MkLayer& ly = hc_lay[l];
@@ -1400,11 +1441,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 float bproj[4];
                 load_cols(ly.b[MK_PROJ], bproj);
                 if (is_head) {
-                    // ---- LN1 -> this CTA's q, k, v columns of head hh --------------
-                    mk_layernorm<MR>(xres, act, D, ln1, scr + 384);
+                    // ---- LN1 folded into this CTA's q, k, v columns of head hh -------
+                    mk_row_moments<MR>(xres, D, scr + 384);
                     MK_TRACE_L(1);
                     if (tid == 0) mk_ring_wait = 0;
-                    it = mk_gemv_q4<MR>(act, D, q3, s_geo[0], ring, full, empty, a.nstage, it, gscr, hc_ys, a.err,
+                    it = mk_gemv_q4<MR>(xres, D, q3, s_geo[0], ring, full, empty, a.nstage, it, gscr, hc_ys, a.err,
                                         &s_abort);
                     MK_TRACE_L(2);
                     if (l == 0) {
@@ -1417,7 +1458,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     const uint32_t xtag = rnd + 1u;  // exchange words of this round
                     if (tid < q3)  // q3 <= 256
                         for (int m = 0; m < MR; m++) {
-                            const float v = hc_ys[m * q3 + tid] + bqkv;
+                            float mu, rstd;
+                            mk_row_stats(scr + 384, m, D, mu, rstd);
+                            const float v = rstd * (hc_ys[m * q3 + tid] - mu * fqS) + fqB;
                             if (qpart > 0 && !s_dummy[m])
                                 a.kv[(size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
                                      (qpart == 2 ? a.v_offset : 0) + ((size_t)hh * a.ctx + pos_of(m, s)) * hd + rk * hq +
@@ -1594,8 +1637,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     MK_TRACE_L(7);
                 }
                 // ---- x2 = x + attention projection; LN2 -> fc -> GELU -> proj2 ------
-                const LnRegs ln2 = ln_prefetch(ly.ln2w, ly.ln2b, D);
-                const float bfc = tid < J ? __ldg(ly.b[MK_FC] + j0 + tid) : 0.f;
+                const float ffS = tid < J ? __ldg(ly.fold[1] + 2 * (j0 + tid)) : 0.f;  // folded LN2 of fc column
+                const float ffB = tid < J ? __ldg(ly.fold[1] + 2 * (j0 + tid) + 1) : 0.f;
                 acc_gather(accx2, act, MR * D, (uint32_t)(nhead / cs), a.err, &s_abort);
                 cons_sync();
 #pragma unroll
@@ -1608,17 +1651,21 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 if (cons_sync_or(s_abort)) return;
                 float bproj2[4];
                 load_cols(ly.b[MK_PROJ2], bproj2);
-                mk_layernorm<MR>(x2res, act, D, ln2, scr + 384);
+                mk_row_moments<MR>(x2res, D, scr + 384);  // LN2 statistics; LN2 itself is folded into fc
                 MK_TRACE_L(11);
                 if (J > 0) {
                     float* hb = act + MR * D;  // [MR][J]
                     if (tid == 0) mk_ring_wait = 0;
-                    it = mk_gemv_q4<MR>(act, D, J, s_geo[2], ring, full, empty, a.nstage, it, gscr, hc_ys, a.err,
+                    it = mk_gemv_q4<MR>(x2res, D, J, s_geo[2], ring, full, empty, a.nstage, it, gscr, hc_ys, a.err,
                                         &s_abort);
                     MK_TRACE_L(12);
                     if (l == 0) MK_TRACE_DUR(16, mk_ring_wait);
                     if (tid < J)  // J <= 256
-                        for (int m = 0; m < MR; m++) hb[m * J + tid] = gelu_tanh(hc_ys[m * J + tid] + bfc);
+                        for (int m = 0; m < MR; m++) {
+                            float mu, rstd;
+                            mk_row_stats(scr + 384, m, D, mu, rstd);
+                            hb[m * J + tid] = gelu_tanh(rstd * (hc_ys[m * J + tid] - mu * ffS) + ffB);
+                        }
                     cons_sync();
                     MK_TRACE_L(13);
                     if (tid == 0) mk_ring_wait = 0;
@@ -1652,9 +1699,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 }
                 MK_TRACE_L(9);
                 // next layer's LN1 parameters and qkv bias, loaded during the wait
-                if (is_head && l + 1 < L) {
-                    ln1 = ln_prefetch(hc_lay[l + 1].ln1w, hc_lay[l + 1].ln1b, D);
-                    if (tid < q3) bqkv = __ldg(hc_lay[l + 1].b[MK_QKV] + qcol);
+                if (is_head && l + 1 < L && tid < q3) {
+                    fqS = __ldg(hc_lay[l + 1].fold[0] + 2 * qcol);
+                    fqB = __ldg(hc_lay[l + 1].fold[0] + 2 * qcol + 1);
                 }
                 // ---- x of the next layer (every CTA) --------------------------------
                 acc_gather(accx, act, MR * D, (uint32_t)(MR <= 2 ? nW / cs : nW), a.err, &s_abort);

@@ -167,6 +167,7 @@ struct DeviceModel {
     bool mk_hc = false;
     int mk_cs = 1, mk_nhead = 0;
     float* relaid = nullptr;
+    float* mk_fold = nullptr;  // head-cluster layout: folded-LayerNorm (S, B) per qkv / fc column
     MkLayer* d_mk_layers = nullptr;
     // tensor-core GEMM: TF32 hi/lo halves of the four projections per layer
     // (qkv, proj, fc, mlp proj) and their TMA descriptors
@@ -457,6 +458,7 @@ static void mk_setup(const fb2_model& m, DeviceModel& dm, const float* const* pa
     const size_t D = m.D, F = m.F;
     const size_t per_layer = 3 * D * D + D * D + D * F + F * D;
     dm.relaid = dalloc<float>(per_layer * m.L);
+    if (hc) dm.mk_fold = dalloc<float>((size_t)m.L * 2 * (3 * D + F));
     std::vector<float> tmp(std::max(3 * D * D, D * F));
     std::vector<MkLayer> host(m.L);
     for (int l = 0; l < m.L; l++) {
@@ -474,12 +476,14 @@ static void mk_setup(const fb2_model& m, DeviceModel& dm, const float* const* pa
                 const size_t cs = dm.mk_cs, hd = m.hd, hq = hd / cs, nhead = dm.mk_nhead, nmlp = nW;
                 size_t o = 0;
                 if (ph == MK_QKV) {
+                    // LN1's gains folded into the weights: g_k W[k][c]
+                    const float* g = q[0];
                     for (size_t c = 0; c < nhead; c++) {
                         const size_t h = c / cs, r = c % cs;
                         for (size_t k = 0; k < K; k++)
                             for (size_t part = 0; part < 3; part++)
                                 for (size_t i = 0; i < hq; i++)
-                                    tmp[o + k * 3 * hq + part * hq + i] = W[k * N + part * D + h * hd + r * hq + i];
+                                    tmp[o + k * 3 * hq + part * hq + i] = g[k] * W[k * N + part * D + h * hd + r * hq + i];
                         o += K * 3 * hq;
                     }
                 } else if (ph == MK_PROJ) {
@@ -491,9 +495,12 @@ static void mk_setup(const fb2_model& m, DeviceModel& dm, const float* const* pa
                         o += hd * wp;
                     }
                 } else if (ph == MK_FC) {
+                    // LN2's gains folded into the weights
+                    const float* g = q[6];
                     for (size_t j = 0; j < nmlp; j++) {
                         const size_t j0 = 4 * (j * (F / 4) / nmlp), j1 = 4 * ((j + 1) * (F / 4) / nmlp), w = j1 - j0;
-                        for (size_t k = 0; k < K; k++) std::memcpy(&tmp[K * j0 + k * w], W + k * N + j0, w * sizeof(float));
+                        for (size_t k = 0; k < K; k++)
+                            for (size_t i = 0; i < w; i++) tmp[K * j0 + k * w + i] = g[k] * W[k * N + j0 + i];
                     }
                 } else {
                     std::memcpy(tmp.data(), W, K * N * sizeof(float));
@@ -508,6 +515,30 @@ static void mk_setup(const fb2_model& m, DeviceModel& dm, const float* const* pa
             CK(cudaMemcpy(dm.relaid + off, tmp.data(), K * N * sizeof(float), cudaMemcpyHostToDevice));
             host[l].w[ph] = dm.relaid + off;
             off += K * N;
+        }
+        if (hc) {
+            // per qkv / fc column: (S, B) of the folded LayerNorm, in double:
+            // S_c = sum_k (g_k W[k][c]) as the kernel multiplies, B_c = sum_k beta_k W[k][c] + bias_c
+            std::vector<float> fold(2 * (3 * D + F));
+            auto fold_cols = [&](const float* W, size_t N, const float* g, const float* beta, const float* bias,
+                                 float* out) {
+                std::vector<double> sS(N, 0.0), sB(N, 0.0);
+                for (size_t k = 0; k < D; k++)
+                    for (size_t c = 0; c < N; c++) {
+                        sS[c] += (double)(g[k] * W[k * N + c]);
+                        sB[c] += (double)beta[k] * (double)W[k * N + c];
+                    }
+                for (size_t c = 0; c < N; c++) {
+                    out[2 * c] = (float)sS[c];
+                    out[2 * c + 1] = (float)(sB[c] + (double)bias[c]);
+                }
+            };
+            fold_cols(q[2], 3 * D, q[0], q[1], q[3], fold.data());
+            fold_cols(q[8], F, q[6], q[7], q[9], fold.data() + 2 * 3 * D);
+            CK(cudaMemcpy(dm.mk_fold + (size_t)l * fold.size(), fold.data(), fold.size() * sizeof(float),
+                          cudaMemcpyHostToDevice));
+            host[l].fold[0] = dm.mk_fold + (size_t)l * fold.size();
+            host[l].fold[1] = host[l].fold[0] + 2 * 3 * D;
         }
         const LayerW& lw = dm.layers[l];
         host[l].b[MK_QKV] = lw.qkv_b;
@@ -1896,6 +1927,7 @@ int32_t fb2_model_create(const fb2_model_desc* desc, const float* const* params,
                 cudaSetDevice(dm.device);
                 dfree(dm.blob);
                 dfree(dm.relaid);
+                dfree(dm.mk_fold);
                 dfree(dm.d_mk_layers);
                 dfree(dm.tc_blob);
                 dfree(dm.tc_head_blob);
@@ -1914,6 +1946,7 @@ void fb2_model_destroy(fb2_model* m) {
         cudaSetDevice(dm.device);
         dfree(dm.blob);
         dfree(dm.relaid);
+        dfree(dm.mk_fold);
         dfree(dm.d_mk_layers);
         dfree(dm.tc_blob);
         dfree(dm.tc_head_blob);
