@@ -1103,7 +1103,9 @@ __device__ __noinline__ uint32_t mk_gemv_wide_acc(const float* actv, int K, int 
     } while (0)
 
 // ---- the kernel ---------------------------------------------------------------
-template <int MR>
+// HC: the head-cluster layer path (a separate instantiation, so each path
+// gets the registers of its own code; MkArgs::hc must match).
+template <int MR, bool HC>
 __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     extern __shared__ __align__(128) unsigned char mk_smem_raw[];
     const int tid = threadIdx.x;
@@ -1127,7 +1129,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     int* surv_i = reinterpret_cast<int*>(surv_v + MK_SURV_MAX);  // [MK_SURV_MAX]
     float* wts_m = reinterpret_cast<float*>(surv_i + MK_SURV_MAX);  // [MR*H][maxc] chunk weights
     // head-cluster region (hc launches only)
-    const MkHcLayout hcl = mk_hc_layout(MR, D, F, hd, a.ctx, a.hc ? a.cs : 1, nW, L);
+    const MkHcLayout hcl = mk_hc_layout(MR, D, F, hd, a.ctx, HC ? a.cs : 1, nW, L);
     float* hcb = reinterpret_cast<float*>(
         (reinterpret_cast<uintptr_t>(wts_m + 2 * MR * H * a.maxc) + 15) & ~(uintptr_t)15);
     unsigned long long* qkv_in = reinterpret_cast<unsigned long long*>(hcb + hcl.qkv_in);
@@ -1184,10 +1186,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 8);
         }
-        if (a.hc) mbar_init(&hc_mbar[4], a.cs);  // exit handshake: one arrival per cluster CTA
+        if (HC) mbar_init(&hc_mbar[4], a.cs);  // exit handshake: one arrival per cluster CTA
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (a.hc) {
+    if constexpr (HC) {
         for (int i = tid; i < L * (int)(sizeof(MkLayer) / 8); i += MK_THREADS)
             reinterpret_cast<const float**>(hc_lay)[i] = reinterpret_cast<const float* const*>(a.layers)[i];
         {
@@ -1206,7 +1208,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     }
     __syncthreads();
     // the cluster's mbarriers are initialised before any CTA arrives on them
-    if (a.hc) cluster_sync_all();
+    if constexpr (HC) cluster_sync_all();
 
     // positions at step s (dummy rows stay at 0); attention units (m, h, c)
     // cover the cached keys [0, pos-1) in chunks of KC
@@ -1266,7 +1268,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         };
         for (int s = 0; s < a.nsteps && ok; s++) {
             const unsigned int gs = a.gstep0 + s;
-            if (a.hc) {
+            if constexpr (HC) {
                 // this CTA's slices of every layer, in the order the consumers use them
                 const int q3 = hcl.q3, wp = D / a.cs;
                 const int j0 = 4 * (int)((long long)cta * (F / 4) / nW), j1 = 4 * (int)((long long)(cta + 1) * (F / 4) / nW);
@@ -1282,7 +1284,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     }
                 }
             }
-            for (int l = 0; l < L && ok && !a.hc; l++) {
+            for (int l = 0; l < L && ok && !HC; l++) {
                 const MkLayer& ly = a.layers[l];
                 issue_strip(ly.w[MK_QKV], D, 3 * D);
                 if (l == 0 && gs >= 2 && ok) {
@@ -1362,7 +1364,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         for (int p = tid; p < MR * w; p += MK_CONS) epilogue(p / w, n0 + p % w, uacc[p]);
     };
 
-    if (a.hc && tid == 0) {
+    if (HC && tid == 0) {
         // the head-cluster geometry, with the launch's only divisions
         int lcs = 0, lhd = 0;
         while ((1 << lcs) < a.cs) lcs++;
@@ -1392,7 +1394,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         }
         cons_sync();
         MK_TRACE(24);
-        if (a.hc) {
+        if constexpr (HC) {
             // ======== head-cluster layers ========
             // Per layer two exchanges through global memory: the attention
             // projection's head partials -> x2, every CTA's MLP partials -> x
@@ -1717,7 +1719,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 if (l < 24) MK_TRACE(33 + l);
             }
         }
-        for (int l = 0; l < L && !a.hc; l++) {
+        for (int l = 0; l < L && !HC; l++) {
             const MkLayer& ly = a.layers[l];
             const uint32_t tg = mk_tag(gs, l, L);
             MK_TRACE_L(0);
@@ -2057,7 +2059,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         // ---- head: LN_f -> logits of this CTA's vocabulary slice ----------------
         const uint32_t th = mk_tag(gs, L, L);
         const LnRegs lnf = ln_prefetch(a.lnf_w, a.lnf_b, D);
-        if (!a.hc) {
+        if constexpr (!HC) {
             gather_tagged(a.xx, xres, MR * D, mk_tag(gs, L - 1, L), a.err, &s_abort);
             if (cons_sync_or(s_abort)) return;
         } else {
@@ -2629,7 +2631,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     }
     };
     consumers();
-    if (a.hc) {
+    if constexpr (HC) {
         // no CTA of a cluster leaves while a cluster CTA may still write
         // into its shared memory: each arrives on every CTA's exit barrier after
         // its last push, then waits (bounded) for all of them

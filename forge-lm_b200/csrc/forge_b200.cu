@@ -256,10 +256,14 @@ static void configure_kernels(int dev) {
     setmax((const void*)k_gemm_tc_swab<64>, 227 * 1024);
     setmax((const void*)k_gemm_tc_swab<128>, 227 * 1024);
     setmax((const void*)k_sample_rows, 227 * 1024);
-    setmax((const void*)k_decode_mega<1>, 0);
-    setmax((const void*)k_decode_mega<2>, 0);
-    setmax((const void*)k_decode_mega<4>, 0);
-    setmax((const void*)k_decode_mega<8>, 0);
+    setmax((const void*)k_decode_mega<1, false>, 0);
+    setmax((const void*)k_decode_mega<2, false>, 0);
+    setmax((const void*)k_decode_mega<4, false>, 0);
+    setmax((const void*)k_decode_mega<8, false>, 0);
+    setmax((const void*)k_decode_mega<1, true>, 0);
+    setmax((const void*)k_decode_mega<2, true>, 0);
+    setmax((const void*)k_decode_mega<4, true>, 0);
+    setmax((const void*)k_decode_mega<8, true>, 0);
 }
 
 // ---------------------------------------------------------------------------
@@ -270,6 +274,19 @@ static int mk_maxc(int ctx, int hd) { return ceil_div(ctx, mk_keys_per_chunk(hd)
 // Vocabulary entries per CTA slice, rounded up to a multiple of 4 so every
 // shared-memory region after the slices stays 16-byte aligned.
 static int mk_slice_max(int V, int nW) { return (ceil_div(V, nW) + 3) & ~3; }
+
+// The persistent kernel's instantiation for MR rows and the layer path.
+static const void* mk_kernel(int MR, bool hc) {
+    if (hc)
+        return MR == 1 ? (const void*)k_decode_mega<1, true>
+             : MR == 2 ? (const void*)k_decode_mega<2, true>
+             : MR == 4 ? (const void*)k_decode_mega<4, true>
+                       : (const void*)k_decode_mega<8, true>;
+    return MR == 1 ? (const void*)k_decode_mega<1, false>
+         : MR == 2 ? (const void*)k_decode_mega<2, false>
+         : MR == 4 ? (const void*)k_decode_mega<4, false>
+                   : (const void*)k_decode_mega<8, false>;
+}
 
 // Dynamic shared memory of k_decode_mega<MR> with `nstage` ring stages
 // (cs > 0: the head-cluster layout, clusters of cs CTAs).
@@ -284,10 +301,7 @@ static int mk_nstage(const fb2_model& m, int MR, int nW, int device, int cs = 0,
     int optin = 0;
     CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
     cudaFuncAttributes fa;
-    const void* f = MR == 1 ? (const void*)k_decode_mega<1>
-                  : MR == 2 ? (const void*)k_decode_mega<2>
-                  : MR == 4 ? (const void*)k_decode_mega<4>
-                            : (const void*)k_decode_mega<8>;
+    const void* f = mk_kernel(MR, cs > 0);
     CK(cudaFuncGetAttributes(&fa, f));
     const long long avail = (long long)optin - (long long)fa.sharedSizeBytes;
     int ns = 16;
@@ -311,7 +325,7 @@ static int mk_max_clusters(const fb2_model& m, int nW, int cs, int device) {
     cfg.attrs = at;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, (const void*)k_decode_mega<1>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, mk_kernel(1, true), &cfg) != cudaSuccess) {
         cudaGetLastError();
         return 0;
     }
@@ -1151,10 +1165,7 @@ static void run_mega(DeviceSession& s, int n, int nsteps, const SampleParams& P,
     a.acc = s.mk_acc;
     const size_t smem = mk_smem(m, MR, nW, nstage, hc_cs, sb);
     void* args[] = {&a};
-    const void* f = MR == 1 ? (const void*)k_decode_mega<1>
-                  : MR == 2 ? (const void*)k_decode_mega<2>
-                  : MR == 4 ? (const void*)k_decode_mega<4>
-                            : (const void*)k_decode_mega<8>;
+    const void* f = mk_kernel(MR, dm.mk_hc);
     if (dm.mk_hc) {
         // clusters of mk_cs CTAs; cooperative, so the launch fails rather than
         // runs if not every CTA can be resident (the CTAs wait on one another)
