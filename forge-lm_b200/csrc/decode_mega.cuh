@@ -915,18 +915,27 @@ FB2_DEV MkGeo mk_geo(int w, int K, int MR) {
 
 // y[m][c] = sum_k act[m][k] * W[k][c] for a [K][w] slice, w % 4 == 0: thread
 // (g, q) reads column quad q of rows g, g + G, ... as float4 (consecutive
-// threads read consecutive 16-byte words of a stage row), two row chains
-// each; the G partials of an output go through scr (4096 floats) and are
-// summed in a fixed order into ys[MR*w] behind a barrier.  No division in
-// the loops: the geometry comes precomputed.
+// threads read consecutive 16-byte words of a stage row), U rows in flight
+// per pass (the loop is bound by shared-memory latency, not bandwidth).
+// Partials: for w <= 128 the groups of a warp are summed with shuffles and
+// the 8 warp partials of an output through scr (MR * 8 * w floats); wider
+// slices put all G group partials through scr (4096 floats).  Either way
+// the order is fixed.  ys[MR*w] holds the results behind a barrier.
+// With `mslots` set, warp 7 also turns the per-warp moments mslots (see
+// mk_row_moments, rows of length K) into stats[2m] = mean, stats[2m+1] =
+// 1/sqrt(var + eps) while the partials are summed.  No division in the
+// loops: the geometry comes precomputed.
 template <int MR>
 __device__ __noinline__ uint32_t mk_gemv_q4(const float* actv, int K, int w, MkGeo geo, unsigned char* ring,
                                             uint64_t* full, uint64_t* empty, int nstage, uint32_t it, float* scr4k,
-                                            float* ys, int* err, volatile int* abort_flag) {
-    const int tid = threadIdx.x;
+                                            float* ys, int* err, volatile int* abort_flag,
+                                            const float* mslots = nullptr, float* stats = nullptr) {
+    constexpr int U = MR <= 2 ? 4 : 2;  // 4 in flight measured fastest (2 and 8 slower)
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int R = geo.R, G = geo.G, nq = w >> 2;
     const int q = tid & ((1 << geo.lgp) - 1), g = tid >> geo.lgp;
     const bool valid = g < G && q < nq;
+    const bool shfl = geo.lgp <= 5 && MR * 8 * w <= 4096;
     if (tid == 0) mk_gemv_t[0] = gtimer();
     float4 a0[MR], a1[MR];
 #pragma unroll
@@ -937,22 +946,23 @@ __device__ __noinline__ uint32_t mk_gemv_q4(const float* actv, int K, int w, MkG
         const float4* st = reinterpret_cast<const float4*>(ring + (size_t)rp_stage(it) * mk_sbytes);
         if (valid) {
             const float* av = actv + r0;
-            int r = g;
-            for (; r + G < rows; r += 2 * G) {
-                const float4 w0 = st[r * nq + q], w1 = st[(r + G) * nq + q];
+            for (int r = g; r < rows; r += U * G) {
+                float4 wv[U];
+#pragma unroll
+                for (int u = 0; u < U; u++)
+                    wv[u] = r + u * G < rows ? st[(r + u * G) * nq + q] : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                 for (int m = 0; m < MR; m++) {
-                    const float x0 = av[m * K + r], x1 = av[m * K + r + G];
-                    a0[m].x += x0 * w0.x; a0[m].y += x0 * w0.y; a0[m].z += x0 * w0.z; a0[m].w += x0 * w0.w;
-                    a1[m].x += x1 * w1.x; a1[m].y += x1 * w1.y; a1[m].z += x1 * w1.z; a1[m].w += x1 * w1.w;
-                }
-            }
-            if (r < rows) {
-                const float4 w0 = st[r * nq + q];
+                    float xv[U];
 #pragma unroll
-                for (int m = 0; m < MR; m++) {
-                    const float x0 = av[m * K + r];
-                    a0[m].x += x0 * w0.x; a0[m].y += x0 * w0.y; a0[m].z += x0 * w0.z; a0[m].w += x0 * w0.w;
+                    for (int u = 0; u < U; u++) xv[u] = r + u * G < rows ? av[m * K + r + u * G] : 0.f;
+#pragma unroll
+                    for (int u = 0; u < U; u += 2) {
+                        a0[m].x += xv[u] * wv[u].x; a0[m].y += xv[u] * wv[u].y;
+                        a0[m].z += xv[u] * wv[u].z; a0[m].w += xv[u] * wv[u].w;
+                        a1[m].x += xv[u + 1] * wv[u + 1].x; a1[m].y += xv[u + 1] * wv[u + 1].y;
+                        a1[m].z += xv[u + 1] * wv[u + 1].z; a1[m].w += xv[u + 1] * wv[u + 1].w;
+                    }
                 }
             }
         }
@@ -960,27 +970,48 @@ __device__ __noinline__ uint32_t mk_gemv_q4(const float* actv, int K, int w, MkG
         it = rp_next(it, nstage);
     }
     if (tid == 0) mk_gemv_t[1] = gtimer();
-    if (valid)
+    float4 p[MR];
 #pragma unroll
-        for (int m = 0; m < MR; m++)
-            reinterpret_cast<float4*>(scr4k)[((m * G + g) * w >> 2) + q] =
-                make_float4(a0[m].x + a1[m].x, a0[m].y + a1[m].y, a0[m].z + a1[m].z, a0[m].w + a1[m].w);
+    for (int m = 0; m < MR; m++)
+        p[m] = make_float4(a0[m].x + a1[m].x, a0[m].y + a1[m].y, a0[m].z + a1[m].z, a0[m].w + a1[m].w);
+    int P;  // partials per output
+    if (shfl) {
+        // the 32 >> lgp groups of this warp (lanes differing in bits lgp..4)
+        for (int o = 16; o >= (1 << geo.lgp); o >>= 1)
+#pragma unroll
+            for (int m = 0; m < MR; m++) {
+                p[m].x += __shfl_xor_sync(0xffffffffu, p[m].x, o);
+                p[m].y += __shfl_xor_sync(0xffffffffu, p[m].y, o);
+                p[m].z += __shfl_xor_sync(0xffffffffu, p[m].z, o);
+                p[m].w += __shfl_xor_sync(0xffffffffu, p[m].w, o);
+            }
+        if (lane < (1 << geo.lgp) && q < nq)
+#pragma unroll
+            for (int m = 0; m < MR; m++) reinterpret_cast<float4*>(scr4k)[(((m << 3) + warp) * w >> 2) + q] = p[m];
+        P = 8;
+    } else {
+        if (valid)
+#pragma unroll
+            for (int m = 0; m < MR; m++) reinterpret_cast<float4*>(scr4k)[((m * G + g) * w >> 2) + q] = p[m];
+        P = G;
+    }
     cons_sync();
 #pragma unroll
     for (int m = 0; m < MR; m++)
         for (int c = tid; c < w; c += MK_CONS) {
-            const float* rp = scr4k + (m * G) * w + c;
+            const float* rp = scr4k + (m * P) * w + c;
             float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
             int gg = 0;
-            for (; gg + 3 < G; gg += 4) {
+            for (; gg + 3 < P; gg += 4) {
                 t0 += rp[gg * w];
                 t1 += rp[(gg + 1) * w];
                 t2 += rp[(gg + 2) * w];
                 t3 += rp[(gg + 3) * w];
             }
-            for (; gg < G; gg++) t0 += rp[gg * w];
+            for (; gg < P; gg++) t0 += rp[gg * w];
             ys[m * w + c] = (t0 + t1) + (t2 + t3);
         }
+    if (mslots && warp == 7 && lane < MR) mk_row_stats(mslots, lane, K, stats[2 * lane], stats[2 * lane + 1]);
     cons_sync();
     if (tid == 0) mk_gemv_t[2] = gtimer();
     return it;
@@ -994,6 +1025,7 @@ __device__ __noinline__ uint32_t mk_gemv_wide_q4(const float* actv, int K, int w
                                                  uint64_t* full, uint64_t* empty, int nstage, uint32_t it,
                                                  unsigned long long* out, const uint32_t* red_remote, int rank,
                                                  int blk, uint32_t tag, int* err, volatile int* abort_flag) {
+    constexpr int U = MR <= 2 ? 4 : 2;  // rows in flight per pass
     const int tid = threadIdx.x;
     const int nq = w >> 2;
     float4 acc[MR];
@@ -1004,12 +1036,20 @@ __device__ __noinline__ uint32_t mk_gemv_wide_q4(const float* actv, int K, int w
         wait_full(full, it, nstage, err, abort_flag);
         const float4* st = reinterpret_cast<const float4*>(ring + (size_t)rp_stage(it) * mk_sbytes);
         if (tid < nq)
-            for (int r = 0; r < rows; r++) {
-                const float4 v = st[r * nq + tid];
+            for (int r = 0; r < rows; r += U) {
+                float4 v[U];
+#pragma unroll
+                for (int u = 0; u < U; u++) v[u] = r + u < rows ? st[(r + u) * nq + tid] : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                 for (int m = 0; m < MR; m++) {
-                    const float x = actv[m * K + r0 + r];
-                    acc[m].x += x * v.x; acc[m].y += x * v.y; acc[m].z += x * v.z; acc[m].w += x * v.w;
+                    float x[U];
+#pragma unroll
+                    for (int u = 0; u < U; u++) x[u] = r + u < rows ? actv[m * K + r0 + r + u] : 0.f;
+#pragma unroll
+                    for (int u = 0; u < U; u++) {
+                        acc[m].x += x[u] * v[u].x; acc[m].y += x[u] * v[u].y;
+                        acc[m].z += x[u] * v[u].z; acc[m].w += x[u] * v[u].w;
+                    }
                 }
             }
         release_stage(empty, it, nstage);
@@ -1448,7 +1488,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     MK_TRACE_L(1);
                     if (tid == 0) mk_ring_wait = 0;
                     it = mk_gemv_q4<MR>(xres, D, q3, s_geo[0], ring, full, empty, a.nstage, it, gscr, hc_ys, a.err,
-                                        &s_abort);
+                                        &s_abort, scr + 384, scr + 320);
                     MK_TRACE_L(2);
                     if (l == 0) {
                         MK_TRACE_DUR(22, mk_gemv_t[0]);
@@ -1460,8 +1500,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     const uint32_t xtag = rnd + 1u;  // exchange words of this round
                     if (tid < q3)  // q3 <= 256
                         for (int m = 0; m < MR; m++) {
-                            float mu, rstd;
-                            mk_row_stats(scr + 384, m, D, mu, rstd);
+                            const float mu = scr[320 + 2 * m], rstd = scr[321 + 2 * m];
                             const float v = rstd * (hc_ys[m * q3 + tid] - mu * fqS) + fqB;
                             if (qpart > 0 && !s_dummy[m])
                                 a.kv[(size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
@@ -1659,13 +1698,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     float* hb = act + MR * D;  // [MR][J]
                     if (tid == 0) mk_ring_wait = 0;
                     it = mk_gemv_q4<MR>(x2res, D, J, s_geo[2], ring, full, empty, a.nstage, it, gscr, hc_ys, a.err,
-                                        &s_abort);
+                                        &s_abort, scr + 384, scr + 320);
                     MK_TRACE_L(12);
                     if (l == 0) MK_TRACE_DUR(16, mk_ring_wait);
                     if (tid < J)  // J <= 256
                         for (int m = 0; m < MR; m++) {
-                            float mu, rstd;
-                            mk_row_stats(scr + 384, m, D, mu, rstd);
+                            const float mu = scr[320 + 2 * m], rstd = scr[321 + 2 * m];
                             hb[m * J + tid] = gelu_tanh(rstd * (hc_ys[m * J + tid] - mu * ffS) + ffB);
                         }
                     cons_sync();
