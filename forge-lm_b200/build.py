@@ -58,18 +58,32 @@ def gen_fixups(verbose: bool = False) -> str:
     return out
 
 
+def _flags() -> list[str]:
+    """nvcc flags; FORGE_B200_PHASE_TRACE=1 adds the persistent kernel's
+    per-phase stamps (a diagnostic build: the stamps cost throughput)."""
+    flags = list(NVCC_FLAGS)
+    if os.environ.get("FORGE_B200_PHASE_TRACE") == "1":
+        flags.append("-DFB2_MK_PHASE_TRACE")
+    return flags
+
+
 def build(verbose: bool = False, force: bool = False) -> str:
     gen_fixups(verbose)
     sources = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh", ".hpp"))]
     sources.append(os.path.join(ROOT, "include", "forge_b200.h"))
     sources.append(os.path.join(GEN, "expf_fixups.inc"))
-    if not force and not _newer(LIB, sources):
+    flags = _flags()
+    stamp = LIB + ".flags"
+    same_flags = os.path.exists(stamp) and open(stamp).read() == " ".join(flags)
+    if not force and same_flags and not _newer(LIB, sources):
         return LIB
-    cmd = [_nvcc(), *NVCC_FLAGS, "-shared", "-o", LIB + ".tmp", os.path.join(CSRC, "forge_b200.cu")]
+    cmd = [_nvcc(), *flags, "-shared", "-o", LIB + ".tmp", os.path.join(CSRC, "forge_b200.cu")]
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)
     os.replace(LIB + ".tmp", LIB)
+    with open(stamp, "w") as f:
+        f.write(" ".join(flags))
     return LIB
 
 

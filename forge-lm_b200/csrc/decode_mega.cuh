@@ -53,6 +53,14 @@ __shared__ unsigned long long mk_ring_wait;
 // Traced runs: thread 0's stamps inside the last column GEMV (start, after
 // the stages, after the reduction).
 __shared__ unsigned long long mk_gemv_t[3];
+#ifdef FB2_MK_PHASE_TRACE
+#define MK_GEMV_STAMP(i) \
+    if (threadIdx.x == 0) mk_gemv_t[i] = gtimer()
+#else
+#define MK_GEMV_STAMP(i) \
+    do {                 \
+    } while (0)
+#endif
 
 enum MkPhase { MK_QKV = 0, MK_PROJ = 1, MK_FC = 2, MK_PROJ2 = 3 };
 
@@ -936,7 +944,7 @@ __device__ __noinline__ uint32_t mk_gemv_q4(const float* actv, int K, int w, MkG
     const int q = tid & ((1 << geo.lgp) - 1), g = tid >> geo.lgp;
     const bool valid = g < G && q < nq;
     const bool shfl = geo.lgp <= 5 && MR * 8 * w <= 4096;
-    if (tid == 0) mk_gemv_t[0] = gtimer();
+    MK_GEMV_STAMP(0);
     float4 a0[MR], a1[MR];
 #pragma unroll
     for (int m = 0; m < MR; m++) a0[m] = a1[m] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -969,7 +977,7 @@ __device__ __noinline__ uint32_t mk_gemv_q4(const float* actv, int K, int w, MkG
         release_stage(empty, it, nstage);
         it = rp_next(it, nstage);
     }
-    if (tid == 0) mk_gemv_t[1] = gtimer();
+    MK_GEMV_STAMP(1);
     float4 p[MR];
 #pragma unroll
     for (int m = 0; m < MR; m++)
@@ -1013,7 +1021,7 @@ __device__ __noinline__ uint32_t mk_gemv_q4(const float* actv, int K, int w, MkG
         }
     if (mslots && warp == 7 && lane < MR) mk_row_stats(mslots, lane, K, stats[2 * lane], stats[2 * lane + 1]);
     cons_sync();
-    if (tid == 0) mk_gemv_t[2] = gtimer();
+    MK_GEMV_STAMP(2);
     return it;
 }
 
@@ -1132,6 +1140,11 @@ __device__ __noinline__ uint32_t mk_gemv_wide_acc(const float* actv, int K, int 
         if (a.trace && s < a.trace_steps && (pt) < MK_TRACE_POINTS)                                  \
             a.trace[((size_t)cta * a.trace_steps + s) * MK_TRACE_POINTS + (pt)] = gtimer();          \
     } while (0)
+// Phase-level stamps inside a layer (layer 0 only) and GEMV timings: built
+// only with FB2_MK_PHASE_TRACE (FORGE_B200_PHASE_TRACE=1 at build time).  The
+// persistent kernel runs each layer's code once per layer, so every extra
+// instruction there costs instruction-cache misses in the production build.
+#ifdef FB2_MK_PHASE_TRACE
 #define MK_TRACE_DUR(pt, v)                                                                         \
     do {                                                                                            \
         if (a.trace && tid == 0 && s < a.trace_steps && (pt) < MK_TRACE_POINTS)                    \
@@ -1141,6 +1154,14 @@ __device__ __noinline__ uint32_t mk_gemv_wide_acc(const float* actv, int K, int 
     do {                                 \
         if (l < 1) MK_TRACE(l * 12 + (off)); \
     } while (0)
+#else
+#define MK_TRACE_DUR(pt, v) \
+    do {                    \
+    } while (0)
+#define MK_TRACE_L(off) \
+    do {                \
+    } while (0)
+#endif
 
 // ---- the kernel ---------------------------------------------------------------
 // HC: the head-cluster layer path (a separate instantiation, so each path

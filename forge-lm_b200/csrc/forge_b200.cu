@@ -1182,7 +1182,12 @@ static void run_mega(DeviceSession& s, int n, int nsteps, const SampleParams& P,
         at[1].id = cudaLaunchAttributeCooperative;
         at[1].val.cooperative = 1;
         cfg.attrs = at;
-        cfg.numAttrs = 2;
+        // FORGE_B200_MK_COOP=0 (profiling only: Nsight Compute does not launch
+        // cooperative cluster grids) drops the residency check; the plan's
+        // cluster count is within the device's active-cluster limit, and a
+        // grid that is not fully resident ends in the waits' timeout status.
+        const char* coop = getenv("FORGE_B200_MK_COOP");
+        cfg.numAttrs = coop && coop[0] == '0' ? 1 : 2;
         CK(cudaLaunchKernelExC(&cfg, f, args));
     } else {
         CK(cudaLaunchCooperativeKernel(f, dim3(nW), dim3(MK_THREADS), args, smem, s.stream));
