@@ -261,6 +261,18 @@ FB2_DEV void dsmem_st_pair(uint32_t addr, float v, uint32_t tag) {
     const unsigned long long w = ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
     asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(addr), "l"(w) : "memory");
 }
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) of
+// this CTA's shared memory to shared::cluster address `dst` of a cluster CTA,
+// completing on that CTA's mbarrier (shared::cluster address `mbar`).  The
+// writers of `src` fence their generic-proxy writes (fence_async_smem) and
+// pass a barrier before the copy is issued.
+FB2_DEV void bulk_s2c(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     dst),
+                 "r"(smem_u32(src)), "r"(bytes), "r"(mbar)
+                 : "memory");
+}
+FB2_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // Waits until words buf[0..n) of this CTA's shared memory (pushed by cluster
 // CTAs) carry `tag`; bounded like every other wait.
 FB2_DEV void wait_tags_smem(const unsigned long long* buf, int n, uint32_t tag, int* err, volatile int* abort_flag) {
@@ -339,6 +351,84 @@ __device__ __noinline__ void acc_gather(const unsigned long long* src, float* ou
         for (int k = 0; k < 8; k++) {
             const int i = base + k * MK_CONS + (int)threadIdx.x;
             if (i < n) out[i] = acc_value(w[k]);
+        }
+    }
+}
+
+// Residual add at a fixed-point exchange: out[m][n] = base[m][n] + (value of
+// src[m * D + n] + bias of column n), n = tid + 256 k (bias k in b0..b3, D <=
+// 1024), once each word's count is `count`; also the per-warp moments of the
+// out rows into mslots (the layout and summation order of mk_row_moments).
+// Bounded like acc_gather.  No trailing barrier.
+template <int MR>
+__device__ __noinline__ void acc_gather_res(const unsigned long long* src, float* out, const float* base, int D,
+                                            float b0, float b1, float b2, float b3, uint32_t count, float* mslots,
+                                            int* err, volatile int* abort_flag) {
+    constexpr int NM = MR < 2 ? MR : 2;  // rows in flight
+    const int tid = threadIdx.x;
+    const float bk[4] = {b0, b1, b2, b3};
+    for (int m0 = 0; m0 < MR; m0 += NM) {
+        unsigned long long w[NM][4];
+        uint32_t pend = 0;
+#pragma unroll
+        for (int mm = 0; mm < NM; mm++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int n = tid + k * MK_CONS;
+                w[mm][k] = 0ull;
+                if (n < D) {
+                    w[mm][k] = ld_pair(src + (size_t)(m0 + mm) * D + n);
+                    pend |= 1u << (mm * 4 + k);
+                }
+            }
+        unsigned long long t0 = 0;
+        for (int n_poll = 0;; n_poll++) {
+            uint32_t still = 0;
+#pragma unroll
+            for (int mm = 0; mm < NM; mm++)
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    if (((pend >> (mm * 4 + k)) & 1u) && (uint32_t)(w[mm][k] & 255ull) != count)
+                        still |= 1u << (mm * 4 + k);
+            if (!still || *abort_flag) break;
+            const unsigned long long now = gtimer();
+            if (!t0) t0 = now;
+            else if (now - t0 > mk_wait_ns) {
+                atomicExch(err, 6);
+                *abort_flag = 1;
+                break;
+            }
+            if ((n_poll & 63) == 63 && ld_relaxed_i32(err) != 0) {
+                *abort_flag = 1;
+                break;
+            }
+#pragma unroll
+            for (int mm = 0; mm < NM; mm++)
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    if ((still >> (mm * 4 + k)) & 1u)
+                        w[mm][k] = ld_pair(src + (size_t)(m0 + mm) * D + tid + k * MK_CONS);
+        }
+#pragma unroll
+        for (int mm = 0; mm < NM; mm++) {
+            const int m = m0 + mm;
+            float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int n = tid + k * MK_CONS;
+                if (n < D) {
+                    const float v = base[m * D + n] + (acc_value(w[mm][k]) + bk[k]);
+                    out[m * D + n] = v;
+                    s1 += v;
+                    s2 += v * v;
+                }
+            }
+            s1 = warp_sum(s1);
+            s2 = warp_sum(s2);
+            if ((tid & 31) == 0) {
+                mslots[m * 16 + (tid >> 5)] = s1;
+                mslots[m * 16 + 8 + (tid >> 5)] = s2;
+            }
         }
     }
 }
@@ -702,23 +792,24 @@ __device__ __noinline__ void mk_layernorm(const float* src, float* dst, int D, c
 // 16-byte aligned base; every part a multiple of 4 floats):
 //   qkv_in [cs][MR][q3]      q/k/v parts pushed by each cluster CTA (q3 = 3 hd / cs),
 //                            64-bit words (round tag << 32 | value bits)
-//   part_in[cs][MR][ps]      attention partials (max, sum, acc[hd]) pushed by each CTA,
-//                            tagged words as qkv_in
+//   part_in[cs][MR][ps]      attention partials (max, sum, acc[hd], padding) of each
+//                            cluster CTA, floats, by bulk copy (completion on mbar[0])
 //   red_in [cs][MR][D / cs]  (MR <= 2) MLP partials of this CTA's column block
-//                            pushed by each cluster CTA, tagged words
+//                            from each cluster CTA, floats, by bulk copy (mbar[1])
 // One buffer each suffices: a round's words are read before any CTA can
 // reach the next round (that needs the layer's global sum, to which every
 // reader contributes after reading).
+//   part_out[MR][ps]         this CTA's attention partials, the bulk copies' source
 //   ctxs   [MR][hd]          the head's combined context
 //   att_p  [np]              scores / probabilities of this CTA's keys of one row
 //   pvred  [256]             p.V partial sums per thread group
 //   ys     [MR][ymax]        outputs of a column slice
 //   hscr   [64]              q of one row, scratch
-//   mbar   [8] (u64)         qkv[2], part[2], exit
+//   mbar   [8] (u64)         [0] partials received, [1] MLP partials received, [4] exit
 //   lay    [L] MkLayer        the layer table (pointers), copied once per launch
 struct MkHcLayout {
     int q3, ps, np, ymax;
-    int qkv_in, part_in, red_in, ctxs, att_p, pvred, ys, hscr, mbar, lay;
+    int qkv_in, part_in, red_in, part_out, ctxs, att_p, pvred, ys, hscr, mbar, lay;
     int total_floats;
 };
 __host__ __device__ inline int mk_r4(int v) { return (v + 3) & ~3; }
@@ -734,13 +825,14 @@ __host__ __device__ inline MkHcLayout mk_hc_layout(int MR, int D, int F, int hd,
     L.qkv_in = o; o += 2 * mk_r4(cs * MR * L.q3);  // u64 words
     L.part_in = o; o += 2 * (cs * MR * L.ps);
     L.red_in = o; o += MR <= 2 ? 2 * mk_r4(cs * MR * (D / cs)) : 0;
+    L.part_out = o; o += MR * L.ps;
     L.ctxs = o; o += mk_r4(MR * hd);
     L.att_p = o; o += L.np;
     L.pvred = o; o += 256;
     L.ys = o; o += MR * L.ymax;
     L.hscr = o; o += 64;
-    L.mbar = o; o += 16;  // 8 x u64; then 3 x 8 u32: cluster addresses of qkv_in, part_in, red_in per rank
-    o += 24;
+    L.mbar = o; o += 16;  // 8 x u64; then 5 x 8 u32: cluster addresses of qkv_in, part_in,
+    o += 40;              // red_in, mbar[0] and mbar[1] of each rank
     L.lay = o; o += nlayers * (int)(sizeof(MkLayer) / 4);
     L.total_floats = o;
     return L;
@@ -1027,12 +1119,13 @@ __device__ __noinline__ uint32_t mk_gemv_q4(const float* actv, int K, int w, MkG
 
 // Wide [K][w] slice, w % 4 == 0, w <= 1024: thread t sums column quad t over
 // the K rows (float4 loads) and adds each output to the fixed-point
-// accumulator out[m * w + c] (one count).  Returns the ring position.
+// accumulator out[m * w + c] (one count), or, with out null, stores it to
+// red_out[own][m][blk] (own = c / blk).  Returns the ring position.
 template <int MR>
 __device__ __noinline__ uint32_t mk_gemv_wide_q4(const float* actv, int K, int w, int R, unsigned char* ring,
                                                  uint64_t* full, uint64_t* empty, int nstage, uint32_t it,
-                                                 unsigned long long* out, const uint32_t* red_remote, int rank,
-                                                 int blk, uint32_t tag, int* err, volatile int* abort_flag) {
+                                                 unsigned long long* out, float* red_out, int blk, int* err,
+                                                 volatile int* abort_flag) {
     constexpr int U = MR <= 2 ? 4 : 2;  // rows in flight per pass
     const int tid = threadIdx.x;
     const int nq = w >> 2;
@@ -1075,16 +1168,11 @@ __device__ __noinline__ uint32_t mk_gemv_wide_q4(const float* actv, int K, int w
                 acc_add(o + 3, acc_term(acc[m].w));
             }
         } else {
-            // to the cluster CTA that owns columns 4 tid .. 4 tid + 3 (blocks of blk)
+            // into red_out[own][m][blk] for the cluster CTA `own` that owns columns
+            // 4 tid .. 4 tid + 3 (blocks of blk, blk % 4 == 0)
             const int c = 4 * tid, own = c / blk, oc = c - own * blk;
 #pragma unroll
-            for (int m = 0; m < MR; m++) {
-                const uint32_t dst = red_remote[own] + (uint32_t)((rank * MR + m) * blk + oc) * 8u;
-                dsmem_st_pair(dst, acc[m].x, tag);
-                dsmem_st_pair(dst + 8u, acc[m].y, tag);
-                dsmem_st_pair(dst + 16u, acc[m].z, tag);
-                dsmem_st_pair(dst + 24u, acc[m].w, tag);
-            }
+            for (int m = 0; m < MR; m++) reinterpret_cast<float4*>(red_out + (own * MR + m) * blk + oc)[0] = acc[m];
         }
     }
     return it;
@@ -1194,16 +1282,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
     float* hcb = reinterpret_cast<float*>(
         (reinterpret_cast<uintptr_t>(wts_m + 2 * MR * H * a.maxc) + 15) & ~(uintptr_t)15);
     unsigned long long* qkv_in = reinterpret_cast<unsigned long long*>(hcb + hcl.qkv_in);
-    unsigned long long* part_in = reinterpret_cast<unsigned long long*>(hcb + hcl.part_in);
+    float* part_in = hcb + hcl.part_in;
+    float* part_out = hcb + hcl.part_out;
     float* ctxs = hcb + hcl.ctxs;
     float* att_p = hcb + hcl.att_p;
     float* pvred = hcb + hcl.pvred;
     float* hc_ys = hcb + hcl.ys;
     float* hscr = hcb + hcl.hscr;
-    uint64_t* hc_mbar = reinterpret_cast<uint64_t*>(hcb + hcl.mbar);  // [4]: exit handshake
-    unsigned long long* red_in = reinterpret_cast<unsigned long long*>(hcb + hcl.red_in);
+    uint64_t* hc_mbar = reinterpret_cast<uint64_t*>(hcb + hcl.mbar);  // [0] partials, [1] MLP partials, [4] exit
+    float* red_in = hcb + hcl.red_in;
     MkLayer* hc_lay = reinterpret_cast<MkLayer*>(hcb + hcl.lay);
-    uint32_t* hc_rb = reinterpret_cast<uint32_t*>(hcb + hcl.mbar + 16);  // [3][8]
+    uint32_t* hc_rb = reinterpret_cast<uint32_t*>(hcb + hcl.mbar + 16);  // [5][8] cluster addresses
     // iscr regions
     uint32_t* seen = reinterpret_cast<uint32_t*>(iscr);  // [8] bits of the slice
     uint32_t* ban = seen + 8;                            // [8]
@@ -1247,7 +1336,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 8);
         }
-        if (HC) mbar_init(&hc_mbar[4], a.cs);  // exit handshake: one arrival per cluster CTA
+        if (HC) {
+            mbar_init(&hc_mbar[0], 1);     // partials: this CTA's expect_tx arrival + the copies' bytes
+            mbar_init(&hc_mbar[1], 1);     // MLP partials: the same
+            mbar_init(&hc_mbar[4], a.cs);  // exit handshake: one arrival per cluster CTA
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if constexpr (HC) {
@@ -1256,14 +1349,14 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         {
             // the exchange words start untagged in every launch (no word of an
             // earlier launch can carry a tag of this one)
-            const int nq = a.cs * MR * hcl.q3, np = a.cs * MR * hcl.ps, nr = MR <= 2 ? a.cs * MR * (D / a.cs) : 0;
+            const int nq = a.cs * MR * hcl.q3;
             for (int i = tid; i < nq; i += MK_THREADS) qkv_in[i] = 0ull;
-            for (int i = tid; i < np; i += MK_THREADS) part_in[i] = 0ull;
-            for (int i = tid; i < nr; i += MK_THREADS) red_in[i] = 0ull;
             if (tid < a.cs) {
                 hc_rb[tid] = dsmem_addr(qkv_in, tid);
                 hc_rb[8 + tid] = dsmem_addr(part_in, tid);
                 hc_rb[16 + tid] = dsmem_addr(red_in, tid);
+                hc_rb[24 + tid] = dsmem_addr(&hc_mbar[0], tid);
+                hc_rb[32 + tid] = dsmem_addr(&hc_mbar[1], tid);
             }
         }
     }
@@ -1505,7 +1598,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 load_cols(ly.b[MK_PROJ], bproj);
                 if (is_head) {
                     // ---- LN1 folded into this CTA's q, k, v columns of head hh -------
-                    mk_row_moments<MR>(xres, D, scr + 384);
+                    // (row moments: the previous layer's x gather, or here at layer 0)
+                    if (l == 0) mk_row_moments<MR>(xres, D, scr + 384);
                     MK_TRACE_L(1);
                     if (tid == 0) mk_ring_wait = 0;
                     it = mk_gemv_q4<MR>(xres, D, q3, s_geo[0], ring, full, empty, a.nstage, it, gscr, hc_ys, a.err,
@@ -1629,59 +1723,41 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                         pvred[g * hd + d] = av0 + av1;
                         cons_sync();
                         if (m == 0) MK_TRACE_L(21);
-                        const uint32_t poff = (uint32_t)(((buf * cs + rk) * MR + m) * ps) * 8u;
+                        // this row's partial (max, sum, p.V) into the copies' source
                         if (tid < hd) {
                             float A = 0.f;
                             for (int gg = 0; gg < ng; gg++) A += pvred[gg * hd + tid];
-                            for (int q = 0; q < cs; q++) dsmem_st_pair(hc_rb[8 + q] + poff + 8u * (2 + tid), A, xtag);
+                            part_out[m * ps + 2 + tid] = A;
                         } else if (tid == hd) {
-                            for (int q = 0; q < cs; q++) {
-                                dsmem_st_pair(hc_rb[8 + q] + poff, nk > 0 ? M : -INFINITY, xtag);
-                                dsmem_st_pair(hc_rb[8 + q] + poff + 8u, nk > 0 ? S : 0.f, xtag);
-                            }
+                            part_out[m * ps] = nk > 0 ? M : -INFINITY;
+                            part_out[m * ps + 1] = nk > 0 ? S : 0.f;
                         }
+                        fence_async_smem();
                         cons_sync();
                     }
+                    // this CTA's partials to every cluster CTA: one bulk copy each,
+                    // completing on the receiver's mbar[0] (one phase per round)
+                    if (tid < cs)
+                        bulk_s2c(hc_rb[8 + tid] + (uint32_t)(rk * MR * ps) * 4u, part_out, (uint32_t)(MR * ps) * 4u,
+                                 hc_rb[24 + tid]);
                     MK_TRACE_L(4);
-                    {
-                        // every pushed word of every rank and row (the padding words
-                        // past hd + 2 are never written)
-                        const unsigned long long* pb = part_in + buf * cs * MR * ps;
-                        for (int i = tid; i < cs * MR * ps; i += MK_CONS) {
-                            if (i % ps >= hd + 2) continue;
-                            const volatile unsigned long long* pw = pb + i;
-                            if ((uint32_t)(*pw >> 32) == xtag) continue;
-                            const unsigned long long t0 = gtimer();
-                            for (int k = 1; (uint32_t)(*pw >> 32) != xtag; k++) {
-                                if (s_abort) break;
-                                if ((k & 63) == 0 && ld_relaxed_i32(a.err) != 0) {
-                                    s_abort = 1;
-                                    break;
-                                }
-                                if (gtimer() - t0 > mk_wait_ns) {
-                                    atomicExch(a.err, 5);
-                                    s_abort = 1;
-                                    break;
-                                }
-                            }
-                        }
-                    }
+                    if (tid == 0) mbar_expect_tx(&hc_mbar[0], (uint32_t)(cs * MR * ps) * 4u);
+                    wait_cluster_bar(&hc_mbar[0], rnd & 1u, a.err, &s_abort);
                     MK_TRACE_L(5);
                     if (cons_sync_or(s_abort)) return;
                     // ---- combine the cluster's partials -> ctx of head hh -------------
                     for (int p = tid; p < MR * hd; p += MK_CONS) {
                         const int m = p >> lhd, dd = p & (hd - 1);
-                        const unsigned long long* pr = part_in + (buf * cs * MR + m) * ps;
-                        auto val = [](unsigned long long w) { return __uint_as_float((uint32_t)w); };
+                        const float* pr = part_in + m * ps;  // rank q's row m at pr + q * MR * ps
                         float Ms = -INFINITY;
-                        for (int q = 0; q < cs; q++) Ms = fmaxf(Ms, val(pr[q * MR * ps]));
+                        for (int q = 0; q < cs; q++) Ms = fmaxf(Ms, pr[q * MR * ps]);
                         float ls = 0.f, A = 0.f;
                         for (int q = 0; q < cs; q++) {
-                            const unsigned long long* pq = pr + q * MR * ps;
-                            const float mq = val(pq[0]);
+                            const float* pq = pr + q * MR * ps;
+                            const float mq = pq[0];
                             const float w = mq == -INFINITY ? 0.f : __expf(mq - Ms);
-                            ls += val(pq[1]) * w;
-                            A += val(pq[2 + dd]) * w;
+                            ls += pq[1] * w;
+                            A += pq[2 + dd] * w;
                         }
                         ctxs[p] = A / ls;
                     }
@@ -1701,20 +1777,16 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 // ---- x2 = x + attention projection; LN2 -> fc -> GELU -> proj2 ------
                 const float ffS = tid < J ? __ldg(ly.fold[1] + 2 * (j0 + tid)) : 0.f;  // folded LN2 of fc column
                 const float ffB = tid < J ? __ldg(ly.fold[1] + 2 * (j0 + tid) + 1) : 0.f;
-                acc_gather(accx2, act, MR * D, (uint32_t)(nhead / cs), a.err, &s_abort);
-                cons_sync();
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const int n = tid + k * MK_CONS;
-                    if (n < D)
-                        for (int m = 0; m < MR; m++) x2res[m * D + n] = xres[m * D + n] + (act[m * D + n] + bproj[k]);
-                }
+                // x2 = x + (projection + bias), with LN2's row moments (LN2 itself is
+                // folded into fc)
+                acc_gather_res<MR>(accx2, x2res, xres, D, bproj[0], bproj[1], bproj[2], bproj[3],
+                                   (uint32_t)(nhead / cs), scr + 384, a.err, &s_abort);
                 MK_TRACE_L(8);
                 if (cons_sync_or(s_abort)) return;
                 float bproj2[4];
                 load_cols(ly.b[MK_PROJ2], bproj2);
-                mk_row_moments<MR>(x2res, D, scr + 384);  // LN2 statistics; LN2 itself is folded into fc
                 MK_TRACE_L(11);
+                float* red_out = act;  // [cs][MR][wp] (MR <= 2): this CTA's proj2 partials by owner rank
                 if (J > 0) {
                     float* hb = act + MR * D;  // [MR][J]
                     if (tid == 0) mk_ring_wait = 0;
@@ -1731,30 +1803,30 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     MK_TRACE_L(13);
                     if (tid == 0) mk_ring_wait = 0;
                     it = mk_gemv_wide_q4<MR>(hb, J, D, s_hci[5], ring, full, empty, a.nstage, it,
-                                             MR <= 2 ? nullptr : accx, hc_rb + 16, rk, wp, (uint32_t)rnd + 1u, a.err,
-                                             &s_abort);
+                                             MR <= 2 ? nullptr : accx, red_out, wp, a.err, &s_abort);
                     if (l == 0) MK_TRACE_DUR(17, mk_ring_wait);
                 } else if (MR > 2) {
                     for (int p = tid; p < MR * D; p += MK_CONS) acc_add(accx + p, acc_term(0.f));
                 } else {
-                    // no hidden units here: zeros for every column block of the cluster
-                    for (int m = 0; m < MR; m++)
-                        for (int c = tid; c < D; c += MK_CONS) {
-                            const int own = c / wp;
-                            dsmem_st_pair(hc_rb[16 + own] + (uint32_t)((rk * MR + m) * wp + (c - own * wp)) * 8u, 0.f,
-                                          (uint32_t)rnd + 1u);
-                        }
+                    for (int p = tid; p < MR * D; p += MK_CONS) red_out[p] = 0.f;  // no hidden units here
                 }
                 if (MR <= 2) {
-                    // this CTA's column block: the cluster's partials summed in rank order,
-                    // one fixed-point term per cluster and column
-                    wait_tags_smem(red_in, cs * MR * wp, (uint32_t)rnd + 1u, a.err, &s_abort);
-                    if (cons_sync_or(s_abort)) return;  // every word verified before any is summed
+                    // each column block to its owner (one bulk copy per cluster CTA,
+                    // completing on the owner's mbar[1]); this CTA's block: the
+                    // cluster's partials summed in rank order, one fixed-point term
+                    // per cluster and column
+                    fence_async_smem();
+                    cons_sync();
+                    if (tid < cs)
+                        bulk_s2c(hc_rb[16 + tid] + (uint32_t)(rk * MR * wp) * 4u, red_out + tid * MR * wp,
+                                 (uint32_t)(MR * wp) * 4u, hc_rb[32 + tid]);
+                    if (tid == 0) mbar_expect_tx(&hc_mbar[1], (uint32_t)(cs * MR * wp) * 4u);
+                    wait_cluster_bar(&hc_mbar[1], rnd & 1u, a.err, &s_abort);
+                    if (cons_sync_or(s_abort)) return;
                     for (int m = 0; m < MR; m++)
                         for (int c = tid; c < wp; c += MK_CONS) {
                             float sum = 0.f;
-                            for (int q = 0; q < cs; q++)
-                                sum += __uint_as_float((uint32_t)red_in[(q * MR + m) * wp + c]);
+                            for (int q = 0; q < cs; q++) sum += red_in[(q * MR + m) * wp + c];
                             acc_add(accx + (size_t)m * D + rk * wp + c, acc_term(sum));
                         }
                 }
@@ -1765,14 +1837,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     fqB = __ldg(hc_lay[l + 1].fold[0] + 2 * qcol + 1);
                 }
                 // ---- x of the next layer (every CTA) --------------------------------
-                acc_gather(accx, act, MR * D, (uint32_t)(MR <= 2 ? nW / cs : nW), a.err, &s_abort);
-                cons_sync();
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const int n = tid + k * MK_CONS;
-                    if (n < D)
-                        for (int m = 0; m < MR; m++) xres[m * D + n] = x2res[m * D + n] + (act[m * D + n] + bproj2[k]);
-                }
+                // x = x2 + (MLP output + bias), with the next layer's LN1 row moments
+                acc_gather_res<MR>(accx, xres, x2res, D, bproj2[0], bproj2[1], bproj2[2], bproj2[3],
+                                   (uint32_t)(MR <= 2 ? nW / cs : nW), scr + 384, a.err, &s_abort);
                 if (cons_sync_or(s_abort)) return;
                 MK_TRACE_L(10);
                 if (l < 24) MK_TRACE(33 + l);
@@ -2700,6 +2767,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         const unsigned long long t0 = gtimer();
         while (!mbar_try_cluster(&hc_mbar[4], 0))
             if (gtimer() - t0 > 4 * mk_wait_ns) break;
+        // after an abort a cluster CTA's last bulk copy into this CTA's shared
+        // memory may not have been waited for: let it land before leaving
+        if (s_abort) {
+            const unsigned long long t1 = gtimer();
+            while (gtimer() - t1 < 50000ull) __nanosleep(1000);
+        }
     }
 }
 
