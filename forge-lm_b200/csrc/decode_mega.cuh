@@ -48,6 +48,7 @@ __shared__ unsigned long long mk_wait_ns;
 // The launch's ring stage size in bytes (MkArgs::stage_bytes; MK_STAGE on
 // the column-strip path), set with mk_wait_ns.
 __shared__ int mk_sbytes;
+
 // Traced runs: thread 0's time spent waiting for ring stages (reset per phase).
 __shared__ unsigned long long mk_ring_wait;
 // Traced runs: thread 0's stamps inside the last column GEMV (start, after
@@ -740,18 +741,16 @@ FB2_DEV void mk_row_moments(const float* x, int D, float* slots) {
     }
 }
 // Mean and 1/sqrt(biased variance + eps) of row m from the partial moments
-// (LayerNorm statistics, CpuBackend.cs:377-398; variance as E[x^2] - mean^2
-// in double).
+// (LayerNorm statistics, CpuBackend.cs:377-398; variance as E[x^2] - mean^2,
+// in float like the per-warp partial sums it combines, tree-summed: this runs
+// on the critical path between a GEMV's partial sums and its epilogue).
 FB2_DEV void mk_row_stats(const float* slots, int m, int D, float& mu, float& rstd) {
-    double s1 = 0.0, s2 = 0.0;
-#pragma unroll
-    for (int w = 0; w < 8; w++) {
-        s1 += slots[m * 16 + w];
-        s2 += slots[m * 16 + 8 + w];
-    }
-    const double mean = s1 / D, var = s2 / D - mean * mean;
-    mu = (float)mean;
-    rstd = 1.0f / sqrtf((float)(var > 0.0 ? var : 0.0) + kLnEps);
+    const float* a = slots + m * 16;
+    const float s1 = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+    const float s2 = ((a[8] + a[9]) + (a[10] + a[11])) + ((a[12] + a[13]) + (a[14] + a[15]));
+    const float mean = s1 / (float)D, var = s2 / (float)D - mean * mean;
+    mu = mean;
+    rstd = 1.0f / sqrtf(fmaxf(var, 0.f) + kLnEps);
 }
 
 // Two-pass LayerNorm of MR rows of length D <= 2048 from src into dst
@@ -998,18 +997,19 @@ __device__ __noinline__ uint32_t mk_gemv_cols(const float* actv, int K, int w, u
 // launch: R rows per ring stage; thread (g, q) = (tid >> lgp, tid & (2^lgp - 1))
 // reads quad q of rows g, g + G, ... (threads with q >= w / 4 or g >= G idle).
 struct MkGeo {
-    int R, G, lgp;
+    int R, G, lgp, mc;  // mc: rows of partials per pass through the 4096-float scratch
 };
 FB2_DEV MkGeo mk_geo(int w, int K, int MR) {
-    MkGeo g{0, 1, 0};
+    MkGeo g{0, 1, 0, 1};
     if (w <= 0) return g;
     g.R = strip_rows(w, K);
     const int nq = w >> 2;
     while ((1 << g.lgp) < nq) g.lgp++;
-    g.G = MK_CONS >> g.lgp;
-    const int gcap = 4096 / (w * MR);
-    if (g.G > gcap) g.G = gcap;
-    if (g.G < 1) g.G = 1;
+    g.G = MK_CONS >> g.lgp;  // lgp <= 8: w <= 1024
+    const int P = g.lgp <= 5 ? 8 : g.G;
+    g.mc = 4096 / (P * w);
+    if (g.mc > MR) g.mc = MR;
+    if (g.mc < 1) g.mc = 1;
     return g;
 }
 
@@ -1017,14 +1017,15 @@ FB2_DEV MkGeo mk_geo(int w, int K, int MR) {
 // (g, q) reads column quad q of rows g, g + G, ... as float4 (consecutive
 // threads read consecutive 16-byte words of a stage row), U rows in flight
 // per pass (the loop is bound by shared-memory latency, not bandwidth).
-// Partials: for w <= 128 the groups of a warp are summed with shuffles and
-// the 8 warp partials of an output through scr (MR * 8 * w floats); wider
-// slices put all G group partials through scr (4096 floats).  Either way
-// the order is fixed.  ys[MR*w] holds the results behind a barrier.
+// Partials: for w <= 128 the groups of a warp are summed with shuffles and the
+// 8 warp partials of an output go through scr; wider slices put their G
+// (<= 4) group partials there.  Rows go through scr (4096 floats) in chunks;
+// the summation order is fixed.  ys[MR*w] holds the results behind a barrier.
 // With `mslots` set, warp 7 also turns the per-warp moments mslots (see
 // mk_row_moments, rows of length K) into stats[2m] = mean, stats[2m+1] =
 // 1/sqrt(var + eps) while the partials are summed.  No division in the
-// loops: the geometry comes precomputed.
+// loops: the geometry comes precomputed.  Loops stay rolled: the persistent
+// kernel runs this once per phase, so code size costs instruction fetches.
 template <int MR>
 __device__ __noinline__ uint32_t mk_gemv_q4(const float* actv, int K, int w, MkGeo geo, unsigned char* ring,
                                             uint64_t* full, uint64_t* empty, int nstage, uint32_t it, float* scr4k,
@@ -1035,17 +1036,18 @@ __device__ __noinline__ uint32_t mk_gemv_q4(const float* actv, int K, int w, MkG
     const int R = geo.R, G = geo.G, nq = w >> 2;
     const int q = tid & ((1 << geo.lgp) - 1), g = tid >> geo.lgp;
     const bool valid = g < G && q < nq;
-    const bool shfl = geo.lgp <= 5 && MR * 8 * w <= 4096;
     MK_GEMV_STAMP(0);
     float4 a0[MR], a1[MR];
 #pragma unroll
     for (int m = 0; m < MR; m++) a0[m] = a1[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
     for (int r0 = 0; r0 < K; r0 += R) {
         const int rows = min(R, K - r0);
         wait_full(full, it, nstage, err, abort_flag);
         const float4* st = reinterpret_cast<const float4*>(ring + (size_t)rp_stage(it) * mk_sbytes);
         if (valid) {
             const float* av = actv + r0;
+#pragma unroll 1
             for (int r = g; r < rows; r += U * G) {
                 float4 wv[U];
 #pragma unroll
@@ -1074,9 +1076,11 @@ __device__ __noinline__ uint32_t mk_gemv_q4(const float* actv, int K, int w, MkG
 #pragma unroll
     for (int m = 0; m < MR; m++)
         p[m] = make_float4(a0[m].x + a1[m].x, a0[m].y + a1[m].y, a0[m].z + a1[m].z, a0[m].w + a1[m].w);
-    int P;  // partials per output
-    if (shfl) {
+    int P, pidx;  // partials per output; this thread's partial index
+    bool writer;
+    if (geo.lgp <= 5) {
         // the 32 >> lgp groups of this warp (lanes differing in bits lgp..4)
+#pragma unroll 1
         for (int o = 16; o >= (1 << geo.lgp); o >>= 1)
 #pragma unroll
             for (int m = 0; m < MR; m++) {
@@ -1085,32 +1089,42 @@ __device__ __noinline__ uint32_t mk_gemv_q4(const float* actv, int K, int w, MkG
                 p[m].z += __shfl_xor_sync(0xffffffffu, p[m].z, o);
                 p[m].w += __shfl_xor_sync(0xffffffffu, p[m].w, o);
             }
-        if (lane < (1 << geo.lgp) && q < nq)
-#pragma unroll
-            for (int m = 0; m < MR; m++) reinterpret_cast<float4*>(scr4k)[(((m << 3) + warp) * w >> 2) + q] = p[m];
         P = 8;
+        pidx = warp;
+        writer = lane < (1 << geo.lgp) && q < nq;
     } else {
-        if (valid)
-#pragma unroll
-            for (int m = 0; m < MR; m++) reinterpret_cast<float4*>(scr4k)[((m * G + g) * w >> 2) + q] = p[m];
         P = G;
+        pidx = g;
+        writer = valid;
     }
-    cons_sync();
+    const int mc = geo.mc;
+#pragma unroll 1
+    for (int m0 = 0; m0 < MR; m0 += mc) {
+        if (writer)
 #pragma unroll
-    for (int m = 0; m < MR; m++)
-        for (int c = tid; c < w; c += MK_CONS) {
-            const float* rp = scr4k + (m * P) * w + c;
-            float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
-            int gg = 0;
-            for (; gg + 3 < P; gg += 4) {
-                t0 += rp[gg * w];
-                t1 += rp[(gg + 1) * w];
-                t2 += rp[(gg + 2) * w];
-                t3 += rp[(gg + 3) * w];
+            for (int m = 0; m < MR; m++)
+                if (m >= m0 && m < m0 + mc)
+                    reinterpret_cast<float4*>(scr4k)[(((m - m0) * P + pidx) * w >> 2) + q] = p[m];
+        cons_sync();
+#pragma unroll 1
+        for (int mm = 0; mm < mc && m0 + mm < MR; mm++)
+#pragma unroll 1
+            for (int c = tid; c < w; c += MK_CONS) {
+                const float* rp = scr4k + (mm * P) * w + c;
+                float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+                int gg = 0;
+#pragma unroll 1
+                for (; gg + 3 < P; gg += 4) {
+                    t0 += rp[gg * w];
+                    t1 += rp[(gg + 1) * w];
+                    t2 += rp[(gg + 2) * w];
+                    t3 += rp[(gg + 3) * w];
+                }
+                for (; gg < P; gg++) t0 += rp[gg * w];
+                ys[(m0 + mm) * w + c] = (t0 + t1) + (t2 + t3);
             }
-            for (; gg < P; gg++) t0 += rp[gg * w];
-            ys[m * w + c] = (t0 + t1) + (t2 + t3);
-        }
+        if (m0 + mc < MR) cons_sync();  // scr is rewritten by the next pass
+    }
     if (mslots && warp == 7 && lane < MR) mk_row_stats(mslots, lane, K, stats[2 * lane], stats[2 * lane + 1]);
     cons_sync();
     MK_GEMV_STAMP(2);
@@ -1332,6 +1346,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
         s_abort = 0;
         mk_wait_ns = a.timeout_ns;
         mk_sbytes = a.stage_bytes;
+
         for (int i = 0; i < a.nstage; i++) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 8);
@@ -1597,6 +1612,24 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 float bproj[4];
                 load_cols(ly.b[MK_PROJ], bproj);
                 if (is_head) {
+                    // the cached K and V rows of this CTA's keys (written by earlier
+                    // steps), pulled into L1 while the q/k/v GEMV runs (4 lines of
+                    // 128 bytes per key at head_dim 64; read below with L1-cached loads)
+                    for (int m = 0; m < MR; m++) {
+                        const int pos = pos_of(m, s), T = pos + 1;
+                        const int k0 = (rk * T) >> lcs;
+                        const int kend = min(((rk + 1) * T) >> lcs, pos);
+                        const int lpr = hd >> 5;  // 128-byte lines per row
+                        const char* kb = reinterpret_cast<const char*>(
+                            a.kv + (size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
+                            (size_t)hh * a.ctx * hd);
+                        for (int i = tid; i < 2 * lpr * (kend - k0); i += MK_CONS) {
+                            const int key = k0 + (i >> (lhd - 4)), part = i & (2 * lpr - 1);
+                            const char* ln = kb + (part >= lpr ? (size_t)a.v_offset * 4 : 0) +
+                                             ((size_t)key * hd) * 4 + (size_t)(part % lpr) * 128;
+                            asm volatile("prefetch.global.L1 [%0];" ::"l"(ln));
+                        }
+                    }
                     // ---- LN1 folded into this CTA's q, k, v columns of head hh -------
                     // (row moments: the previous layer's x gather, or here at layer 0)
                     if (l == 0) mk_row_moments<MR>(xres, D, scr + 384);
@@ -1626,24 +1659,6 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                                 for (int q = 0; q < cs; q++) dsmem_st_pair(hc_rb[q] + off, v, xtag);
                         }
                     MK_TRACE_L(19);
-                    // the cached K and V rows of this CTA's keys, pulled into L1 while
-                    // the cluster's q/k/v parts arrive (4 lines of 128 bytes per key
-                    // at head_dim 64; they are read below with L1-cached loads)
-                    for (int m = 0; m < MR; m++) {
-                        const int pos = pos_of(m, s), T = pos + 1;
-                        const int k0 = (rk * T) >> lcs;
-                        const int kend = min(((rk + 1) * T) >> lcs, pos);
-                        const int lpr = hd >> 5;  // 128-byte lines per row
-                        const char* kb = reinterpret_cast<const char*>(
-                            a.kv + (size_t)s_slot[m] * a.kv_slot_stride + (size_t)l * a.kv_layer_stride +
-                            (size_t)hh * a.ctx * hd);
-                        for (int i = tid; i < 2 * lpr * (kend - k0); i += MK_CONS) {
-                            const int key = k0 + (i >> (lhd - 4)), part = i & (2 * lpr - 1);
-                            const char* ln = kb + (part >= lpr ? (size_t)a.v_offset * 4 : 0) +
-                                             ((size_t)key * hd) * 4 + (size_t)(part % lpr) * 128;
-                            asm volatile("prefetch.global.L1 [%0];" ::"l"(ln));
-                        }
-                    }
                     wait_tags_smem(qkv_in + buf * cs * MR * q3, cs * MR * q3, xtag, a.err, &s_abort);
                     MK_TRACE_L(3);
                     if (cons_sync_or(s_abort)) return;
@@ -1668,7 +1683,18 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                             if (j < pos) {
                                 const float4* q4 = reinterpret_cast<const float4*>(hscr);
                                 const float4* kr = reinterpret_cast<const float4*>(kbase + (size_t)j * hd);
-                                for (int e0 = 0; e0 < hd / 4; e0 += 4) {
+                                int e0 = 0;
+                                for (; e0 + 8 <= hd / 4; e0 += 8) {  // 8 loads in flight (one L2 trip on a miss)
+                                    float4 kv4[8];
+#pragma unroll
+                                    for (int e = 0; e < 8; e++) kv4[e] = __ldca(kr + e0 + e);
+#pragma unroll
+                                    for (int e = 0; e < 8; e++) {
+                                        const float4 qv = q4[e0 + e];
+                                        d += qv.x * kv4[e].x + qv.y * kv4[e].y + qv.z * kv4[e].z + qv.w * kv4[e].w;
+                                    }
+                                }
+                                for (; e0 < hd / 4; e0 += 4) {
                                     float4 kv4[4];
 #pragma unroll
                                     for (int e = 0; e < 4; e++) kv4[e] = __ldca(kr + e0 + e);
