@@ -572,6 +572,64 @@ FB2_DEV int cons_excl_scan(int v, int* wsum, int& total) {
     total = tot;
     return base + x - v;
 }
+// The k-th largest (in float_key order) of the slices' top values tops[ns][4]
+// (ns <= 256 slices, 1 <= k <= 4 ns), with ties counted: the key with fewer
+// than k keys above it and at least k at or above it.  When k <= ns the k-th
+// largest of the slices' first entries bounds it from below (a subset's k-th
+// largest), so only the entries at or above that bound are ranked.
+// kbuf: 256 + 4 * ns words; st: 10 ints.  Ends behind a barrier.
+__device__ __noinline__ float cons_kth_tops(const float* tops, int ns, int k, uint32_t* kbuf, int* st) {
+    const int tid = threadIdx.x;
+    uint32_t* k1 = kbuf;        // [256] keys of the first entries
+    uint32_t* cand = kbuf + 256;  // [4 ns] candidate keys
+    uint32_t bound = 0u;          // the smallest key: everything is a candidate
+    if (k <= ns) {
+        const uint32_t mine = tid < ns ? float_key(tops[tid * 4]) : 0u;
+        k1[tid] = mine;
+        cons_sync();
+        if (tid < ns) {
+            int gt = 0, ge = 0;
+            for (int j = 0; j < ns; j++) {
+                const uint32_t kj = k1[j];
+                gt += kj > mine;
+                ge += kj >= mine;
+            }
+            if (gt < k && ge >= k) st[0] = (int)mine;  // every such thread writes the same key
+        }
+        cons_sync();
+        bound = (uint32_t)st[0];
+    }
+    uint32_t ck[4];
+    int c = 0;
+    if (tid < ns)
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const uint32_t key = float_key(tops[tid * 4 + q]);
+            ck[q] = key;
+            c += key >= bound;
+        }
+    int C;
+    const int off = cons_excl_scan(c, st + 2, C);
+    if (tid < ns) {
+        int o = off;
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+            if (ck[q] >= bound) cand[o++] = ck[q];
+    }
+    cons_sync();
+    for (int i = tid; i < C; i += MK_CONS) {
+        const uint32_t mine = cand[i];
+        int gt = 0, ge = 0;
+        for (int j = 0; j < C; j++) {
+            const uint32_t kj = cand[j];
+            gt += kj > mine;
+            ge += kj >= mine;
+        }
+        if (gt < k && ge >= k) st[1] = (int)mine;
+    }
+    cons_sync();
+    return key_float((uint32_t)st[1]);
+}
 // Warp 0: the bin (counted from the top of a 256-bin histogram) that holds the
 // k-th largest key, and the count in the bins above it.
 FB2_DEV void radix_pick(const uint32_t* hist, int kk, int& bin, int& above_out) {
@@ -609,47 +667,6 @@ FB2_DEV void radix_pick(const uint32_t* hist, int kk, int& bin, int& above_out) 
     if (bin < 0) bin = 0;
 }
 
-// The k-th largest of vals[0..n) (ties counted, as "fewer than k strictly
-// larger"), by the consumer threads: an exact 4-pass radix select on the
-// order-preserving keys.  hist = 256 words, st = 3 ints of shared scratch;
-// every consumer thread returns the value.  k in [1, n].
-__device__ __noinline__ float cons_kth_largest(const float* vals, int n, int k, uint32_t* hist, int* st) {
-    const int tid = threadIdx.x;
-    if (tid == 0) {
-        st[0] = 0;  // prefix
-        st[1] = 0;  // mask
-        st[2] = k;  // rank still to find within the prefix
-    }
-    for (int shift = 24; shift >= 0; shift -= 8) {
-        hist[tid] = 0u;
-        cons_sync();
-        const uint32_t prefix = (uint32_t)st[0], mask = (uint32_t)st[1];
-        // one shared atomic per distinct bin per warp: the leading passes put
-        // most keys in one bin, where per-lane atomics would serialize
-        for (int base = 0; base < n; base += MK_CONS) {
-            const int i = base + tid;
-            int bin = -1;
-            if (i < n) {
-                const uint32_t key = float_key(vals[i]);
-                if ((key & mask) == prefix) bin = (int)((key >> shift) & 255u);
-            }
-            const unsigned peers = __match_any_sync(0xffffffffu, bin);
-            if (bin >= 0 && (int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
-        }
-        cons_sync();
-        if ((tid >> 5) == 0) {
-            int bin, above;
-            radix_pick(hist, st[2], bin, above);
-            if (tid == 0) {
-                st[0] = (int)(prefix | ((uint32_t)bin << shift));
-                st[1] = (int)(mask | (255u << shift));
-                st[2] -= above;
-            }
-        }
-        cons_sync();
-    }
-    return key_float((uint32_t)st[0]);
-}
 
 // A consumer's ring position: stage index in the low 16 bits, the stage's
 // phase parity in bit 16 (advanced without a division).
@@ -2524,8 +2541,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                 // lower bound of the row's k-th largest: the k-th largest of the
                 // slices' top values (a subset of the row)
                 const int ntops = 4 * nW;
-                const float tlo = cons_kth_largest(tops, ntops, min(sp.top_k, ntops), reinterpret_cast<uint32_t*>(scr),
-                                                   misc + 24);
+                const float tlo =
+                    cons_kth_tops(tops, nW, min(sp.top_k, ntops), reinterpret_cast<uint32_t*>(iscr + 768), misc + 24);
                 if (m == 0) MK_TRACE(58);
                 // stage every candidate >= the bound: from the header when the
                 // slice's 4th largest is below the bound (then every such entry
