@@ -43,7 +43,8 @@ FORGE_220M = dict(vocab_size=16384, context_length=1024, d_model=1024, n_layers=
 # Measured DRAM traffic of the dominant kernel is read from a record written
 # by `bench.py --record-traffic <ncu csv>` (the one-pass launch-list capture
 # with dram__bytes_read.sum and dram__bytes_write.sum); it is used only when
-# the record names the SHA-256 of the library file loaded now, else null.
+# the record names the source fingerprint the loaded library was built from
+# (the build writes it beside the library), else null.
 TRAFFIC_RECORD = os.path.join(ROOT, "profiles", "traffic_record.json")
 WEIGHT_SEED = 1234
 
@@ -298,25 +299,27 @@ def run_reference(args, wl):
     print(json.dumps(line), flush=True)
 
 
-def lib_sha256(path: str) -> str:
-    import hashlib
-    h = hashlib.sha256()
-    with open(path, "rb") as f:
-        for chunk in iter(lambda: f.read(1 << 20), b""):
-            h.update(chunk)
-    return h.hexdigest()
+def build_fingerprint(lib_path: str):
+    """The source fingerprint the library file was built from (written beside
+    it by the build), or None."""
+    try:
+        with open(lib_path + ".flags") as f:
+            return json.load(f).get("sources_sha256")
+    except (OSError, ValueError):
+        return None
 
 
 def recorded_traffic(workload: str, lib_path: str):
     """DRAM bytes per decode step from the traffic record, if it was measured
-    on this exact library file; else None."""
+    on a library built from the same sources and flags; else None."""
     try:
         with open(TRAFFIC_RECORD) as f:
             rec = json.load(f)
     except (OSError, ValueError):
         return None
     r = rec.get(workload)
-    if not r or r.get("lib_sha256") != lib_sha256(lib_path):
+    fp = build_fingerprint(lib_path)
+    if not r or fp is None or r.get("build_sha256") != fp:
         return None
     return float(r["dram_bytes_per_step"])
 
@@ -324,7 +327,7 @@ def recorded_traffic(workload: str, lib_path: str):
 def record_traffic(csv_path: str, workload: str, kernel: str, steps_per_launch: int) -> None:
     """Writes the traffic record from an ncu --csv capture of one or more
     launches of `kernel` with dram__bytes_read.sum and dram__bytes_write.sum
-    (bytes, or the unit ncu prints), keyed by the library's SHA-256."""
+    (bytes, or the unit ncu prints), keyed by the build's source fingerprint."""
     import csv
     import __graft_entry__ as graft
     unit = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "KB": 1e3, "MB": 1e6, "GB": 1e9}
@@ -345,7 +348,7 @@ def record_traffic(csv_path: str, workload: str, kernel: str, steps_per_launch: 
     lib = graft.load_package().library_path()
     rec[workload] = {"kernel": kernel, "launches": len(per_launch), "steps_per_launch": steps_per_launch,
                      "dram_bytes_per_step": sum(per_launch.values()) / len(per_launch) / steps_per_launch,
-                     "lib_sha256": lib_sha256(lib)}
+                     "build_sha256": build_fingerprint(lib)}
     with open(TRAFFIC_RECORD, "w") as f:
         json.dump(rec, f, indent=1)
     print(json.dumps(rec[workload]))

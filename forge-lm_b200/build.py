@@ -9,6 +9,8 @@ No fast-math: the sampler's division and exponentials must round as IEEE.
 """
 from __future__ import annotations
 
+import hashlib
+import json
 import os
 import shutil
 import subprocess
@@ -67,14 +69,43 @@ def _flags() -> list[str]:
     return flags
 
 
-def build(verbose: bool = False, force: bool = False) -> str:
-    gen_fixups(verbose)
+def _sources() -> list[str]:
     sources = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh", ".hpp"))]
     sources.append(os.path.join(ROOT, "include", "forge_b200.h"))
     sources.append(os.path.join(GEN, "expf_fixups.inc"))
+    return sorted(sources)
+
+
+def source_fingerprint(flags: list[str], sources: list[str]) -> str:
+    """SHA-256 of the nvcc flags and every source file (path and contents):
+    names the build independently of the binary, which nvcc does not
+    reproduce byte for byte."""
+    h = hashlib.sha256(" ".join(flags).encode())
+    for path in sources:
+        h.update(os.path.relpath(path, ROOT).encode())
+        with open(path, "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()
+
+
+def stamp_path(lib: str = LIB) -> str:
+    """The JSON beside the library: the flags and source fingerprint it was built from."""
+    return lib + ".flags"
+
+
+def read_stamp(lib: str = LIB) -> dict:
+    try:
+        with open(stamp_path(lib)) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def build(verbose: bool = False, force: bool = False) -> str:
+    gen_fixups(verbose)
+    sources = _sources()
     flags = _flags()
-    stamp = LIB + ".flags"
-    same_flags = os.path.exists(stamp) and open(stamp).read() == " ".join(flags)
+    same_flags = read_stamp().get("flags") == flags
     if not force and same_flags and not _newer(LIB, sources):
         return LIB
     cmd = [_nvcc(), *flags, "-shared", "-o", LIB + ".tmp", os.path.join(CSRC, "forge_b200.cu")]
@@ -82,8 +113,8 @@ def build(verbose: bool = False, force: bool = False) -> str:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)
     os.replace(LIB + ".tmp", LIB)
-    with open(stamp, "w") as f:
-        f.write(" ".join(flags))
+    with open(stamp_path(), "w") as f:
+        json.dump({"flags": flags, "sources_sha256": source_fingerprint(flags, sources)}, f)
     return LIB
 
 

@@ -4,9 +4,13 @@ decode step streams are every parameter except pos_emb (one row of it per
 sequence goes with the sequence's bytes), and one sliding-window step is the
 block projections for every row, causal attention over T(T+1)/2 pairs, and
 the head on the last row."""
+import os
+
 import numpy as np
 
 import bench
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def test_weight_bytes_are_the_parameters_a_step_streams(pkg):
@@ -55,15 +59,34 @@ def test_reference_step_flops_and_cpu_sample_on_a_tiny_workload(O):
     assert p["first_mismatch"] == 0 and p["ids_equal"] == 5
 
 
-def test_traffic_record_is_keyed_by_the_library_file(tmp_path, monkeypatch):
-    """A DRAM-traffic figure is reported only for the library file it was
-    measured on."""
+def test_traffic_record_is_keyed_by_the_build(tmp_path, monkeypatch):
+    """A DRAM-traffic figure is reported only for a library built from the
+    sources and flags it was measured on (the build's fingerprint, written
+    beside the library)."""
     lib = tmp_path / "lib.so"
-    lib.write_bytes(b"build A")
+    lib.write_bytes(b"binary")
+    stamp = tmp_path / "lib.so.flags"
+    stamp.write_text('{"flags": [], "sources_sha256": "aaa"}')
     rec = tmp_path / "traffic.json"
     monkeypatch.setattr(bench, "TRAFFIC_RECORD", str(rec))
-    rec.write_text('{"c2": {"dram_bytes_per_step": 123.0, "lib_sha256": "%s"}}' % bench.lib_sha256(str(lib)))
+    rec.write_text('{"c2": {"dram_bytes_per_step": 123.0, "build_sha256": "aaa"}}')
     assert bench.recorded_traffic("c2", str(lib)) == 123.0
     assert bench.recorded_traffic("c3", str(lib)) is None
-    lib.write_bytes(b"build B")
+    stamp.write_text('{"flags": [], "sources_sha256": "bbb"}')
     assert bench.recorded_traffic("c2", str(lib)) is None
+    stamp.unlink()
+    assert bench.recorded_traffic("c2", str(lib)) is None
+
+
+def test_build_fingerprint_follows_sources_and_flags(tmp_path):
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("fb2_build", os.path.join(ROOT, "forge-lm_b200", "build.py"))
+    b = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(b)
+    src = tmp_path / "k.cu"
+    src.write_text("int x;")
+    f1 = b.source_fingerprint(["-O3"], [str(src)])
+    assert f1 == b.source_fingerprint(["-O3"], [str(src)])
+    assert f1 != b.source_fingerprint(["-O2"], [str(src)])
+    src.write_text("int y;")
+    assert f1 != b.source_fingerprint(["-O3"], [str(src)])
