@@ -499,7 +499,7 @@ def main():
                     "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
                     "traffic": recorded_traffic(args.workload, pkg.library_path()) if default_wl else None,
                     "traffic_unit": "bytes per decode step: ncu dram__bytes_read.sum + dram__bytes_write.sum of the "
-                                    "workload's launch / its steps, recorded for this library file (else null)",
+                                    "workload's launch / its steps, recorded for this build (same source fingerprint; else null)",
                     "step_ms": step_ms, "algorithmic_bytes_per_step": bytes_step}
 
     # ---- e2e: the public host-buffer call, copies inside the timed region ----
