@@ -102,8 +102,9 @@ def test_c2_forge98m_persistent_kernel(pkg, O, forge98m):
     """BASELINE configs[1] exactly as the bench runs it: Forge-98M fp32, one
     sequence, prompt 64, 512 tokens at T 0.7, top-k 30, penalty 1.1,
     no-repeat-ngram 4, `new Random(1)`.  Every decode step runs inside the
-    persistent kernel (D 768: 148 column strips, 12 heads of attention units).
-    All 512 steps: logits within 1e-3, ids teacher-forced."""
+    persistent kernel (D 768: the head-cluster layout, 12 head clusters and 3
+    MLP clusters of 8 CTAs).  All 512 steps: logits within 1e-3, ids
+    teacher-forced."""
     cfg, params = forge98m
     wl = bench.WORKLOADS["c2"]
     prompt = bench.prompts_for(0, 1, wl["prompt_len"], cfg.vocab_size)[0]
