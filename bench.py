@@ -275,6 +275,27 @@ def parity_vs_cpu(device_ids, cpu_ids) -> dict:
             "first_mismatch": first, "reference": "oracle port of the reference CPU loop (sequence 0)"}
 
 
+def seqs_of(wl: dict, world: int, rank: int) -> tuple[int, int]:
+    """(first sequence, count) of this rank."""
+    if wl["seqs_total"]:
+        return shard(wl["seqs_total"], world, rank)
+    return rank * wl["seqs_per_gpu"], wl["seqs_per_gpu"]
+
+
+def workload_config(wl: dict, world: int) -> dict:
+    """The `config` object of a bench line (both arms print the same one)."""
+    m = wl["model"]
+    _, count = seqs_of(wl, world, 0)
+    plen = wl["prompt_len"]
+    wdt = wl.get("weight_dtype", "fp32")
+    return {"workload": wl["name"], "model": model_name(m),
+            "sequences_per_gpu": count, "prompt_len": plen if isinstance(plen, int) else list(plen),
+            "new_tokens": wl["new_tokens"], "weights": wdt,
+            "parallelism": f"request-parallel x{world} (independent sequences, no collective)",
+            "l2": f"inputs larger than L2: every decode step streams {weight_bytes(m, wdt) / 1e6:.0f} MB "
+                  f"of weights"}
+
+
 def run_reference(args, wl):
     rank, world, _ = dist_env()
     if rank != 0:
@@ -292,7 +313,7 @@ def run_reference(args, wl):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * secs / len(steps),
             "higher_is_better": True, "scaling": wl["scaling"], "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random weights and prompt ids)",
-            "config": {"workload": wl["name"], "sample": last["sample"]},
+            "config": workload_config(wl, world),
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": last["cores"], "cpu_model": last["cpu_model"],
                              "kind": "port", "sample": last["sample"], "full_run": last.get("full_run")},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -379,10 +400,7 @@ def main():
     pkg = graft.load_package()
     m = wl["model"]
     cfg = pkg.ModelConfig(**m)
-    if wl["seqs_total"]:
-        first, count = shard(wl["seqs_total"], world, rank)
-    else:
-        first, count = rank * wl["seqs_per_gpu"], wl["seqs_per_gpu"]
+    first, count = seqs_of(wl, world, rank)
     params = pkg.init_params(cfg, WEIGHT_SEED)
     wdt = wl.get("weight_dtype", "fp32")
     be = pkg.B200Backend(cfg, params, devices=[local], max_seqs=max(count, 1), weight_dtype=wdt)
@@ -540,12 +558,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": wl["scaling"], "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init weights, uniform-random prompt ids)",
-            "config": {"workload": wl["name"], "model": model_name(m),
-                       "sequences_per_gpu": count, "prompt_len": plen if isinstance(plen, int) else list(plen),
-                       "new_tokens": new, "weights": wdt,
-                       "parallelism": f"request-parallel x{world} (independent sequences, no collective)",
-                       "l2": f"inputs larger than L2: every decode step streams {weight_bytes(m, wdt) / 1e6:.0f} MB "
-                             f"of weights"},
+            "config": workload_config(wl, world),
             "roofline": roofline,
             "cpu_baseline": cpu,
             "parity": parity,

@@ -90,3 +90,21 @@ def test_build_fingerprint_follows_sources_and_flags(tmp_path):
     assert f1 != b.source_fingerprint(["-O2"], [str(src)])
     src.write_text("int y;")
     assert f1 != b.source_fingerprint(["-O3"], [str(src)])
+
+
+def test_reference_arm_prints_the_same_config(monkeypatch, capsys):
+    """Both arms' lines carry the same `config` object (the driver compares
+    them), whatever the rank count."""
+    import json
+    import types
+    fake = {"value": 1.0, "unit": "tokens/s", "cores": 1, "cpu_model": "x", "kind": "port", "sample": "s",
+            "seconds": 1.0, "ids": [1, 2]}
+    monkeypatch.setattr(bench, "cpu_reference_sample", lambda wl, full_run=True: dict(fake))
+    for world in (1, 2):
+        monkeypatch.setattr(bench, "dist_env", lambda w=world: (0, w, 0))
+        wl = dict(bench.WORKLOADS["c3"])
+        bench.run_reference(types.SimpleNamespace(warmup=1, steps=1), wl)
+        line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+        assert line["impl"] == "reference"
+        assert line["config"] == bench.workload_config(wl, world)
+    assert bench.workload_config(dict(bench.WORKLOADS["c3"]), 2)["sequences_per_gpu"] == 32
