@@ -182,9 +182,12 @@ struct DeviceModel {
     bool bf16 = false;
     unsigned short* blob16 = nullptr;
     std::unordered_map<const float*, const unsigned short*> w16;
-    std::vector<std::array<CUtensorMap, 8>> tc_maps;  // per layer: {hi, lo} x 4 matrices (W^T, 128-row boxes)
+    // per layer, for each of the 4 matrices: {hi, lo, stored} descriptors of
+    // W^T (128-row boxes); `stored` is W^T as fp32, or as bf16 for bf16
+    // weights (the decode-batch GEMM reads it once and splits it on chip)
+    std::vector<std::array<CUtensorMap, 12>> tc_maps;
     // the tied head: tok_emb [V][D] is already W^T of logits = x * tok_emb^T
-    CUtensorMap tc_head_maps[2];
+    CUtensorMap tc_head_maps[3];
     float* tc_head_blob = nullptr;  // tok_emb hi, lo halves, then V zeros (the head has no bias)
 };
 
@@ -253,8 +256,10 @@ static void configure_kernels(int dev) {
     setmax((const void*)k_head<16, WBF16>, 227 * 1024);
     setmax((const void*)k_sample_step, 227 * 1024);
     setmax((const void*)k_gemm_tc<128>, 227 * 1024);
-    setmax((const void*)k_gemm_tc_swab<64>, 227 * 1024);
-    setmax((const void*)k_gemm_tc_swab<128>, 227 * 1024);
+    setmax((const void*)k_gemm_tc_swab<64, false>, 227 * 1024);
+    setmax((const void*)k_gemm_tc_swab<128, false>, 227 * 1024);
+    setmax((const void*)k_gemm_tc_swab<64, true>, 227 * 1024);
+    setmax((const void*)k_gemm_tc_swab<128, true>, 227 * 1024);
     setmax((const void*)k_sample_rows, 227 * 1024);
     setmax((const void*)k_decode_mega<1, false>, 0);
     setmax((const void*)k_decode_mega<2, false>, 0);
@@ -381,12 +386,29 @@ static void launch_split_tf32(cudaStream_t st, const float* x, size_t n, float* 
     launch_pdl(k_split_tf32, std::max(blocks, 1), 256, 0, st, reinterpret_cast<const float4*>(x), n4,
                                                       reinterpret_cast<float4*>(hi), reinterpret_cast<float4*>(lo));
 }
-static void launch_split_tf32_transpose(cudaStream_t st, const float* W, int K, int N, float* hiT, float* loT) {
-    launch_pdl(k_split_tf32_transpose, dim3(ceil_div(N, 32), ceil_div(K, 32)), dim3(32, 8), 0, st, W, K, N, hiT, loT);
+static void launch_split_tf32_transpose(cudaStream_t st, const float* W, int K, int N, float* hiT, float* loT,
+                                        float* rawT = nullptr) {
+    launch_pdl(k_split_tf32_transpose, dim3(ceil_div(N, 32), ceil_div(K, 32)), dim3(32, 8), 0, st, W, K, N, hiT, loT,
+               rawT);
 }
-// TF32 hi/lo copies of every projection, transposed to W^T [N][K], and their
-// descriptors (boxes of 32 K x 128 N rows).  FORGE_B200_GEMM=simt leaves the
-// tensor-core path off.
+// 2-D bf16 row-major [outer][inner] map, unswizzled boxes of 32 x box_outer
+// elements (64-byte rows).
+static bool tc_encode_bf16(CUtensorMap* map, const unsigned short* base, uint64_t inner, uint64_t outer,
+                           uint32_t box_outer) {
+    auto fn = tc_encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {inner * 2};
+    const cuuint32_t box[2] = {32, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<unsigned short*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// TF32 hi/lo copies of every projection, transposed to W^T [N][K], W^T as
+// stored (fp32, or the bf16 bits of bf16 weights, whose TF32 hi half is the
+// value itself), and their descriptors (boxes of 32 K x 128 N rows).
+// FORGE_B200_GEMM=simt leaves the tensor-core path off.
 static void tc_setup(const fb2_model& m, DeviceModel& dm) {
     dm.tc_ok = false;
     const char* env = getenv("FORGE_B200_GEMM");
@@ -394,22 +416,29 @@ static void tc_setup(const fb2_model& m, DeviceModel& dm) {
     if (!tc_encode_fn() || (m.D % 32) != 0) return;
     const size_t D = m.D, F = m.F;
     const size_t per_layer = 3 * D * D + D * D + D * F + F * D;
-    dm.tc_blob = dalloc<float>(2 * per_layer * m.L);
+    dm.tc_blob = dalloc<float>(3 * per_layer * m.L);
     dm.tc_maps.resize(m.L);
     for (int l = 0; l < m.L; l++) {
         const LayerW& w = dm.layers[l];
         const float* src[4] = {w.qkv_w, w.proj_w, w.fc_w, w.mproj_w};
         const size_t Ks[4] = {D, D, D, F}, Ns[4] = {3 * D, D, F, D};
-        float* at = dm.tc_blob + 2 * per_layer * l;
+        float* at = dm.tc_blob + 3 * per_layer * l;
         for (int j = 0; j < 4; j++) {
             const size_t n = Ks[j] * Ns[j];
             float* hi = at;
             float* lo = at + n;
-            launch_split_tf32_transpose(0, src[j], (int)Ks[j], (int)Ns[j], hi, lo);
-            if (!tc_encode(&dm.tc_maps[l][2 * j], hi, Ks[j], Ns[j], 128) ||
-                !tc_encode(&dm.tc_maps[l][2 * j + 1], lo, Ks[j], Ns[j], 128))
+            float* raw = at + 2 * n;
+            CUtensorMap* mp = &dm.tc_maps[l][3 * j];
+            launch_split_tf32_transpose(0, src[j], (int)Ks[j], (int)Ns[j], hi, lo, dm.bf16 ? nullptr : raw);
+            if (!tc_encode(&mp[0], hi, Ks[j], Ns[j], 128) || !tc_encode(&mp[1], lo, Ks[j], Ns[j], 128)) return;
+            if (dm.bf16) {
+                unsigned short* raw16 = reinterpret_cast<unsigned short*>(raw);
+                k_to_bf16_bits<<<(int)std::min<size_t>(4096, (n + 255) / 256), 256>>>(hi, (long long)n, raw16);
+                if (!tc_encode_bf16(&mp[2], raw16, Ks[j], Ns[j], 128)) return;
+            } else if (!tc_encode(&mp[2], raw, Ks[j], Ns[j], 128)) {
                 return;
-            at += 2 * n;
+            }
+            at += 3 * n;
         }
     }
     {
@@ -420,6 +449,12 @@ static void tc_setup(const fb2_model& m, DeviceModel& dm) {
         if (!tc_encode(&dm.tc_head_maps[0], dm.tc_head_blob, D, m.V, 128) ||
             !tc_encode(&dm.tc_head_maps[1], dm.tc_head_blob + nv, D, m.V, 128))
             return;
+        if (dm.bf16) {
+            auto it = dm.w16.find(dm.tok_emb);
+            if (it == dm.w16.end() || !tc_encode_bf16(&dm.tc_head_maps[2], it->second, D, m.V, 128)) return;
+        } else if (!tc_encode(&dm.tc_head_maps[2], dm.tok_emb, D, m.V, 128)) {
+            return;
+        }
     }
     CK(cudaDeviceSynchronize());
     dm.tc_ok = true;
@@ -799,9 +834,10 @@ constexpr int kTcMinRows = 512;
 // The launch of one tensor-core projection; false when it does not apply.
 // a_split: A's TF32 halves are already in ahi / alo (written by the producer
 // of A); prefill only.
+// bmaps: {hi, lo, stored} descriptors of W^T; w_bf16: `stored` is bf16.
 static bool launch_gemm_tc(cudaStream_t st, int sm_count, int M, int K, int N, const float* A, float* ahi, float* alo,
                            const CUtensorMap* bmaps, Epi e, int* err, float* part, size_t part_cap, int64_t* launches,
-                           bool a_split = false) {
+                           bool w_bf16, bool a_split = false) {
     if (M <= kMaxGemvRows || (K % 4) || (N % 4)) return false;
     TcMaps maps;
     maps.b_hi = bmaps[0];
@@ -818,18 +854,26 @@ static bool launch_gemm_tc(cudaStream_t st, int sm_count, int M, int K, int N, c
         launch_pdl(k_gemm_tc<128>, std::min(tiles, sm_count), TCP_THREADS, TcCfg<128>::SMEM, st, maps, M, N, K, e, err);
         return true;
     }
-    // decode batches: the kernel splits A's tiles itself (maps.a_hi = A)
+    // decode batches: the kernel splits A's tiles and W^T's stored tiles
+    // itself (maps.a_hi = A, maps.b_hi = W^T as stored)
     const int bnb = M <= 64 ? 64 : 128;
     if (!tc_encode(&maps.a_hi, A, K, M, bnb)) fail(FB2_CUDA_ERROR, "cuTensorMapEncodeTiled failed for a GEMM operand");
     maps.a_lo = maps.a_hi;
+    maps.b_hi = bmaps[2];
+    maps.b_lo = bmaps[2];
     const int tiles = ceil_div(N, 128) * ceil_div(M, bnb), nk = ceil_div(K, TC_BK);
     int S = std::max(1, std::min({kTcSplitMax, nk, sm_count / tiles}));
     S = ceil_div(nk, ceil_div(nk, S));  // balanced k blocks per split
     if ((size_t)S * M * N > part_cap) S = 1;
     dim3 grid(ceil_div(N, 128), ceil_div(M, bnb), S);
     (*launches)++;
-    if (bnb == 64) launch_pdl(k_gemm_tc_swab<64>, grid, 128, TcSwabCfg<64>::SMEM, st, maps, M, N, K, e, err, part);
-    else launch_pdl(k_gemm_tc_swab<128>, grid, 128, TcSwabCfg<128>::SMEM, st, maps, M, N, K, e, err, part);
+    if (bnb == 64) {
+        if (w_bf16) launch_pdl(k_gemm_tc_swab<64, true>, grid, TCS_THREADS, TcSwabCfg<64>::SMEM, st, maps, M, N, K, e, err, part);
+        else launch_pdl(k_gemm_tc_swab<64, false>, grid, TCS_THREADS, TcSwabCfg<64>::SMEM, st, maps, M, N, K, e, err, part);
+    } else {
+        if (w_bf16) launch_pdl(k_gemm_tc_swab<128, true>, grid, TCS_THREADS, TcSwabCfg<128>::SMEM, st, maps, M, N, K, e, err, part);
+        else launch_pdl(k_gemm_tc_swab<128, false>, grid, TCS_THREADS, TcSwabCfg<128>::SMEM, st, maps, M, N, K, e, err, part);
+    }
     if (S > 1) {
         const size_t n4 = (size_t)M * N / 4;
         (*launches)++;
@@ -848,7 +892,7 @@ static void launch_linear(DeviceSession& s, int M, int K, int N, const float* A,
     // faster than a bf16 gemv pass per 16 rows
     if (bmaps && s.d_ahi && !(s.dm->bf16 && M <= kMaxGemvRows) &&
         launch_gemm_tc(s.stream, s.dm->sm_count, M, K, N, A, s.d_ahi, s.d_alo, bmaps, e, s.d_tc_err, s.d_tc_part,
-                       s.tc_part_cap, &s.stats.kernel_launches))
+                       s.tc_part_cap, &s.stats.kernel_launches, s.dm->bf16))
         return;
     launch_linear(s, M, K, N, A, W, e);
 }
@@ -858,7 +902,7 @@ static void launch_linear(DeviceSession& s, int M, int K, int N, const float* A,
 static void launch_linear_split(DeviceSession& s, int M, int K, int N, float* ahi, float* alo, const CUtensorMap* bmaps,
                                 Epi e) {
     if (!launch_gemm_tc(s.stream, s.dm->sm_count, M, K, N, nullptr, ahi, alo, bmaps, e, s.d_tc_err, s.d_tc_part,
-                        s.tc_part_cap, &s.stats.kernel_launches, true))
+                        s.tc_part_cap, &s.stats.kernel_launches, s.dm->bf16, true))
         fail(FB2_CUDA_ERROR, "tensor-core GEMM refused a pre-split operand");
 }
 
@@ -987,11 +1031,12 @@ static void launch_head(DeviceSession& s, int M, const float* xln, const int* ou
                         float* logits_base) {
     (void)out_slot_host_unused;
     const fb2_model& m = *s.model;
-    // batches of rows: one pass over tok_emb on the tensor cores
-    if (M > kMaxGemvRows && s.dm->tc_ok && !s.dm->bf16 && s.d_ahi) {
+    // batches of rows: one pass over tok_emb on the tensor cores (bf16
+    // weights: the decode-batch GEMM reads the bf16 rows once)
+    if (M > kMaxGemvRows && s.dm->tc_ok && s.d_ahi && !(s.dm->bf16 && M >= kTcMinRows)) {
         Epi e = make_epi(EPI_BIAS, s.dm->tc_head_blob + 2 * (size_t)m.V * m.D, nullptr, logits_base);
         if (launch_gemm_tc(s.stream, s.dm->sm_count, M, m.D, m.V, xln, s.d_ahi, s.d_alo, s.dm->tc_head_maps, e,
-                           s.d_tc_err, s.d_tc_part, s.tc_part_cap, &s.stats.kernel_launches))
+                           s.d_tc_err, s.d_tc_part, s.tc_part_cap, &s.stats.kernel_launches, s.dm->bf16))
             return;
     }
     int blocks = std::min(ceil_div(m.V, 8), 8 * s.dm->sm_count);
@@ -1038,22 +1083,22 @@ static void run_layers(DeviceSession& s, int M, Rows R, bool decode, QBlocks qb)
             launch_layernorm(s, M, s.d_x, w.ln1_w, w.ln1_b, s.d_ahi, nullptr, s.d_alo);
             launch_linear_split(s, M, m.D, 3 * m.D, s.d_ahi, s.d_alo, tcm, eq);
             const Epi ep = make_epi(EPI_RESID, w.proj_b, s.d_x, s.d_x2);
-            if (launch_attn_prefill(s, qb, l, s.d_ahi, s.d_alo)) launch_linear_split(s, M, m.D, m.D, s.d_ahi, s.d_alo, tcm + 2, ep);
-            else launch_linear(s, M, m.D, m.D, s.d_att, w.proj_w, ep, tcm + 2);
+            if (launch_attn_prefill(s, qb, l, s.d_ahi, s.d_alo)) launch_linear_split(s, M, m.D, m.D, s.d_ahi, s.d_alo, tcm + 3, ep);
+            else launch_linear(s, M, m.D, m.D, s.d_att, w.proj_w, ep, tcm + 3);
             launch_layernorm(s, M, s.d_x2, w.ln2_w, w.ln2_b, s.d_ahi, nullptr, s.d_alo);
             Epi ef = make_epi(EPI_GELU_SPLIT, w.fc_b, nullptr, s.d_ahi2);
             ef.out_lo = s.d_alo2;
-            launch_linear_split(s, M, m.D, m.F, s.d_ahi, s.d_alo, tcm + 4, ef);
-            launch_linear_split(s, M, m.F, m.D, s.d_ahi2, s.d_alo2, tcm + 6, make_epi(EPI_RESID, w.mproj_b, s.d_x2, s.d_x));
+            launch_linear_split(s, M, m.D, m.F, s.d_ahi, s.d_alo, tcm + 6, ef);
+            launch_linear_split(s, M, m.F, m.D, s.d_ahi2, s.d_alo2, tcm + 9, make_epi(EPI_RESID, w.mproj_b, s.d_x2, s.d_x));
             continue;
         }
         launch_linear(s, M, m.D, 3 * m.D, s.d_ln, w.qkv_w, eq, tcm);
         if (decode) launch_attn_decode(s, M, l, R);
         else launch_attn_prefill(s, qb, l);
-        launch_linear(s, M, m.D, m.D, s.d_att, w.proj_w, make_epi(EPI_RESID, w.proj_b, s.d_x, s.d_x2), tcm ? tcm + 2 : nullptr);
+        launch_linear(s, M, m.D, m.D, s.d_att, w.proj_w, make_epi(EPI_RESID, w.proj_b, s.d_x, s.d_x2), tcm ? tcm + 3 : nullptr);
         launch_layernorm(s, M, s.d_x2, w.ln2_w, w.ln2_b, s.d_ln, nullptr);
-        launch_linear(s, M, m.D, m.F, s.d_ln, w.fc_w, make_epi(EPI_GELU, w.fc_b, nullptr, s.d_h), tcm ? tcm + 4 : nullptr);
-        launch_linear(s, M, m.F, m.D, s.d_h, w.mproj_w, make_epi(EPI_RESID, w.mproj_b, s.d_x2, s.d_x), tcm ? tcm + 6 : nullptr);
+        launch_linear(s, M, m.D, m.F, s.d_ln, w.fc_w, make_epi(EPI_GELU, w.fc_b, nullptr, s.d_h), tcm ? tcm + 6 : nullptr);
+        launch_linear(s, M, m.F, m.D, s.d_h, w.mproj_w, make_epi(EPI_RESID, w.mproj_b, s.d_x2, s.d_x), tcm ? tcm + 9 : nullptr);
     }
 }
 
@@ -2708,8 +2753,9 @@ int32_t fb2_test_gemm_tc(int32_t M, int32_t N, int32_t K, const float* A, const 
         CK(cudaGetDevice(&dev));
         configure_kernels(dev);
         const size_t na = (size_t)M * K, nw = (size_t)K * N, no = (size_t)M * N;
-        float* buf = dalloc<float>(3 * na + 3 * nw + no + (size_t)N);
-        float *a = buf, *ahi = a + na, *alo = ahi + na, *w = alo + na, *whi = w + nw, *wlo = whi + nw, *o = wlo + nw;
+        float* buf = dalloc<float>(3 * na + 4 * nw + no + (size_t)N);
+        float *a = buf, *ahi = a + na, *alo = ahi + na, *w = alo + na, *whi = w + nw, *wlo = whi + nw, *wt = wlo + nw,
+              *o = wt + nw;
         float* bias = o + no;
         int* err = dalloc<int>(1);
         float* part = nullptr;
@@ -2718,15 +2764,16 @@ int32_t fb2_test_gemm_tc(int32_t M, int32_t N, int32_t K, const float* A, const 
             CK(cudaMemcpy(w, W, nw * 4, cudaMemcpyHostToDevice));
             CK(cudaMemset(bias, 0, (size_t)N * 4));
             CK(cudaMemset(err, 0, sizeof(int)));
-            launch_split_tf32_transpose(0, w, K, N, whi, wlo);
-            CUtensorMap bm[2];
-            if (!tc_encode(&bm[0], whi, K, N, 128) || !tc_encode(&bm[1], wlo, K, N, 128))
+            launch_split_tf32_transpose(0, w, K, N, whi, wlo, wt);
+            CUtensorMap bm[3];
+            if (!tc_encode(&bm[0], whi, K, N, 128) || !tc_encode(&bm[1], wlo, K, N, 128) ||
+                !tc_encode(&bm[2], wt, K, N, 128))
                 fail(FB2_CUDA_ERROR, "cuTensorMapEncodeTiled failed");
             const size_t cap = (size_t)kTcSplitMax * M * N;
             part = dalloc<float>(cap);
             int64_t launches = 0;
             Epi e = make_epi(EPI_BIAS, bias, nullptr, o);
-            if (!launch_gemm_tc(0, 148, M, K, N, a, ahi, alo, bm, e, err, part, cap, &launches))
+            if (!launch_gemm_tc(0, 148, M, K, N, a, ahi, alo, bm, e, err, part, cap, &launches, false))
                 fail(FB2_UNSUPPORTED, "the tensor-core GEMM takes more than 16 rows");
             CK(cudaGetLastError());
             CK(cudaDeviceSynchronize());

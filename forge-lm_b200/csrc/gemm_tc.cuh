@@ -144,9 +144,10 @@ FB2_DEV void tmem_ld16(uint32_t taddr, float* v) {
 
 }  // namespace tc
 
-// W [K][N] -> W^T halves hiT, loT [N][K] (32 x 32 tiles through shared memory).
+// W [K][N] -> W^T halves hiT, loT [N][K] (32 x 32 tiles through shared
+// memory), and W^T itself into rawT when it is not null.
 __global__ void k_split_tf32_transpose(const float* __restrict__ W, int K, int N, float* __restrict__ hiT,
-                                       float* __restrict__ loT) {
+                                       float* __restrict__ loT, float* __restrict__ rawT) {
     pdl_wait();
     __shared__ float t[32][33];
     const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
@@ -159,9 +160,11 @@ __global__ void k_split_tf32_transpose(const float* __restrict__ W, int K, int N
         const int n = n0 + r, k = k0 + threadIdx.x;
         if (n < N && k < K) {
             float h, l;
-            tf32_split(t[threadIdx.x][r], h, l);
+            const float v = t[threadIdx.x][r];
+            tf32_split(v, h, l);
             hiT[(size_t)n * K + k] = h;
             loT[(size_t)n * K + k] = l;
+            if (rawT) rawT[(size_t)n * K + k] = v;
         }
     }
 }
@@ -342,10 +345,22 @@ __global__ void __launch_bounds__(TCP_THREADS, 1) k_gemm_tc(const __grid_constan
 // column n, TMEM column = batch row m.  gridDim = (ceil(N/128),
 // ceil(M/BNB), S): with S > 1 each CTA writes partial[z][M][N] and
 // k_splitk_reduce sums the splits in order and applies the epilogue.
-// The batch rows arrive as plain fp32 (maps.a_hi describes A itself): per
-// stage, warps 2-3 split the landed tile in place into its TF32 halves
-// (the swizzled positions are the same for A, hi and lo) and release it to
-// the MMA warp through split[stage], so no separate split kernel runs.
+//
+// Both operands arrive as they are stored, so each weight element crosses
+// HBM once: maps.b_hi describes W^T itself (fp32, or bf16 when WB16) and
+// maps.a_hi the fp32 batch rows.  Per stage, warps 2-7 turn the landed tiles
+// into TF32 halves in shared memory and release the stage to the MMA warp
+// through split[stage]:
+//   fp32 W^T and A: in place (x_hi) plus x_lo at the same swizzled offset
+//                   (the 128-byte swizzle places hi, lo and the source alike);
+//   bf16 W^T:       the 64-byte rows land unswizzled in the w_lo slot and are
+//                   widened into the swizzled w_hi tile; a bf16 value is exact
+//                   in TF32, so w_lo is zero and its MMA is skipped.
+// The halves equal the ones k_split_tf32_transpose makes for the prefill GEMM
+// (both round to nearest, ties to even).
+constexpr int TCS_THREADS = 256;
+constexpr int TCS_SPLIT_WARPS = 6;  // warps 2..7
+
 template <int BNB>
 struct TcSwabCfg {
     static constexpr int TILE_B = BNB * TC_BK * 4;
@@ -354,11 +369,12 @@ struct TcSwabCfg {
     static constexpr int SMEM = STAGES * STAGE + 1024;
 };
 
-template <int BNB>
-__global__ void __launch_bounds__(128, 1) k_gemm_tc_swab(const __grid_constant__ TcMaps maps, int M, int N, int K,
-                                                         Epi e, int* err, float* __restrict__ partial) {
+template <int BNB, bool WB16>
+__global__ void __launch_bounds__(TCS_THREADS, 1) k_gemm_tc_swab(const __grid_constant__ TcMaps maps, int M, int N,
+                                                                 int K, Epi e, int* err, float* __restrict__ partial) {
     using Cfg = TcSwabCfg<BNB>;
     constexpr int STAGES = Cfg::STAGES, STAGE = Cfg::STAGE, TILE_B = Cfg::TILE_B;
+    constexpr int W_BYTES = WB16 ? TC_TILE_A / 2 : TC_TILE_A;  // one weight tile as stored
     extern __shared__ unsigned char tc_smem_raw[];
     __shared__ __align__(8) uint64_t full[STAGES], split[STAGES], empty[STAGES], accb;
     __shared__ uint32_t tmem_base;
@@ -375,7 +391,7 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc_swab(const __grid_constant__
         s_abort = 0;
         for (int i = 0; i < STAGES; i++) {
             tc::bar_init(&full[i], 1);
-            tc::bar_init(&split[i], 2);  // one arrival per splitting warp
+            tc::bar_init(&split[i], TCS_SPLIT_WARPS);  // one arrival per splitting warp
             tc::bar_init(&empty[i], 1);
         }
         tc::bar_init(&accb, 1);
@@ -398,24 +414,24 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc_swab(const __grid_constant__
             const int st = i % STAGES;
             if (i >= STAGES && !tc::bar_wait(&empty[st], ((i / STAGES) - 1) & 1, &s_abort)) break;
             unsigned char* sb = sm + (size_t)st * STAGE;
-            tc::bar_expect_tx(&full[st], 2 * TC_TILE_A + TILE_B);
+            tc::bar_expect_tx(&full[st], W_BYTES + TILE_B);
             const int k0 = (kb0 + i) * TC_BK;
-            // maps.b_* = weights W^T (128-row boxes), maps.a_hi = batch rows A (BNB-row boxes, fp32)
-            tc::tma_load_2d(sb, &maps.b_hi, k0, n0, &full[st]);
-            tc::tma_load_2d(sb + TC_TILE_A, &maps.b_lo, k0, n0, &full[st]);
+            // weights W^T (128-row boxes): fp32 into w_hi, bf16 into the w_lo slot
+            tc::tma_load_2d(sb + (WB16 ? TC_TILE_A : 0), &maps.b_hi, k0, n0, &full[st]);
             tc::tma_load_2d(sb + 2 * TC_TILE_A, &maps.a_hi, k0, m0, &full[st]);
         }
     } else if (warp >= 2) {
-        // A tile -> TF32 halves in place (x_hi) and into x_lo
         const int t = tid - 64;
+        constexpr int NT = TCS_SPLIT_WARPS * 32;
         for (int i = 0; i < nk; i++) {
             const int st = i % STAGES;
             const bool ok = tc::bar_wait(&full[st], (i / STAGES) & 1, &s_abort);
             if (!__all_sync(0xffffffffu, ok)) break;
-            float4* xh = reinterpret_cast<float4*>(sm + (size_t)st * STAGE + 2 * TC_TILE_A);
-            float4* xl = reinterpret_cast<float4*>(sm + (size_t)st * STAGE + 2 * TC_TILE_A + TILE_B);
-#pragma unroll 4
-            for (int j = t; j < TILE_B / 16; j += 64) {
+            unsigned char* sb = sm + (size_t)st * STAGE;
+            float4* xh = reinterpret_cast<float4*>(sb + 2 * TC_TILE_A);
+            float4* xl = reinterpret_cast<float4*>(sb + 2 * TC_TILE_A + TILE_B);
+#pragma unroll 2
+            for (int j = t; j < TILE_B / 16; j += NT) {
                 const float4 v = xh[j];
                 float4 h, l;
                 tf32_split_rn(v.x, h.x, l.x);
@@ -424,6 +440,42 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc_swab(const __grid_constant__
                 tf32_split_rn(v.w, h.w, l.w);
                 xh[j] = h;
                 xl[j] = l;
+            }
+            if constexpr (WB16) {
+                // 128 rows x 32 bf16 (64 bytes) -> the swizzled fp32 tile:
+                // element k of row r sits in 16-byte chunk (k / 4) ^ (r % 8)
+                const uint4* src = reinterpret_cast<const uint4*>(sb + TC_TILE_A);
+#pragma unroll 2
+                for (int j = t; j < TC_TILE_A / 2 / 16; j += NT) {
+                    const uint4 u = src[j];
+                    const int r = j >> 2, c = (j & 3) * 2;
+                    float4 a, b;
+                    a.x = __uint_as_float(u.x << 16);
+                    a.y = __uint_as_float(u.x & 0xFFFF0000u);
+                    a.z = __uint_as_float(u.y << 16);
+                    a.w = __uint_as_float(u.y & 0xFFFF0000u);
+                    b.x = __uint_as_float(u.z << 16);
+                    b.y = __uint_as_float(u.z & 0xFFFF0000u);
+                    b.z = __uint_as_float(u.w << 16);
+                    b.w = __uint_as_float(u.w & 0xFFFF0000u);
+                    unsigned char* row = sb + r * 128;
+                    *reinterpret_cast<float4*>(row + ((c ^ (r & 7)) << 4)) = a;
+                    *reinterpret_cast<float4*>(row + (((c + 1) ^ (r & 7)) << 4)) = b;
+                }
+            } else {
+                float4* wh = reinterpret_cast<float4*>(sb);
+                float4* wl = reinterpret_cast<float4*>(sb + TC_TILE_A);
+#pragma unroll 2
+                for (int j = t; j < TC_TILE_A / 16; j += NT) {
+                    const float4 v = wh[j];
+                    float4 h, l;
+                    tf32_split_rn(v.x, h.x, l.x);
+                    tf32_split_rn(v.y, h.y, l.y);
+                    tf32_split_rn(v.z, h.z, l.z);
+                    tf32_split_rn(v.w, h.w, l.w);
+                    wh[j] = h;
+                    wl[j] = l;
+                }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
@@ -440,12 +492,11 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc_swab(const __grid_constant__
 #pragma unroll
             for (int ks = 0; ks < TC_BK / 8; ks++) {
                 const uint64_t dwh = tc::sw128_desc(w_hi + ks * 32, 16, 1024);
-                const uint64_t dwl = tc::sw128_desc(w_lo + ks * 32, 16, 1024);
                 const uint64_t dxh = tc::sw128_desc(x_hi + ks * 32, 16, 1024);
                 const uint64_t dxl = tc::sw128_desc(x_lo + ks * 32, 16, 1024);
                 tc::mma_tf32(tmem, dwh, dxh, idesc, (i | ks) != 0);
                 tc::mma_tf32(tmem, dwh, dxl, idesc, 1u);
-                tc::mma_tf32(tmem, dwl, dxh, idesc, 1u);
+                if constexpr (!WB16) tc::mma_tf32(tmem, tc::sw128_desc(w_lo + ks * 32, 16, 1024), dxh, idesc, 1u);
             }
             tc::mma_commit(&empty[st]);
         }
@@ -462,8 +513,9 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc_swab(const __grid_constant__
     }
     __syncwarp();
     tc::fence_after();
-    const int n = n0 + warp * 32 + lane;  // this thread's output column (TMEM lane)
-    if (ok && !s_abort && nk > 0) {
+    // epilogue: warps 0-3, TMEM lane quarter = warp (TMEM lane = output column)
+    const int n = n0 + warp * 32 + lane;  // this thread's output column
+    if (warp < 4 && ok && !s_abort && nk > 0) {
 #pragma unroll 1
         for (int c0 = 0; c0 < BNB; c0 += 16) {
             float v[16];
