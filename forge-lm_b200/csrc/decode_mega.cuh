@@ -2275,6 +2275,24 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkArgs a) {
                     const float4* er = reinterpret_cast<const float4*>(E + (size_t)r * D);
                     const int n4 = D / 4;
                     int i = lane;
+                    // six float4 of the row per lane issued before their FMAs
+                    for (; i + 160 < n4; i += 192) {
+                        float4 e[6];
+#pragma unroll
+                        for (int u = 0; u < 6; u++) e[u] = er[i + 32 * u];
+#pragma unroll
+                        for (int m = 0; m < MR; m++) {
+                            float4 x[6];
+#pragma unroll
+                            for (int u = 0; u < 6; u++) x[u] = *reinterpret_cast<const float4*>(act + m * D + (i + 32 * u) * 4);
+#pragma unroll
+                            for (int u = 0; u < 6; u += 2) {
+                                acc0[m] += x[u].x * e[u].x + x[u].y * e[u].y + x[u].z * e[u].z + x[u].w * e[u].w;
+                                acc1[m] += x[u + 1].x * e[u + 1].x + x[u + 1].y * e[u + 1].y + x[u + 1].z * e[u + 1].z +
+                                           x[u + 1].w * e[u + 1].w;
+                            }
+                        }
+                    }
                     for (; i + 32 < n4; i += 64) {
                         const float4 e0 = er[i], e1 = er[i + 32];
 #pragma unroll
