@@ -1067,7 +1067,6 @@ static void run_layers(DeviceSession& s, int M, Rows R, bool decode, QBlocks qb)
     const fb2_model& m = *s.model;
     for (int l = 0; l < m.L; l++) {
         const LayerW& w = s.dm->layers[l];
-        launch_layernorm(s, M, s.d_x, w.ln1_w, w.ln1_b, s.d_ln, nullptr);
         Epi eq = make_epi(EPI_QKV, w.qkv_b, nullptr, s.d_q);
         eq.kv_layer = s.d_kv + (size_t)l * s.kv_layer_stride;
         eq.kv_slot_stride = s.kv_slot_stride;
@@ -1092,6 +1091,7 @@ static void run_layers(DeviceSession& s, int M, Rows R, bool decode, QBlocks qb)
             launch_linear_split(s, M, m.F, m.D, s.d_ahi2, s.d_alo2, tcm + 9, make_epi(EPI_RESID, w.mproj_b, s.d_x2, s.d_x));
             continue;
         }
+        launch_layernorm(s, M, s.d_x, w.ln1_w, w.ln1_b, s.d_ln, nullptr);
         launch_linear(s, M, m.D, 3 * m.D, s.d_ln, w.qkv_w, eq, tcm);
         if (decode) launch_attn_decode(s, M, l, R);
         else launch_attn_prefill(s, qb, l);
