@@ -1368,6 +1368,17 @@ static void plan_prefill(const DeviceSession& s, const std::vector<int>& order, 
             slot.push_back(sl);
             r += w - a;
         }
+        // tensor-core attention blocks, most keys first (the grid walks them in
+        // order, so the short causal blocks fill the tail of the launch)
+        {
+            std::vector<std::array<int, 4>> b2(q2.size() / 4);
+            for (size_t t = 0; t < b2.size(); t++) b2[t] = {q2[4 * t], q2[4 * t + 1], q2[4 * t + 2], q2[4 * t + 3]};
+            std::stable_sort(b2.begin(), b2.end(), [](const std::array<int, 4>& x, const std::array<int, 4>& y) {
+                return x[3] + x[1] > y[3] + y[1];
+            });
+            for (size_t t = 0; t < b2.size(); t++)
+                for (int u = 0; u < 4; u++) q2[4 * t + u] = b2[t][u];
+        }
         tab.insert(tab.end(), seq.begin(), seq.end());
         tab.insert(tab.end(), pos.begin(), pos.end());
         while (tab.size() % 4) tab.push_back(0);  // int4 alignment
