@@ -93,6 +93,9 @@ def parse():
     ap.add_argument("--skip-e2e", action="store_true", help="omit the host-buffer e2e leg (profiling runs)")
     ap.add_argument("--record-traffic", metavar="NCU_CSV", default=None,
                     help="write the DRAM traffic record of --workload from an ncu --csv capture and exit")
+    ap.add_argument("--kernel-times", action="store_true",
+                    help="after the warm-up, run one step under the CUDA activity profiler (CUPTI, through "
+                         "torch.profiler) and print every kernel's warm device time instead of the bench line")
     ap.add_argument("--record-kernel", default="k_decode_mega")
     ap.add_argument("--record-steps-per-launch", type=int, default=511)
     return ap.parse_args()
@@ -375,6 +378,36 @@ def record_traffic(csv_path: str, workload: str, kernel: str, steps_per_launch: 
     print(json.dumps(rec[workload]))
 
 
+def kernel_times(step, torch) -> None:
+    """One step under the CUDA activity profiler: launches, total and mean
+    device time per kernel (warm, in the step's own order and overlap, so
+    the figures add up to the step; ncu's replayed times are cold and
+    serialised), and the span from the first kernel's start to the last's end."""
+    import collections
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize()
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    t0, t1 = None, None
+    for ev in prof.events():
+        if ev.device_type.name != "CUDA":
+            continue
+        agg[ev.name][0] += 1
+        agg[ev.name][1] += ev.device_time_total
+        t0 = ev.time_range.start if t0 is None else min(t0, ev.time_range.start)
+        t1 = ev.time_range.end if t1 is None else max(t1, ev.time_range.end)
+    total = sum(v[1] for v in agg.values())
+    print(f"{sum(v[0] for v in agg.values())} kernels, {total / 1000:.2f} ms device time, "
+          f"span {(t1 - t0) / 1000 if t0 is not None else 0:.2f} ms")
+    print("| kernel | launches | total ms | share | mean us |")
+    print("|---|---:|---:|---:|---:|")
+    for name, (n, t) in sorted(agg.items(), key=lambda kv: -kv[1][1]):
+        print(f"| {name.split('(')[0].replace('void ', '')} | {n} | {t / 1000:.3f} | {100 * t / total:.1f} % | "
+              f"{t / n:.2f} |")
+
+
 def main():
     args = parse()
     if args.record_traffic:
@@ -447,6 +480,11 @@ def main():
     for _ in range(args.warmup):
         step_device()
     barrier()
+    if args.kernel_times:
+        if world > 1:
+            raise SystemExit("--kernel-times runs on one GPU")
+        kernel_times(step_device, torch)
+        return
     be.reset_stats()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
