@@ -556,12 +556,21 @@ __global__ void k_splitk_reduce(const float* __restrict__ partial, int S, int M,
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const int m = (int)(i / n4), n = (int)(i - (size_t)m * n4) * 4;
         float4 acc = __ldcg(reinterpret_cast<const float4*>(partial + (size_t)m * N + n));
-        for (int z = 1; z < S; z++) {
-            const float4 p = __ldcg(reinterpret_cast<const float4*>(partial + ((size_t)z * M + m) * N + n));
-            acc.x += p.x;
-            acc.y += p.y;
-            acc.z += p.z;
-            acc.w += p.w;
+        // eight splits' loads in flight before their adds (one L2 round trip
+        // per eight); the adds keep the order z = 1, 2, ...
+        for (int z0 = 1; z0 < S; z0 += 8) {
+            float4 p[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (z0 + j < S) p[j] = __ldcg(reinterpret_cast<const float4*>(partial + ((size_t)(z0 + j) * M + m) * N + n));
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (z0 + j < S) {
+                    acc.x += p[j].x;
+                    acc.y += p[j].y;
+                    acc.z += p[j].z;
+                    acc.w += p[j].w;
+                }
         }
         epi_store4(e, m, n, N, acc);
     }

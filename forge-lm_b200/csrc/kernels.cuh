@@ -495,14 +495,43 @@ __global__ void k_attn_decode_combine(const float* __restrict__ part, int H, int
     const int T = R.pos[r] + 1;
     const int ns = (T + kAttnChunk - 1) / kAttnChunk;
     const float* p = part + ((size_t)r * H + h) * nsplit * (HD + 2);
+    // loads eight chunks at a time ahead of their use; sums in chunk order
     float M = -INFINITY;
-    for (int s = 0; s < ns; s++) M = fmaxf(M, p[s * (HD + 2)]);
+    for (int s0 = 0; s0 < ns; s0 += 8) {
+        float mv[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) mv[j] = s0 + j < ns ? p[(s0 + j) * (HD + 2)] : -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 8; j++) M = fmaxf(M, mv[j]);
+    }
     float L = 0.f;
-    for (int s = 0; s < ns; s++) L += p[s * (HD + 2) + 1] * __expf(p[s * (HD + 2)] - M);
+    for (int s0 = 0; s0 < ns; s0 += 8) {
+        float mv[8], lv[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (s0 + j < ns) {
+                mv[j] = p[(s0 + j) * (HD + 2)];
+                lv[j] = p[(s0 + j) * (HD + 2) + 1];
+            }
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (s0 + j < ns) L += lv[j] * __expf(mv[j] - M);
+    }
     float inv = 1.0f / L;
     for (int d = threadIdx.x; d < HD; d += blockDim.x) {
         float a = 0.f;
-        for (int s = 0; s < ns; s++) a += p[s * (HD + 2) + 2 + d] * __expf(p[s * (HD + 2)] - M);
+        for (int s0 = 0; s0 < ns; s0 += 8) {
+            float mv[8], xv[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (s0 + j < ns) {
+                    mv[j] = p[(s0 + j) * (HD + 2)];
+                    xv[j] = p[(s0 + j) * (HD + 2) + 2 + d];
+                }
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (s0 + j < ns) a += xv[j] * __expf(mv[j] - M);
+        }
         o[d] = a * inv;
     }
 }
