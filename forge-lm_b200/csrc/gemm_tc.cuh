@@ -555,6 +555,8 @@ __global__ void k_splitk_reduce(const float* __restrict__ partial, int S, int M,
     const size_t total = (size_t)M * n4;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         const int m = (int)(i / n4), n = (int)(i - (size_t)m * n4) * 4;
+        float4 bb, rr;
+        epi_operands4(e, m, n, N, bb, rr);  // in flight with the partials
         float4 acc = __ldcg(reinterpret_cast<const float4*>(partial + (size_t)m * N + n));
         // eight splits' loads in flight before their adds (one L2 round trip
         // per eight); the adds keep the order z = 1, 2, ...
@@ -572,7 +574,7 @@ __global__ void k_splitk_reduce(const float* __restrict__ partial, int S, int M,
                     acc.w += p[j].w;
                 }
         }
-        epi_store4(e, m, n, N, acc);
+        epi_store4_with(e, m, n, N, acc, bb, rr);
     }
 }
 

@@ -70,9 +70,22 @@ template <int PER_LANE>
 __global__ void k_layernorm(int rows, int D, const float* __restrict__ x, const float* __restrict__ w,
                             const float* __restrict__ b, float* __restrict__ y, const int* __restrict__ row_map,
                             float* __restrict__ y_lo) {
-    pdl_wait();
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
+    // gain and bias (weights, written only when the model is created) are
+    // loaded before the grid-dependency wait, so their round trip overlaps
+    // the predecessor's tail instead of following the statistics
+    constexpr bool kPre = PER_LANE <= 32;
+    float wv[kPre ? PER_LANE : 1], bv[kPre ? PER_LANE : 1];
+    if constexpr (kPre) {
+#pragma unroll
+        for (int i = 0; i < PER_LANE; i++) {
+            const int c = lane + i * 32;
+            wv[i] = c < D ? w[c] : 0.f;
+            bv[i] = c < D ? b[c] : 0.f;
+        }
+    }
+    pdl_wait();
     if (warp >= rows) return;
     int src = row_map ? row_map[warp] : warp;
     const float* xr = x + (size_t)src * D;
@@ -101,14 +114,20 @@ __global__ void k_layernorm(int rows, int D, const float* __restrict__ x, const 
 #pragma unroll
         for (int i = 0; i < PER_LANE; i++) {
             int c = lane + i * 32;
-            if (c < D) tf32_split((v[i] - mu) * rs * w[c] + b[c], yr[c], yl[c]);
+            if (c < D) {
+                const float g = kPre ? wv[kPre ? i : 0] : w[c], be = kPre ? bv[kPre ? i : 0] : b[c];
+                tf32_split((v[i] - mu) * rs * g + be, yr[c], yl[c]);
+            }
         }
         return;
     }
 #pragma unroll
     for (int i = 0; i < PER_LANE; i++) {
         int c = lane + i * 32;
-        if (c < D) yr[c] = (v[i] - mu) * rs * w[c] + b[c];
+        if (c < D) {
+            const float g = kPre ? wv[kPre ? i : 0] : w[c], be = kPre ? bv[kPre ? i : 0] : b[c];
+            yr[c] = (v[i] - mu) * rs * g + be;
+        }
     }
 }
 
@@ -165,11 +184,17 @@ FB2_DEV void epi_store1(const Epi& e, int m, int n, int N, float a) {
     e.out[(size_t)m * N + n] = a;
 }
 
-FB2_DEV void epi_store4(const Epi& e, int m, int n, int N, float4 a) {
-    float4 bb = *reinterpret_cast<const float4*>(e.bias + n);
+// The epilogue's operands of output quad (m, n..n+3): the bias, and the
+// residual for EPI_RESID (zeros otherwise).
+FB2_DEV void epi_operands4(const Epi& e, int m, int n, int N, float4& bb, float4& rr) {
+    bb = *reinterpret_cast<const float4*>(e.bias + n);
+    rr = e.kind == EPI_RESID ? *reinterpret_cast<const float4*>(e.resid + (size_t)m * N + n)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+// epi_store4 with its operands already loaded (epi_operands4).
+FB2_DEV void epi_store4_with(const Epi& e, int m, int n, int N, float4 a, float4 bb, float4 r) {
     a.x += bb.x; a.y += bb.y; a.z += bb.z; a.w += bb.w;
     if (e.kind == EPI_RESID) {
-        float4 r = *reinterpret_cast<const float4*>(e.resid + (size_t)m * N + n);
         a.x += r.x; a.y += r.y; a.z += r.z; a.w += r.w;
     } else if (e.kind == EPI_GELU) {
         a.x = gelu_tanh(a.x); a.y = gelu_tanh(a.y); a.z = gelu_tanh(a.z); a.w = gelu_tanh(a.w);
@@ -201,6 +226,12 @@ FB2_DEV void epi_store4(const Epi& e, int m, int n, int N, float4 a) {
         return;
     }
     *reinterpret_cast<float4*>(e.out + (size_t)m * N + n) = a;
+}
+
+FB2_DEV void epi_store4(const Epi& e, int m, int n, int N, float4 a) {
+    float4 bb, rr;
+    epi_operands4(e, m, n, N, bb, rr);
+    epi_store4_with(e, m, n, N, a, bb, rr);
 }
 
 // ---------------------------------------------------------------------------
