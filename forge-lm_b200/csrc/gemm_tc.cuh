@@ -513,21 +513,36 @@ __global__ void __launch_bounds__(TCS_THREADS, 1) k_gemm_tc_swab(const __grid_co
     }
     __syncwarp();
     tc::fence_after();
-    // epilogue: warps 0-3, TMEM lane quarter = warp (TMEM lane = output column)
-    const int n = n0 + warp * 32 + lane;  // this thread's output column
-    if (warp < 4 && ok && !s_abort && nk > 0) {
+    // epilogue, warps 0-3 (TMEM lane quarter = warp; TMEM lane = output
+    // column, TMEM column = batch row): the accumulator goes through shared
+    // memory (the ring is free: every MMA, and so every read of the ring, has
+    // completed) as a [BNB rows][128 columns] tile, then each warp writes
+    // whole rows, one float4 per lane (512 contiguous bytes a store), through
+    // the quad epilogue or into the split's partial rows.  Per-column stores
+    // straight from the TMEM registers (128 bytes a store, a row apart)
+    // measured 1.3-1.5 us slower a launch.
+    const bool epi = ok && !s_abort && nk > 0;
+    float* stg = reinterpret_cast<float*>(sm);
+    if (warp < 4 && epi) {
 #pragma unroll 1
         for (int c0 = 0; c0 < BNB; c0 += 16) {
             float v[16];
             tc::tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
-            if (n < N) {
 #pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    const int m = m0 + c0 + i;
-                    if (m >= M) break;
-                    if (S == 1) epi_store1(e, m, n, N, v[i]);
-                    else partial[((size_t)z * M + m) * N + n] = v[i];
-                }
+            for (int i = 0; i < 16; i++) stg[(c0 + i) * 128 + warp * 32 + lane] = v[i];
+        }
+    }
+    if (warp < 4) asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (warp < 4 && epi) {
+        const int nq = n0 + 4 * lane;
+#pragma unroll 1
+        for (int ml = warp; ml < BNB; ml += 4) {
+            const int m = m0 + ml;
+            if (m >= M) break;
+            if (nq < N) {
+                const float4 v = *reinterpret_cast<const float4*>(stg + ml * 128 + 4 * lane);
+                if (S == 1) epi_store4(e, m, nq, N, v);
+                else *reinterpret_cast<float4*>(partial + ((size_t)z * M + m) * N + nq) = v;
             }
         }
     }
